@@ -1,0 +1,220 @@
+"""edgexpu-llm_b200: B200 (sm_100a) implementation of EdgeXPU-LLM's quantized matrix-product path.
+
+The product is two shared libraries built by ``make -C edgexpu-llm_b200``:
+
+* ``lib/libedgexpu_cuda.so`` -- hand-written CUDA kernels behind the C ABI of
+  ``include/edgexpu_cuda.h`` (``edgexpu_cuda_*``);
+* ``lib/libedgexpu_b200_host.so`` -- the C host shim of ``include/edgexpu_b200_host.h``: the
+  reference's own entry points (``edgexpu_cpu_linear_quant_batch``, ``edgexpu_gguf_quantize_q8_0``
+  ...) with bodies that forward to the C ABI.
+
+This module is a thin ctypes binding over both, used by the tests, ``bench.py`` and
+``__graft_entry__``.  It never computes anything itself and has no CPU fallback: if a library
+is missing, :func:`load_cuda` / :func:`load_host` raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import pathlib
+
+PKG_DIR = pathlib.Path(__file__).resolve().parent
+LIB_DIR = PKG_DIR / "lib"
+CUDA_LIB = LIB_DIR / "libedgexpu_cuda.so"
+HOST_LIB = LIB_DIR / "libedgexpu_b200_host.so"
+
+TYPE_Q8_0 = 8
+TYPE_Q4_K = 12
+QK8_0, QK_K = 32, 256
+Q8_0_BYTES, Q8_K_BYTES, Q4_K_BYTES = 34, 292, 144
+
+_c_u8p = ctypes.POINTER(ctypes.c_uint8)
+_c_f32p = ctypes.POINTER(ctypes.c_float)
+_c_vp = ctypes.c_void_p
+_c_sz = ctypes.c_size_t
+_c_int = ctypes.c_int
+_c_u32 = ctypes.c_uint32
+_c_str = ctypes.c_char_p
+
+_CUDA_SIGS = {
+    "edgexpu_cuda_abi_version": (_c_int, []),
+    "edgexpu_cuda_init": (_c_int, [_c_int, _c_str, _c_sz]),
+    "edgexpu_cuda_shutdown": (_c_int, []),
+    "edgexpu_cuda_last_error": (_c_str, []),
+    "edgexpu_cuda_upload_weight": (_c_int, [_c_vp, _c_sz, _c_u32, _c_int, _c_int, ctypes.POINTER(_c_vp), _c_str, _c_sz]),
+    "edgexpu_cuda_register_weight": (_c_int, [_c_vp, _c_sz, _c_u32, _c_int, _c_int, _c_str, _c_sz]),
+    "edgexpu_cuda_free_weight": (_c_int, [_c_vp]),
+    "edgexpu_cuda_quantize_q8_0": (_c_int, [_c_vp, _c_int, _c_vp, _c_str, _c_sz]),
+    "edgexpu_cuda_quantize_q8_k": (_c_int, [_c_vp, _c_int, _c_vp, _c_str, _c_sz]),
+    "edgexpu_cuda_linear_quant_batch": (
+        _c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int, _c_str, _c_sz]),
+    "edgexpu_cuda_logits_argmax": (
+        _c_int, [_c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp, ctypes.POINTER(_c_u32), _c_f32p, _c_str, _c_sz]),
+    "edgexpu_cuda_quantize_dev": (_c_int, [_c_u32, _c_vp, _c_int, _c_int, _c_vp, _c_vp]),
+    "edgexpu_cuda_linear_quant_batch_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int, _c_vp]),
+    "edgexpu_cuda_logits_argmax_dev": (_c_int, [_c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp, ctypes.c_int64, _c_vp, _c_vp]),
+    "edgexpu_cuda_block_partials_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_int, _c_int, _c_int, _c_vp]),
+    "edgexpu_cuda_reserve": (_c_int, [_c_int, _c_int, _c_str, _c_sz]),
+    "edgexpu_cuda_stream_sync": (_c_int, [_c_vp, _c_str, _c_sz]),
+}
+
+_HOST_SIGS = {
+    "edgexpu_cpu_linear_quant": (None, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int]),
+    "edgexpu_cpu_linear_quant_batch": (None, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int]),
+    "edgexpu_gguf_q8_0_nbytes": (_c_sz, [_c_int]),
+    "edgexpu_gguf_quantize_q8_0": (_c_int, [_c_vp, _c_int, _c_vp]),
+    "edgexpu_gguf_can_dot_q8": (_c_int, [_c_u32]),
+    "edgexpu_gguf_q8_k_nbytes": (_c_sz, [_c_int]),
+    "edgexpu_gguf_quantize_q8_k": (_c_int, [_c_vp, _c_int, _c_vp]),
+    "edgexpu_gguf_can_dot_q8k": (_c_int, [_c_u32]),
+    "edgexpu_b200_init": (_c_int, [_c_int, _c_str, _c_sz]),
+    "edgexpu_b200_shutdown": (None, []),
+    "edgexpu_b200_last_error": (_c_str, []),
+    "edgexpu_b200_clear_error": (None, []),
+    "edgexpu_b200_logits_greedy": (_c_int, [_c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp, ctypes.POINTER(_c_u32), _c_str, _c_sz]),
+}
+
+_libs: dict[str, ctypes.CDLL] = {}
+
+
+def _bind(path: pathlib.Path, sigs: dict) -> ctypes.CDLL:
+    if not path.exists():
+        raise ImportError(f"{path} is missing: build it with `make -C {PKG_DIR}` (no CPU fallback exists)")
+    lib = ctypes.CDLL(str(path))
+    for name, (res, args) in sigs.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+def load_cuda() -> ctypes.CDLL:
+    """The CUDA C ABI (raises ImportError if the library has not been built)."""
+    if "cuda" not in _libs:
+        _libs["cuda"] = _bind(CUDA_LIB, _CUDA_SIGS)
+    return _libs["cuda"]
+
+
+def load_host() -> ctypes.CDLL:
+    """The C host shim with the reference's entry-point names."""
+    if "host" not in _libs:
+        load_cuda()
+        _libs["host"] = _bind(HOST_LIB, _HOST_SIGS)
+    return _libs["host"]
+
+
+class EdgexpuError(RuntimeError):
+    pass
+
+
+def _err_buf():
+    return ctypes.create_string_buffer(512)
+
+
+def _check(ok: int, buf=None) -> None:
+    if not ok:
+        msg = buf.value.decode() if buf is not None and buf.value else load_cuda().edgexpu_cuda_last_error().decode()
+        raise EdgexpuError(msg)
+
+
+def row_bytes(wtype: int, n: int) -> int:
+    if wtype == TYPE_Q8_0:
+        return (n // QK8_0) * Q8_0_BYTES
+    if wtype == TYPE_Q4_K:
+        return (n // QK_K) * Q4_K_BYTES
+    raise ValueError(f"unsupported type {wtype}")
+
+
+def act_row_bytes(wtype: int, n: int) -> int:
+    return (n // QK8_0) * Q8_0_BYTES if wtype == TYPE_Q8_0 else (n // QK_K) * Q8_K_BYTES
+
+
+def init(device: int = 0) -> None:
+    buf = _err_buf()
+    _check(load_cuda().edgexpu_cuda_init(device, buf, 512), buf)
+
+
+def shutdown() -> None:
+    load_cuda().edgexpu_cuda_shutdown()
+
+
+def _ptr(a) -> int:
+    """Address of a numpy array (host) or torch tensor (device or host)."""
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+def upload_weight(w_bytes, wtype: int, n_out: int, n_in: int) -> int:
+    """Upload a packed GGUF tensor (numpy uint8) once; returns the device handle (int)."""
+    import numpy as np
+
+    w_bytes = np.ascontiguousarray(w_bytes, dtype=np.uint8)
+    h = _c_vp()
+    buf = _err_buf()
+    _check(load_cuda().edgexpu_cuda_upload_weight(w_bytes.ctypes.data, w_bytes.nbytes, wtype, n_out, n_in,
+                                                  ctypes.byref(h), buf, 512), buf)
+    return int(h.value)
+
+
+def register_weight(dev_tensor, wtype: int, n_out: int, n_in: int) -> int:
+    """Register caller-owned device memory (a torch uint8 CUDA tensor with >= 16 spare bytes)."""
+    buf = _err_buf()
+    _check(load_cuda().edgexpu_cuda_register_weight(dev_tensor.data_ptr(), dev_tensor.numel(), wtype, n_out, n_in,
+                                                    buf, 512), buf)
+    return int(dev_tensor.data_ptr())
+
+
+def free_weight(handle: int) -> None:
+    load_cuda().edgexpu_cuda_free_weight(handle)
+
+
+def quantize(x, wtype: int):
+    """Quantize one fp32 row on the GPU through the host-buffer C ABI (returns numpy uint8)."""
+    import numpy as np
+
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.empty(act_row_bytes(wtype, x.size), np.uint8)
+    buf = _err_buf()
+    fn = load_cuda().edgexpu_cuda_quantize_q8_0 if wtype == TYPE_Q8_0 else load_cuda().edgexpu_cuda_quantize_q8_k
+    _check(fn(x.ctypes.data, x.size, out.ctypes.data, buf, 512), buf)
+    return out
+
+
+def linear_quant_batch(x, handle: int, wtype: int, n_out: int, bias=None):
+    """out[m][n_out] through the reference-named host shim ``edgexpu_cpu_linear_quant_batch``."""
+    import numpy as np
+
+    host = load_host()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if x.ndim == 1:
+        x = x[None, :]
+    m, n_in = x.shape
+    out = np.empty((m, n_out), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    host.edgexpu_b200_clear_error()
+    host.edgexpu_cpu_linear_quant_batch(out.ctypes.data, x.ctypes.data, handle, wtype,
+                                        None if b is None else b.ctypes.data, m, n_out, n_in)
+    err = host.edgexpu_b200_last_error()
+    if err:
+        raise EdgexpuError(err.decode())
+    return out
+
+
+def logits_greedy(handle: int, wtype: int, hidden, vocab: int, bias=None):
+    """(token_id, best_score) through the C ABI's synchronous greedy-logits call."""
+    import numpy as np
+
+    h = np.ascontiguousarray(hidden, dtype=np.float32).ravel()
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    tok = _c_u32()
+    score = ctypes.c_float()
+    buf = _err_buf()
+    _check(load_cuda().edgexpu_cuda_logits_argmax(handle, wtype, h.ctypes.data, h.size, vocab,
+                                                  None if b is None else b.ctypes.data, ctypes.byref(tok),
+                                                  ctypes.byref(score), buf, 512), buf)
+    return int(tok.value), float(score.value)
+
+
+def key_to_id(key: int) -> int:
+    return 0 if key == 0 else 0xFFFFFFFF - (key & 0xFFFFFFFF)

@@ -1,0 +1,501 @@
+// capi.cu -- the C ABI of libedgexpu_cuda.so (declared in include/edgexpu_cuda.h).
+//
+// Owns the per-process device context: the CUDA stream, the weight registry (device address
+// ranges of every uploaded or registered GGUF tensor), the activation/output scratch in HBM,
+// pinned host staging for the synchronous host-buffer calls, and the device status word the
+// kernels report timeouts through.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+
+#include "../../include/edgexpu_cuda.h"
+#include "common.cuh"
+#include "launch.h"
+
+namespace {
+
+struct WeightRec {
+  size_t capacity;
+  uint32_t type;
+  int n_out;
+  int n_in;
+  bool owned;
+};
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+};
+
+struct HostBuf {
+  void* p = nullptr;
+  size_t cap = 0;
+};
+
+struct Ctx {
+  bool ready = false;
+  int device = -1;
+  cudaStream_t stream = nullptr;
+  ex::DeviceInfo info{};
+  std::map<uintptr_t, WeightRec> weights;
+  DevBuf x, xq, out, bias;
+  HostBuf hx, hout, hbias;
+  unsigned long long* d_key = nullptr;
+  uint32_t* d_status = nullptr;
+  unsigned long long* h_key = nullptr;
+  uint32_t* h_status = nullptr;
+};
+
+Ctx g;
+std::recursive_mutex g_mu;
+char g_err[512] = "";
+
+int fail(char* error, size_t error_size, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  if (error != nullptr && error_size > 0) snprintf(error, error_size, "%s", g_err);
+  return 0;
+}
+
+#define EX_CUDA(call, error, error_size)                                                                   \
+  do {                                                                                                     \
+    cudaError_t e_ = (call);                                                                               \
+    if (e_ != cudaSuccess) return fail(error, error_size, "%s: %s", #call, cudaGetErrorString(e_));       \
+  } while (0)
+
+size_t row_bytes_of(uint32_t type, int n) {
+  if (n <= 0) return 0;
+  if (type == ex::TYPE_Q8_0) return (n % ex::QK8_0) ? 0 : static_cast<size_t>(n / ex::QK8_0) * ex::Q8_0_BYTES;
+  if (type == ex::TYPE_Q4_K) return (n % ex::QK_K) ? 0 : static_cast<size_t>(n / ex::QK_K) * ex::Q4_K_BYTES;
+  return 0;
+}
+
+size_t act_row_bytes_of(uint32_t type, int n) {
+  if (type == ex::TYPE_Q8_0) return static_cast<size_t>(n / ex::QK8_0) * ex::Q8_0_BYTES;
+  return static_cast<size_t>(n / ex::QK_K) * ex::Q8_K_BYTES;
+}
+
+cudaStream_t pick(void* stream) { return stream != nullptr ? static_cast<cudaStream_t>(stream) : g.stream; }
+
+int need_ready(char* error, size_t error_size) {
+  if (!g.ready) return fail(error, error_size, "edgexpu_cuda_init has not been called");
+  cudaError_t e = cudaSetDevice(g.device);
+  if (e != cudaSuccess) return fail(error, error_size, "cudaSetDevice: %s", cudaGetErrorString(e));
+  return 1;
+}
+
+bool capturing(cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) return false;
+  return cs != cudaStreamCaptureStatusNone;
+}
+
+int grow_dev(DevBuf& b, size_t need, cudaStream_t st, char* error, size_t error_size) {
+  if (b.cap >= need) return 1;
+  if (capturing(st)) return fail(error, error_size, "scratch must grow during stream capture; call edgexpu_cuda_reserve first");
+  size_t cap = std::max<size_t>(need, 2 * b.cap);
+  cap = (cap + 4095) & ~static_cast<size_t>(4095);
+  EX_CUDA(cudaDeviceSynchronize(), error, error_size);
+  if (b.p != nullptr) cudaFree(b.p);
+  b.p = nullptr;
+  b.cap = 0;
+  EX_CUDA(cudaMalloc(&b.p, cap), error, error_size);
+  b.cap = cap;
+  return 1;
+}
+
+int grow_host(HostBuf& b, size_t need, char* error, size_t error_size) {
+  if (b.cap >= need) return 1;
+  size_t cap = std::max<size_t>(need, 2 * b.cap);
+  cap = (cap + 4095) & ~static_cast<size_t>(4095);
+  if (b.p != nullptr) {
+    EX_CUDA(cudaDeviceSynchronize(), error, error_size);
+    cudaFreeHost(b.p);
+  }
+  b.p = nullptr;
+  b.cap = 0;
+  EX_CUDA(cudaHostAlloc(&b.p, cap, cudaHostAllocDefault), error, error_size);
+  b.cap = cap;
+  return 1;
+}
+
+// Find the registered tensor holding rows [weight, weight + n_out rows) of width n_in.
+int lookup(const uint8_t* weight, uint32_t type, int n_out, int n_in, char* error, size_t error_size) {
+  const size_t rb = row_bytes_of(type, n_in);
+  if (rb == 0) return fail(error, error_size, "unsupported weight type %u or n_in %d (Q8_0: n_in %% 32, Q4_K: n_in %% 256)", type, n_in);
+  const uintptr_t w = reinterpret_cast<uintptr_t>(weight);
+  auto it = g.weights.upper_bound(w);
+  if (it == g.weights.begin()) return fail(error, error_size, "weight %p is not a registered device tensor", weight);
+  --it;
+  const WeightRec& rec = it->second;
+  const uintptr_t base = it->first;
+  if (w >= base + rec.capacity) return fail(error, error_size, "weight %p is not a registered device tensor", weight);
+  if (rec.type != type) return fail(error, error_size, "weight %p was registered with type %u, called with %u", weight, rec.type, type);
+  if (rec.n_in != n_in) return fail(error, error_size, "weight %p was registered with n_in %d, called with %d", weight, rec.n_in, n_in);
+  if ((w - base) % rb != 0) return fail(error, error_size, "weight %p does not point at a row start", weight);
+  const size_t row = (w - base) / rb;
+  if (row + static_cast<size_t>(n_out) > static_cast<size_t>(rec.n_out))
+    return fail(error, error_size, "rows [%zu, %zu) exceed the tensor's %d rows", row, row + n_out, rec.n_out);
+  return 1;
+}
+
+int run_linear_dev(float* out, const float* x, const uint8_t* weight, uint32_t type, const float* bias, int m,
+                   int n_out, int n_in, cudaStream_t st, char* error, size_t error_size) {
+  if (out == nullptr || x == nullptr || weight == nullptr || m <= 0 || n_out <= 0 || n_in <= 0)
+    return fail(error, error_size, "invalid arguments");
+  if (!lookup(weight, type, n_out, n_in, error, error_size)) return 0;
+  const size_t qb = act_row_bytes_of(type, n_in);
+  if (!grow_dev(g.xq, static_cast<size_t>(m) * qb + 64, st, error, error_size)) return 0;
+  uint8_t* xq = static_cast<uint8_t*>(g.xq.p);
+  const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  const int max_m = ex::rowstream_max_m(fmt, n_in, g.info);
+  if (max_m <= 0) return fail(error, error_size, "n_in %d too large for the shared-memory activation tile", n_in);
+  EX_CUDA(type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n_in, xq, st) : ex::launch_quantize_q8_k(x, m, n_in, xq, st),
+          error, error_size);
+  for (int t0 = 0; t0 < m; t0 += max_m) {
+    ex::RowStreamArgs a{};
+    a.fmt = fmt;
+    a.mode = ex::RowOut::Store;
+    a.w = weight;
+    a.n_rows = n_out;
+    a.row0 = 0;
+    a.row_bytes = static_cast<int>(row_bytes_of(type, n_in));
+    a.K = n_in;
+    a.m = std::min(max_m, m - t0);
+    a.act = xq + static_cast<size_t>(t0) * qb;
+    a.act_row_bytes = static_cast<int>(qb);
+    a.bias = bias;
+    a.out = out + static_cast<size_t>(t0) * n_out;
+    a.out_stride = n_out;
+    a.status = g.d_status;
+    EX_CUDA(ex::launch_rowstream(a, g.info, st), error, error_size);
+  }
+  return 1;
+}
+
+int run_logits_dev(const uint8_t* weight, uint32_t type, const float* hidden, int n_embd, int vocab, const float* bias,
+                   int64_t row0, unsigned long long* key, cudaStream_t st, char* error, size_t error_size) {
+  if (weight == nullptr || hidden == nullptr || key == nullptr || n_embd <= 0 || vocab <= 0)
+    return fail(error, error_size, "invalid arguments");
+  if (row0 < 0 || row0 + vocab > 0xFFFFFFFFll) return fail(error, error_size, "row0 %lld out of range", (long long)row0);
+  if (!lookup(weight, type, vocab, n_embd, error, error_size)) return 0;
+  EX_CUDA(cudaMemsetAsync(key, 0, sizeof(unsigned long long), st), error, error_size);
+  ex::RowStreamArgs a{};
+  a.mode = ex::RowOut::Argmax;
+  a.w = weight;
+  a.n_rows = vocab;
+  a.row0 = row0;
+  a.row_bytes = static_cast<int>(row_bytes_of(type, n_embd));
+  a.K = n_embd;
+  a.m = 1;
+  a.bias = bias;
+  a.key = key;
+  a.status = g.d_status;
+  if (type == ex::TYPE_Q8_0) {
+    // native.c:2317-2319: Q8_0-class logits weights see a Q8_0-quantized hidden state.
+    const size_t qb = act_row_bytes_of(type, n_embd);
+    if (!grow_dev(g.xq, qb + 64, st, error, error_size)) return 0;
+    EX_CUDA(ex::launch_quantize_q8_0(hidden, 1, n_embd, static_cast<uint8_t*>(g.xq.p), st), error, error_size);
+    a.fmt = ex::Fmt::Q8_0xQ8_0;
+    a.act = g.xq.p;
+    a.act_row_bytes = static_cast<int>(qb);
+  } else {
+    // logit_dot_row native.c:445-462 -> dot_q4_k gguf_quant.c:704-752: fp32 hidden state.
+    a.fmt = ex::Fmt::Q4_KxF32;
+    a.act = hidden;
+    a.act_row_bytes = n_embd * 4;
+  }
+  if (ex::rowstream_max_m(a.fmt, n_embd, g.info) < 1) return fail(error, error_size, "n_embd %d too large", n_embd);
+  EX_CUDA(ex::launch_rowstream(a, g.info, st), error, error_size);
+  return 1;
+}
+
+int check_status(char* error, size_t error_size) {
+  // Called after the stream was synchronised and the status word copied to h_status.
+  if (*g.h_status != 0) {
+    const uint32_t s = *g.h_status;
+    *g.h_status = 0;
+    cudaMemset(g.d_status, 0, sizeof(uint32_t));
+    return fail(error, error_size, "device wait timed out (status 0x%x): a tile copy never completed", s);
+  }
+  return 1;
+}
+
+int sync_and_check(cudaStream_t st, char* error, size_t error_size) {
+  EX_CUDA(cudaMemcpyAsync(g.h_status, g.d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost, st), error, error_size);
+  EX_CUDA(cudaStreamSynchronize(st), error, error_size);
+  return check_status(error, error_size);
+}
+
+}  // namespace
+
+extern "C" {
+
+int edgexpu_cuda_abi_version(void) { return EDGEXPU_CUDA_ABI_VERSION; }
+
+const char* edgexpu_cuda_last_error(void) { return g_err; }
+
+int edgexpu_cuda_init(int device, char* error, size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (g.ready) {
+    if (g.device == device) return 1;
+    return fail(error, error_size, "already initialised on device %d", g.device);
+  }
+  int n = 0;
+  EX_CUDA(cudaGetDeviceCount(&n), error, error_size);
+  if (device < 0 || device >= n) return fail(error, error_size, "CUDA device %d not present (%d devices)", device, n);
+  EX_CUDA(cudaSetDevice(device), error, error_size);
+  int major = 0, minor = 0;
+  EX_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device), error, error_size);
+  EX_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device), error, error_size);
+  if (major != 10 || minor != 0) return fail(error, error_size, "device %d is sm_%d%d; this build targets sm_100a (B200)", device, major, minor);
+  EX_CUDA(cudaDeviceGetAttribute(&g.info.sm_count, cudaDevAttrMultiProcessorCount, device), error, error_size);
+  EX_CUDA(cudaDeviceGetAttribute(&g.info.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device), error, error_size);
+  EX_CUDA(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking), error, error_size);
+  EX_CUDA(cudaMalloc(reinterpret_cast<void**>(&g.d_key), 64), error, error_size);
+  EX_CUDA(cudaMalloc(reinterpret_cast<void**>(&g.d_status), 64), error, error_size);
+  EX_CUDA(cudaMemset(g.d_status, 0, 64), error, error_size);
+  EX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&g.h_key), 64, cudaHostAllocDefault), error, error_size);
+  EX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&g.h_status), 64, cudaHostAllocDefault), error, error_size);
+  *g.h_status = 0;
+  g.device = device;
+  g.ready = true;
+  return 1;
+}
+
+int edgexpu_cuda_shutdown(void) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!g.ready) return 1;
+  cudaSetDevice(g.device);
+  cudaDeviceSynchronize();
+  for (auto& kv : g.weights)
+    if (kv.second.owned) cudaFree(reinterpret_cast<void*>(kv.first));
+  g.weights.clear();
+  for (DevBuf* b : {&g.x, &g.xq, &g.out, &g.bias})
+    if (b->p) cudaFree(b->p);
+  for (HostBuf* b : {&g.hx, &g.hout, &g.hbias})
+    if (b->p) cudaFreeHost(b->p);
+  cudaFree(g.d_key);
+  cudaFree(g.d_status);
+  cudaFreeHost(g.h_key);
+  cudaFreeHost(g.h_status);
+  cudaStreamDestroy(g.stream);
+  g = Ctx{};
+  return 1;
+}
+
+int edgexpu_cuda_upload_weight(const uint8_t* host, size_t nbytes, uint32_t type, int n_out, int n_in,
+                               const uint8_t** handle, char* error, size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  const size_t rb = row_bytes_of(type, n_in);
+  if (host == nullptr || handle == nullptr || n_out <= 0 || rb == 0) return fail(error, error_size, "invalid arguments");
+  if (rb > (1u << 19)) return fail(error, error_size, "row of %zu bytes too large", rb);
+  if (nbytes < rb * static_cast<size_t>(n_out)) return fail(error, error_size, "%zu bytes < %d rows x %zu", nbytes, n_out, rb);
+  const size_t data = rb * static_cast<size_t>(n_out);
+  const size_t cap = ((data + 255) & ~static_cast<size_t>(255)) + 256;  // padding for the aligned tail copy
+  void* d = nullptr;
+  EX_CUDA(cudaMalloc(&d, cap), error, error_size);
+  cudaError_t e = cudaMemcpy(d, host, data, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(static_cast<uint8_t*>(d) + data, 0, cap - data);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return fail(error, error_size, "upload: %s", cudaGetErrorString(e));
+  }
+  g.weights[reinterpret_cast<uintptr_t>(d)] = WeightRec{cap, type, n_out, n_in, true};
+  *handle = static_cast<const uint8_t*>(d);
+  return 1;
+}
+
+int edgexpu_cuda_register_weight(const void* device_ptr, size_t capacity, uint32_t type, int n_out, int n_in,
+                                 char* error, size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  const size_t rb = row_bytes_of(type, n_in);
+  if (device_ptr == nullptr || n_out <= 0 || rb == 0) return fail(error, error_size, "invalid arguments");
+  if (rb > (1u << 19)) return fail(error, error_size, "row of %zu bytes too large", rb);
+  if (reinterpret_cast<uintptr_t>(device_ptr) & 15u) return fail(error, error_size, "device_ptr must be 16-byte aligned");
+  if (capacity < rb * static_cast<size_t>(n_out) + 16) return fail(error, error_size, "capacity must cover the rows plus 16 bytes");
+  cudaPointerAttributes attr{};
+  EX_CUDA(cudaPointerGetAttributes(&attr, device_ptr), error, error_size);
+  if (attr.type != cudaMemoryTypeDevice || attr.device != g.device)
+    return fail(error, error_size, "device_ptr is not device memory of device %d", g.device);
+  g.weights[reinterpret_cast<uintptr_t>(device_ptr)] = WeightRec{capacity, type, n_out, n_in, false};
+  return 1;
+}
+
+int edgexpu_cuda_free_weight(const void* handle) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  auto it = g.weights.find(reinterpret_cast<uintptr_t>(handle));
+  if (it == g.weights.end()) return fail(nullptr, 0, "free_weight: %p is not a registered handle", handle);
+  if (it->second.owned) {
+    cudaDeviceSynchronize();
+    cudaFree(const_cast<void*>(handle));
+  }
+  g.weights.erase(it);
+  return 1;
+}
+
+static int quantize_host(uint32_t wtype, const float* x, int n, uint8_t* dst, char* error, size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  const int blk = wtype == ex::TYPE_Q8_0 ? ex::QK8_0 : ex::QK_K;
+  if (x == nullptr || dst == nullptr || n <= 0 || n % blk != 0) return fail(error, error_size, "invalid arguments");
+  const size_t qb = act_row_bytes_of(wtype, n);
+  cudaStream_t st = g.stream;
+  if (!grow_host(g.hx, static_cast<size_t>(n) * 4, error, error_size) || !grow_dev(g.x, static_cast<size_t>(n) * 4, st, error, error_size) ||
+      !grow_dev(g.xq, qb + 64, st, error, error_size) || !grow_host(g.hout, qb, error, error_size))
+    return 0;
+  std::memcpy(g.hx.p, x, static_cast<size_t>(n) * 4);
+  EX_CUDA(cudaMemcpyAsync(g.x.p, g.hx.p, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, st), error, error_size);
+  uint8_t* xq = static_cast<uint8_t*>(g.xq.p);
+  EX_CUDA(wtype == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(static_cast<float*>(g.x.p), 1, n, xq, st)
+                                 : ex::launch_quantize_q8_k(static_cast<float*>(g.x.p), 1, n, xq, st),
+          error, error_size);
+  EX_CUDA(cudaMemcpyAsync(g.hout.p, xq, qb, cudaMemcpyDeviceToHost, st), error, error_size);
+  EX_CUDA(cudaStreamSynchronize(st), error, error_size);
+  std::memcpy(dst, g.hout.p, qb);
+  return 1;
+}
+
+int edgexpu_cuda_quantize_q8_0(const float* x, int n, uint8_t* dst, char* error, size_t error_size) {
+  return quantize_host(ex::TYPE_Q8_0, x, n, dst, error, error_size);
+}
+
+int edgexpu_cuda_quantize_q8_k(const float* x, int n, uint8_t* dst, char* error, size_t error_size) {
+  return quantize_host(ex::TYPE_Q4_K, x, n, dst, error, error_size);
+}
+
+int edgexpu_cuda_linear_quant_batch(float* out, const float* x, const uint8_t* weight, uint32_t type, const float* bias,
+                                    int m, int n_out, int n_in, char* error, size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  if (out == nullptr || x == nullptr || weight == nullptr || m <= 0 || n_out <= 0 || n_in <= 0)
+    return fail(error, error_size, "invalid arguments");
+  if (!lookup(weight, type, n_out, n_in, error, error_size)) return 0;
+  cudaStream_t st = g.stream;
+  const size_t xb = static_cast<size_t>(m) * n_in * 4, ob = static_cast<size_t>(m) * n_out * 4;
+  const size_t bb = bias != nullptr ? static_cast<size_t>(n_out) * 4 : 0;
+  if (!grow_host(g.hx, xb, error, error_size) || !grow_dev(g.x, xb, st, error, error_size) ||
+      !grow_host(g.hout, ob, error, error_size) || !grow_dev(g.out, ob, st, error, error_size))
+    return 0;
+  if (bb && (!grow_host(g.hbias, bb, error, error_size) || !grow_dev(g.bias, bb, st, error, error_size))) return 0;
+  std::memcpy(g.hx.p, x, xb);
+  EX_CUDA(cudaMemcpyAsync(g.x.p, g.hx.p, xb, cudaMemcpyHostToDevice, st), error, error_size);
+  if (bb) {
+    std::memcpy(g.hbias.p, bias, bb);
+    EX_CUDA(cudaMemcpyAsync(g.bias.p, g.hbias.p, bb, cudaMemcpyHostToDevice, st), error, error_size);
+  }
+  if (!run_linear_dev(static_cast<float*>(g.out.p), static_cast<const float*>(g.x.p), weight, type,
+                      bb ? static_cast<const float*>(g.bias.p) : nullptr, m, n_out, n_in, st, error, error_size))
+    return 0;
+  EX_CUDA(cudaMemcpyAsync(g.hout.p, g.out.p, ob, cudaMemcpyDeviceToHost, st), error, error_size);
+  if (!sync_and_check(st, error, error_size)) return 0;
+  std::memcpy(out, g.hout.p, ob);
+  return 1;
+}
+
+int edgexpu_cuda_logits_argmax(const uint8_t* weight, uint32_t type, const float* hidden, int n_embd, int vocab,
+                               const float* bias, uint32_t* token_id, float* best_score, char* error,
+                               size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  if (hidden == nullptr || token_id == nullptr || n_embd <= 0 || vocab <= 0) return fail(error, error_size, "invalid arguments");
+  cudaStream_t st = g.stream;
+  const size_t hb = static_cast<size_t>(n_embd) * 4, bb = bias != nullptr ? static_cast<size_t>(vocab) * 4 : 0;
+  if (!grow_host(g.hx, hb, error, error_size) || !grow_dev(g.x, hb, st, error, error_size)) return 0;
+  if (bb && (!grow_host(g.hbias, bb, error, error_size) || !grow_dev(g.bias, bb, st, error, error_size))) return 0;
+  std::memcpy(g.hx.p, hidden, hb);
+  EX_CUDA(cudaMemcpyAsync(g.x.p, g.hx.p, hb, cudaMemcpyHostToDevice, st), error, error_size);
+  if (bb) {
+    std::memcpy(g.hbias.p, bias, bb);
+    EX_CUDA(cudaMemcpyAsync(g.bias.p, g.hbias.p, bb, cudaMemcpyHostToDevice, st), error, error_size);
+  }
+  if (!run_logits_dev(weight, type, static_cast<const float*>(g.x.p), n_embd, vocab,
+                      bb ? static_cast<const float*>(g.bias.p) : nullptr, 0, g.d_key, st, error, error_size))
+    return 0;
+  EX_CUDA(cudaMemcpyAsync(g.h_key, g.d_key, 8, cudaMemcpyDeviceToHost, st), error, error_size);
+  if (!sync_and_check(st, error, error_size)) return 0;
+  const unsigned long long key = *g.h_key;
+  *token_id = edgexpu_cuda_argmax_key_id(key);
+  if (best_score != nullptr) {
+    uint32_t u = static_cast<uint32_t>(key >> 32);
+    u = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
+    float s;
+    std::memcpy(&s, &u, 4);
+    *best_score = key == 0 ? -INFINITY : s;
+  }
+  return 1;
+}
+
+int edgexpu_cuda_quantize_dev(uint32_t weight_type, const float* x, int m, int n, uint8_t* dst, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(nullptr, 0)) return 0;
+  const int blk = weight_type == ex::TYPE_Q8_0 ? ex::QK8_0 : (weight_type == ex::TYPE_Q4_K ? ex::QK_K : 0);
+  if (blk == 0 || x == nullptr || dst == nullptr || m <= 0 || n <= 0 || n % blk != 0) return fail(nullptr, 0, "invalid arguments");
+  cudaStream_t st = pick(stream);
+  EX_CUDA(weight_type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n, dst, st) : ex::launch_quantize_q8_k(x, m, n, dst, st),
+          nullptr, 0);
+  return 1;
+}
+
+int edgexpu_cuda_linear_quant_batch_dev(float* out, const float* x, const uint8_t* weight, uint32_t type,
+                                        const float* bias, int m, int n_out, int n_in, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(nullptr, 0)) return 0;
+  return run_linear_dev(out, x, weight, type, bias, m, n_out, n_in, pick(stream), nullptr, 0);
+}
+
+int edgexpu_cuda_logits_argmax_dev(const uint8_t* weight, uint32_t type, const float* hidden, int n_embd, int vocab,
+                                   const float* bias, int64_t row0, uint64_t* key, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(nullptr, 0)) return 0;
+  return run_logits_dev(weight, type, hidden, n_embd, vocab, bias, row0, reinterpret_cast<unsigned long long*>(key),
+                        pick(stream), nullptr, 0);
+}
+
+int edgexpu_cuda_block_partials_dev(int32_t* partials, const uint8_t* xq, const uint8_t* weight, uint32_t type, int m,
+                                    int n_out, int n_in, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(nullptr, 0)) return 0;
+  if (partials == nullptr || xq == nullptr || m <= 0) return fail(nullptr, 0, "invalid arguments");
+  if (!lookup(weight, type, n_out, n_in, nullptr, 0)) return 0;
+  ex::RowStreamArgs a{};
+  a.fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  a.mode = ex::RowOut::Partials;
+  a.w = weight;
+  a.n_rows = n_out;
+  a.row_bytes = static_cast<int>(row_bytes_of(type, n_in));
+  a.K = n_in;
+  a.m = m;
+  a.act = xq;
+  a.act_row_bytes = static_cast<int>(act_row_bytes_of(type, n_in));
+  a.partials = partials;
+  a.status = g.d_status;
+  if (ex::rowstream_max_m(a.fmt, n_in, g.info) < m) return fail(nullptr, 0, "m %d too large for one partials launch", m);
+  EX_CUDA(ex::launch_rowstream(a, g.info, pick(stream)), nullptr, 0);
+  return 1;
+}
+
+int edgexpu_cuda_reserve(int m, int n_in, char* error, size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  if (m <= 0 || n_in <= 0) return fail(error, error_size, "invalid arguments");
+  const size_t need = static_cast<size_t>(m) * std::max(act_row_bytes_of(ex::TYPE_Q8_0, n_in), act_row_bytes_of(ex::TYPE_Q4_K, n_in)) + 64;
+  return grow_dev(g.xq, need, g.stream, error, error_size);
+}
+
+int edgexpu_cuda_stream_sync(void* stream, char* error, size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  return sync_and_check(pick(stream), error, error_size);
+}
+
+}  // extern "C"

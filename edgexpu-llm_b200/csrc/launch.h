@@ -1,0 +1,57 @@
+// launch.h -- host-side launchers of the edgexpu CUDA kernels (internal to libedgexpu_cuda.so).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ex {
+
+// Activation quantizers (device buffers, stream ordered).
+//   x: [m][n] fp32 rows; dst: [m][n/32 * 34] (Q8_0) or [m][n/256 * 292] (Q8_K), GGUF layout.
+cudaError_t launch_quantize_q8_0(const float* x, int m, int n, uint8_t* dst, cudaStream_t st);
+cudaError_t launch_quantize_q8_k(const float* x, int m, int n, uint8_t* dst, cudaStream_t st);
+
+// What the row-stream kernel does with each finished row.
+enum class RowOut : int {
+  Store = 0,     // out[t*out_stride + r] = bias[r] + dot
+  Argmax = 1,    // atomicMax of argmax_key(bias[r] + dot, row0 + r) into *key (m == 1)
+  Partials = 2,  // per-block int32 partials instead of the float dot (test hook)
+};
+
+enum class Fmt : int {
+  Q8_0xQ8_0 = 0,  // Q8_0 weight . Q8_0 activation   (gguf_dot_q8.c:436-480)
+  Q4_KxQ8_K = 1,  // Q4_K weight . Q8_K activation   (gguf_dot_q8.c:603-762)
+  Q4_KxF32 = 2,   // Q4_K weight . fp32 activation   (gguf_quant.c:704-752, logits path)
+};
+
+struct RowStreamArgs {
+  Fmt fmt;
+  RowOut mode;
+  const uint8_t* w;       // first weight row (device)
+  long long n_rows;
+  long long row0;         // global id of the first row (argmax ids)
+  int row_bytes;
+  int K;
+  int m;                  // activation rows (tokens)
+  const void* act;        // quantized activations [m][act_row_bytes], or fp32 [m][K] for Q4_KxF32
+  int act_row_bytes;
+  const float* bias;      // [n_rows] or nullptr
+  float* out;             // Store: [m][out_stride]
+  long long out_stride;
+  unsigned long long* key;  // Argmax
+  int32_t* partials;      // Partials: Q8_0 [m][n_rows][nb]; Q4_K [m][n_rows][nb][2] (sumi, summ)
+  uint32_t* status;       // device-visible status word
+};
+
+struct DeviceInfo {
+  int sm_count;
+  int max_smem_optin;
+};
+
+// Largest number of activation rows one row-stream launch keeps in shared memory for this K.
+int rowstream_max_m(Fmt fmt, int K, const DeviceInfo& dev);
+
+cudaError_t launch_rowstream(const RowStreamArgs& a, const DeviceInfo& dev, cudaStream_t st);
+
+}  // namespace ex

@@ -1,0 +1,124 @@
+/*
+ * edgexpu_cpu_kernel_cuda.c -- C host shim: the reference's quantized-linear and activation
+ * quantizer entry points, forwarding to the CUDA C ABI.  See include/edgexpu_b200_host.h.
+ *
+ * Reference counterparts (inside the reference project):
+ *   edgexpu_cpu_linear_quant_batch  src/cpu_kernel.c:545-644
+ *   edgexpu_cpu_linear_quant        src/cpu_kernel.c:646-656
+ *   edgexpu_gguf_quantize_q8_0/_k   src/gguf_dot_q8.c:269-412
+ *   edgexpu_gguf_q8_0/_k_nbytes     src/gguf_dot_q8.c:255-267
+ *   edgexpu_gguf_can_dot_q8(k)      src/gguf_dot_q8.c:414-434
+ */
+#include "../../include/edgexpu_b200_host.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "../../include/edgexpu_cuda.h"
+
+#define GGUF_TYPE_Q4_0 2u
+#define GGUF_TYPE_Q5_0 6u
+#define GGUF_TYPE_Q8_0 8u
+#define GGUF_TYPE_Q4_K 12u
+#define GGUF_TYPE_Q5_K 13u
+#define GGUF_TYPE_Q6_K 14u
+
+static char g_sticky[512];
+
+static void record(const char *what, const char *msg) {
+    if (g_sticky[0] == '\0') {
+        snprintf(g_sticky, sizeof g_sticky, "%s: %s", what, msg);
+    }
+}
+
+static void fill_nan(float *out, size_t n) {
+    size_t i;
+    for (i = 0; i < n; i++) {
+        out[i] = NAN;
+    }
+}
+
+int edgexpu_b200_init(int device, char *error, size_t error_size) {
+    return edgexpu_cuda_init(device, error, error_size);
+}
+
+void edgexpu_b200_shutdown(void) {
+    edgexpu_cuda_shutdown();
+}
+
+const char *edgexpu_b200_last_error(void) {
+    return g_sticky;
+}
+
+void edgexpu_b200_clear_error(void) {
+    g_sticky[0] = '\0';
+}
+
+void edgexpu_cpu_linear_quant_batch(float *out, const float *x, const uint8_t *weight, uint32_t type,
+                                    const float *bias, int m, int n_out, int n_in) {
+    char err[256];
+    if (out == NULL || x == NULL || weight == NULL || m <= 0 || n_out <= 0 || n_in <= 0) {
+        return; /* cpu_kernel.c:562-564 */
+    }
+    if (!edgexpu_cuda_linear_quant_batch(out, x, weight, type, bias, m, n_out, n_in, err, sizeof err)) {
+        record("edgexpu_cpu_linear_quant_batch", err);
+        fill_nan(out, (size_t)m * (size_t)n_out);
+    }
+}
+
+void edgexpu_cpu_linear_quant(float *out, const float *x, const uint8_t *weight, uint32_t type, const float *bias,
+                              int n_out, int n_in) {
+    edgexpu_cpu_linear_quant_batch(out, x, weight, type, bias, 1, n_out, n_in);
+}
+
+size_t edgexpu_gguf_q8_0_nbytes(int n) {
+    return (n <= 0 || n % 32 != 0) ? 0 : (size_t)(n / 32) * 34u;
+}
+
+size_t edgexpu_gguf_q8_k_nbytes(int n) {
+    return (n <= 0 || n % 256 != 0) ? 0 : (size_t)(n / 256) * 292u;
+}
+
+int edgexpu_gguf_can_dot_q8(uint32_t type) {
+    return type == GGUF_TYPE_Q4_0 || type == GGUF_TYPE_Q5_0 || type == GGUF_TYPE_Q8_0;
+}
+
+int edgexpu_gguf_can_dot_q8k(uint32_t type) {
+    return type == GGUF_TYPE_Q4_K || type == GGUF_TYPE_Q5_K || type == GGUF_TYPE_Q6_K;
+}
+
+int edgexpu_gguf_quantize_q8_0(const float *x, int n, uint8_t *dst) {
+    char err[256];
+    if (x == NULL || dst == NULL || n <= 0 || n % 32 != 0) {
+        return 0; /* gguf_dot_q8.c:272-274 */
+    }
+    if (!edgexpu_cuda_quantize_q8_0(x, n, dst, err, sizeof err)) {
+        record("edgexpu_gguf_quantize_q8_0", err);
+        return 0;
+    }
+    return 1;
+}
+
+int edgexpu_gguf_quantize_q8_k(const float *x, int n, uint8_t *dst) {
+    char err[256];
+    if (x == NULL || dst == NULL || n <= 0 || n % 256 != 0) {
+        return 0; /* gguf_dot_q8.c:363-365 */
+    }
+    if (!edgexpu_cuda_quantize_q8_k(x, n, dst, err, sizeof err)) {
+        record("edgexpu_gguf_quantize_q8_k", err);
+        return 0;
+    }
+    return 1;
+}
+
+int edgexpu_b200_logits_greedy(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
+                               const float *bias, uint32_t *token_id, char *error, size_t error_size) {
+    if (weight == NULL || hidden == NULL || token_id == NULL || vocab <= 0) {
+        if (error != NULL && error_size > 0) {
+            snprintf(error, error_size, "logits: missing weight, hidden state or vocab"); /* as native.c:2313-2315 */
+        }
+        return 0;
+    }
+    return edgexpu_cuda_logits_argmax(weight, type, hidden, n_embd, vocab, bias, token_id, NULL, error, error_size);
+}

@@ -1,0 +1,70 @@
+"""Seeded synthetic GGUF blocks following the recipes of the benchmark configurations.
+
+* Q8_0 weight block (34 B): fp16 d ~ U(1e-4, 2e-3), 32 int8 qs ~ U{-127..127}.
+* Q4_K super-block (144 B): fp16 d, dmin ~ U(1e-4, 1e-3); 12 scale bytes whose eight 6-bit
+  (scale, min) pairs are ~ U{0..63}; 128 bytes of nibbles ~ U{0..15}.  The 6-bit fields of the
+  packing (get_scale_min_k4, gguf_quant.c:212-220) are a bijection of the 96 scale bits, so
+  uniform random scale bytes give uniform independent (scale, min) pairs.
+* Activations: fp32 ~ N(0, 1).
+
+The numpy versions are used for parity tests; the torch versions generate the multi-GB
+benchmark tensors directly in HBM.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+Q8_0_BYTES, Q4_K_BYTES = 34, 144
+
+
+def _fp16_bits(v: np.ndarray) -> np.ndarray:
+    return v.astype(np.float16).view(np.uint8).reshape(v.shape + (2,))
+
+
+def q8_0_weight(rng: np.random.Generator, n_out: int, n_in: int) -> np.ndarray:
+    nb = n_in // 32
+    blk = np.empty((n_out, nb, Q8_0_BYTES), np.uint8)
+    blk[..., 0:2] = _fp16_bits(rng.uniform(1e-4, 2e-3, (n_out, nb)))
+    blk[..., 2:] = rng.integers(-127, 128, (n_out, nb, 32), dtype=np.int8).view(np.uint8)
+    return blk.reshape(n_out, nb * Q8_0_BYTES)
+
+
+def q4_k_weight(rng: np.random.Generator, n_out: int, n_in: int) -> np.ndarray:
+    nb = n_in // 256
+    blk = rng.integers(0, 256, (n_out, nb, Q4_K_BYTES), dtype=np.uint8)
+    blk[..., 0:2] = _fp16_bits(rng.uniform(1e-4, 1e-3, (n_out, nb)))
+    blk[..., 2:4] = _fp16_bits(rng.uniform(1e-4, 1e-3, (n_out, nb)))
+    return blk.reshape(n_out, nb * Q4_K_BYTES)
+
+
+def weight(rng: np.random.Generator, wtype: int, n_out: int, n_in: int) -> np.ndarray:
+    return q8_0_weight(rng, n_out, n_in) if wtype == 8 else q4_k_weight(rng, n_out, n_in)
+
+
+def activations(rng: np.random.Generator, m: int, n: int) -> np.ndarray:
+    return rng.standard_normal((m, n)).astype(np.float32)
+
+
+def torch_weight(wtype: int, n_out: int, n_in: int, generator, device, pad: int = 256):
+    """Same recipe generated on the device; returns a flat uint8 tensor with `pad` spare bytes."""
+    import torch
+
+    if wtype == 8:
+        nb, bb, lo, hi = n_in // 32, Q8_0_BYTES, 1e-4, 2e-3
+    else:
+        nb, bb, lo, hi = n_in // 256, Q4_K_BYTES, 1e-4, 1e-3
+    nblk = n_out * nb
+    flat = torch.empty(nblk * bb + pad, dtype=torch.uint8, device=device)
+    flat[nblk * bb:] = 0
+    blk = flat[: nblk * bb].view(nblk, bb)
+    if wtype == 8:
+        blk[:, 2:] = torch.randint(-127, 128, (nblk, 32), dtype=torch.int8, device=device,
+                                   generator=generator).view(torch.uint8)
+        d = torch.empty(nblk, dtype=torch.float32, device=device).uniform_(lo, hi, generator=generator)
+        blk[:, 0:2] = d.to(torch.float16).view(torch.uint8).view(nblk, 2)
+    else:
+        blk[:, 4:] = torch.randint(0, 256, (nblk, bb - 4), dtype=torch.uint8, device=device, generator=generator)
+        dd = torch.empty(nblk, 2, dtype=torch.float32, device=device).uniform_(lo, hi, generator=generator)
+        blk[:, 0:4] = dd.to(torch.float16).view(torch.uint8).view(nblk, 4)
+    return flat

@@ -1,0 +1,67 @@
+/*
+ * edgexpu_b200_host.h -- C host shim of libedgexpu_b200_host.so: the reference's own
+ * quantized-linear entry points, with bodies that forward to the CUDA C ABI (edgexpu_cuda.h).
+ *
+ * A maintainer drops this in by deleting the same-named definitions from the reference's
+ * src/cpu_kernel.c and src/gguf_dot_q8.c and linking this library; src/native.c's layer loop,
+ * src/backend_native.c and the src/arch plugins keep calling the same names.
+ *
+ * Signatures are identical to the reference (paths inside the reference project):
+ *   edgexpu_cpu_linear_quant        include/edgexpu/cpu_kernel.h:60-68
+ *   edgexpu_cpu_linear_quant_batch  include/edgexpu/cpu_kernel.h:71-80
+ *   edgexpu_gguf_quantize_q8_0      include/edgexpu/gguf_quant.h:80-81
+ *   edgexpu_gguf_quantize_q8_k      include/edgexpu/gguf_quant.h:85-86
+ *   edgexpu_gguf_q8_0_nbytes        include/edgexpu/gguf_quant.h:80
+ *   edgexpu_gguf_q8_k_nbytes        include/edgexpu/gguf_quant.h:85
+ *   edgexpu_gguf_can_dot_q8         include/edgexpu/gguf_quant.h:82
+ *   edgexpu_gguf_can_dot_q8k        include/edgexpu/gguf_quant.h:87
+ *
+ * Error behaviour follows the reference: the void linear entry points return silently on
+ * NULL / non-positive arguments (cpu_kernel.c:562-564).  A GPU-side failure (unregistered
+ * weight, unsupported type, CUDA error) fills `out` with NaN -- so the finite-RMS check of
+ * native.c:2232-2234 stops generation -- and records a sticky message readable through
+ * edgexpu_b200_last_error().  The quantizers return 1/0 like the reference.
+ *
+ * The shim adds three calls the reference has no counterpart for: init/shutdown of the device,
+ * the sticky error, and the greedy logits call that replaces sample_next_token's chunk loop
+ * (src/native.c:2355-2400).
+ */
+#ifndef EDGEXPU_B200_HOST_H
+#define EDGEXPU_B200_HOST_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+void edgexpu_cpu_linear_quant(float *out, const float *x, const uint8_t *weight, uint32_t type, const float *bias,
+                              int n_out, int n_in);
+void edgexpu_cpu_linear_quant_batch(float *out, const float *x, const uint8_t *weight, uint32_t type,
+                                    const float *bias, int m, int n_out, int n_in);
+
+size_t edgexpu_gguf_q8_0_nbytes(int n);
+int edgexpu_gguf_quantize_q8_0(const float *x, int n, uint8_t *dst);
+int edgexpu_gguf_can_dot_q8(uint32_t type);
+size_t edgexpu_gguf_q8_k_nbytes(int n);
+int edgexpu_gguf_quantize_q8_k(const float *x, int n, uint8_t *dst);
+int edgexpu_gguf_can_dot_q8k(uint32_t type);
+
+/* Binds the shim to a CUDA device; must run before the first linear call (edgexpu_native_load). */
+int edgexpu_b200_init(int device, char *error, size_t error_size);
+void edgexpu_b200_shutdown(void);
+/* Sticky message of the first failure since the last clear ("" if none). */
+const char *edgexpu_b200_last_error(void);
+void edgexpu_b200_clear_error(void);
+
+/* Greedy token for the logits weight (tied token_embd or output.weight), as sample_next_token
+ * with temperature <= 1e-4.  Returns 1/0 and fills error like the reference's session calls. */
+int edgexpu_b200_logits_greedy(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
+                               const float *bias, uint32_t *token_id, char *error, size_t error_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

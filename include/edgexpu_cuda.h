@@ -1,0 +1,120 @@
+/*
+ * edgexpu_cuda.h -- C ABI of libedgexpu_cuda.so, the B200 (sm_100a) implementation of
+ * EdgeXPU-LLM's quantized matrix-product path.
+ *
+ * Plain C types only (no CUDA or torch types): pointers, sizes, and `void *stream` (a
+ * cudaStream_t, or NULL for the library's own stream).  Every entry point returns 1 on
+ * success and 0 on failure; failures also leave a message in `error` (when given) and in
+ * edgexpu_cuda_last_error().  There is no CPU fallback: without a CUDA device every call
+ * fails.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   edgexpu_cuda_linear_quant_batch   edgexpu_cpu_linear_quant_batch   include/edgexpu/cpu_kernel.h:71-80
+ *                                     (and edgexpu_cpu_linear_quant    include/edgexpu/cpu_kernel.h:60-68)
+ *   edgexpu_cuda_quantize_q8_0        edgexpu_gguf_quantize_q8_0       include/edgexpu/gguf_quant.h:80-81
+ *   edgexpu_cuda_quantize_q8_k        edgexpu_gguf_quantize_q8_k       include/edgexpu/gguf_quant.h:85-86
+ *   edgexpu_cuda_logits_argmax        greedy branch of sample_next_token src/native.c:2355-2400
+ *                                     (chunk loop + logit_score src/native.c:500-514)
+ *   edgexpu_cuda_upload_weight        per-token staging of load_qweight src/native.c:593-655,
+ *                                     stage_copy_bytes src/native.c:350-380 (uploaded once instead)
+ *
+ * Weight handles: edgexpu_cuda_upload_weight returns a device address (typed const uint8_t *)
+ * that callers keep in edgexpu_qweight.data (include/edgexpu/native.h:23-28) in place of the
+ * staging pointer.  Any row of a registered tensor may be passed as `weight` (e.g. a vocab
+ * chunk or a tensor-parallel shard), with n_out rows from there.
+ *
+ * Threading: one device per process; calls are serialised internally.  Host-buffer calls are
+ * synchronous; *_dev calls are ordered on `stream` and do not synchronise the host.
+ */
+#ifndef EDGEXPU_CUDA_H
+#define EDGEXPU_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EDGEXPU_CUDA_ABI_VERSION 1
+
+/* GGUF type ids, as EDGEXPU_GGUF_TYPE_* in include/edgexpu/gguf_quant.h:140-147. */
+#define EDGEXPU_CUDA_TYPE_Q8_0 8u
+#define EDGEXPU_CUDA_TYPE_Q4_K 12u
+
+int edgexpu_cuda_abi_version(void);
+
+/* Bind the library to CUDA device `device` (creates its stream and scratch). */
+int edgexpu_cuda_init(int device, char *error, size_t error_size);
+/* Free every uploaded weight and all scratch; the library can be initialised again. */
+int edgexpu_cuda_shutdown(void);
+/* Last failure message of this process ("" if none). */
+const char *edgexpu_cuda_last_error(void);
+
+/* Copy a packed GGUF tensor (n_out rows of n_in elements, native block layout) to HBM once and
+ * return its device handle.  Replaces the per-layer, per-token staging memcpy. */
+int edgexpu_cuda_upload_weight(const uint8_t *host, size_t nbytes, uint32_t type, int n_out, int n_in,
+                               const uint8_t **handle, char *error, size_t error_size);
+/* Register device memory the caller already holds (16-byte aligned, with at least 16 readable
+ * bytes past the last row) so it can be passed as `weight`. */
+int edgexpu_cuda_register_weight(const void *device_ptr, size_t capacity, uint32_t type, int n_out, int n_in,
+                                 char *error, size_t error_size);
+/* Forget a handle; frees the memory if it came from edgexpu_cuda_upload_weight. */
+int edgexpu_cuda_free_weight(const void *handle);
+
+/* ---- host-buffer entry points (synchronous) ---------------------------------------------- */
+
+/* fp32[n] -> Q8_0 blocks (n/32 * 34 bytes), bytes identical to the reference x86 build. */
+int edgexpu_cuda_quantize_q8_0(const float *x, int n, uint8_t *dst, char *error, size_t error_size);
+/* fp32[n] -> Q8_K blocks (n/256 * 292 bytes), bytes identical to the reference. */
+int edgexpu_cuda_quantize_q8_k(const float *x, int n, uint8_t *dst, char *error, size_t error_size);
+
+/* out[t*n_out + o] = bias[o] + dot(W_o, quantize(x_t)) for t < m, o < n_out; x is [m][n_in]
+ * row-major, out is [m][n_out]; bias may be NULL.  Q8_0 weights use Q8_0 activations, Q4_K
+ * weights use Q8_K activations (cpu_kernel.c:577-631). */
+int edgexpu_cuda_linear_quant_batch(float *out, const float *x, const uint8_t *weight, uint32_t type,
+                                    const float *bias, int m, int n_out, int n_in, char *error,
+                                    size_t error_size);
+
+/* Greedy next token: argmax over rows i < vocab of dot(W_i, hidden) + bias[i], lowest id on
+ * ties.  Q8_0 weights see a Q8_0-quantized hidden state, Q4_K weights the fp32 hidden state
+ * (native.c:2317-2319, :445-481).  best_score may be NULL. */
+int edgexpu_cuda_logits_argmax(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
+                               const float *bias, uint32_t *token_id, float *best_score, char *error,
+                               size_t error_size);
+
+/* ---- device-buffer entry points (ordered on `stream`, no host synchronisation) ----------- */
+
+/* Quantize m rows of n fp32 values into the activation format used with `weight_type`. */
+int edgexpu_cuda_quantize_dev(uint32_t weight_type, const float *x, int m, int n, uint8_t *dst, void *stream);
+
+int edgexpu_cuda_linear_quant_batch_dev(float *out, const float *x, const uint8_t *weight, uint32_t type,
+                                        const float *bias, int m, int n_out, int n_in, void *stream);
+
+/* Writes the argmax key of rows [0, vocab) of `weight` into *key (device).  The key packs the
+ * order-preserving bits of the best score (high word) and 0xFFFFFFFF - (row0 + row) (low
+ * word), so max over keys from several vocab shards is the global greedy choice. */
+int edgexpu_cuda_logits_argmax_dev(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
+                                   const float *bias, int64_t row0, uint64_t *key, void *stream);
+
+/* Test hook: per-block int32 partials of the production kernel.  xq holds m pre-quantized
+ * activation rows.  Q8_0: partials[t][o][b] = ip.  Q4_K: partials[t][o][b][2] = (sumi, summ). */
+int edgexpu_cuda_block_partials_dev(int32_t *partials, const uint8_t *xq, const uint8_t *weight, uint32_t type,
+                                    int m, int n_out, int n_in, void *stream);
+
+/* Make sure scratch for m activation rows of n_in elements exists (call before graph capture). */
+int edgexpu_cuda_reserve(int m, int n_in, char *error, size_t error_size);
+
+/* Wait for `stream`, then report any device-side timeout recorded by the kernels. */
+int edgexpu_cuda_stream_sync(void *stream, char *error, size_t error_size);
+
+/* Token id encoded in an argmax key (0 when no row had a finite score). */
+static inline uint32_t edgexpu_cuda_argmax_key_id(uint64_t key) {
+    return key == 0 ? 0u : 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
+}
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif
