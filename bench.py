@@ -1,0 +1,717 @@
+#!/usr/bin/env python3
+"""Throughput of EdgeXPU-LLM's quantized matrix-product hot path on B200.
+
+Metric: Q4_K / Q8_0 GEMV HBM GB/s -- algorithmic bytes (packed weights plus
+activations in, quantized activations, outputs) per second, whole job.
+
+Workloads (``--workload``):
+
+* ``llama3_8b_q4k_decode`` (default): one step = every quantized matrix product of one
+  Llama-3-8B-shaped decode token at batch ``--batch`` (default 1) -- 32 layers x {q 4096x4096,
+  k 1024x4096, v 1024x4096, o 4096x4096, gate 14336x4096, up 14336x4096, down 4096x14336} plus
+  the greedy logits over output.weight 128256x4096 with the fp32 hidden state (native.c:2355-2397).
+  These are configuration 2's GEMV shapes in configuration 4's per-token arrangement:
+  4,221,370,368 bytes of random-init Q4_K weights resident in HBM (far larger than L2, so no
+  flush is needed between steps).  Each projection quantizes its activation (Q8_K) first.
+  With N > 1 GPUs the path is tensor-parallel: q/k/v/gate/up and the logits shard by rows,
+  o/down by input columns, followed by an NCCL fp32 all-reduce; the greedy token is an NCCL
+  max-reduction of packed (score, id) keys.  Total work is fixed, so scaling is "strong".
+* ``smollm2_q8_0_decode``: configuration 1's weight stream (30 layers of SmolLM2-135M-shaped
+  Q8_0 projections + the tied 49152x576 Q8_0 logits), replicas only at N > 1.
+
+Arms: ``--impl ours`` (default) times the CUDA path; ``--impl reference`` times the reference's
+own CPU implementation (oracle/_ref, compiled from the reference sources) on this host's cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import importlib.util
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+PKG_DIR = ROOT / "edgexpu-llm_b200"
+REF_LIB = ROOT / "oracle" / "_ref" / "libedgexpu_ref_avx2.so"
+REF_DRIVER = ROOT / "oracle" / "_ref" / "libedgexpu_ref_driver.so"
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+TRAFFIC = ROOT / "profiles" / "traffic.json"
+
+TYPE_Q8_0, TYPE_Q4_K = 8, 12
+FALLBACK_HBM_GBS = 6650.0
+
+WORKLOADS = {
+    "llama3_8b_q4k_decode": {
+        "type": TYPE_Q4_K, "layers": 32, "hidden": 4096,
+        "proj": [("attn_q", 4096, 4096, "row"), ("attn_k", 1024, 4096, "row"), ("attn_v", 1024, 4096, "row"),
+                 ("attn_output", 4096, 4096, "col"), ("ffn_gate", 14336, 4096, "row"),
+                 ("ffn_up", 14336, 4096, "row"), ("ffn_down", 4096, 14336, "col")],
+        "vocab": 128256, "tp": True,
+    },
+    "smollm2_q8_0_decode": {
+        "type": TYPE_Q8_0, "layers": 30, "hidden": 576,
+        "proj": [("attn_q", 576, 576, "row"), ("attn_k", 192, 576, "row"), ("attn_v", 192, 576, "row"),
+                 ("attn_output", 576, 576, "row"), ("ffn_gate", 1536, 576, "row"), ("ffn_up", 1536, 576, "row"),
+                 ("ffn_down", 576, 1536, "row")],
+        "vocab": 49152, "tp": False,
+    },
+}
+
+
+def load_pkg():
+    name = "edgexpu_llm_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, PKG_DIR / "__init__.py", submodule_search_locations=[str(PKG_DIR)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def row_bytes(t, n):
+    return n // 32 * 34 if t == TYPE_Q8_0 else n // 256 * 144
+
+
+def act_bytes(t, n):
+    return n // 32 * 34 if t == TYPE_Q8_0 else n // 256 * 292
+
+
+def linear_alg_bytes(t, n_out, n_in, m):
+    """W + b * (4K in + quantized activation + 4N out)."""
+    return n_out * row_bytes(t, n_in) + m * (4 * n_in + act_bytes(t, n_in) + 4 * n_out)
+
+
+def logits_alg_bytes(t, vocab, n_embd):
+    extra = act_bytes(t, n_embd) if t == TYPE_Q8_0 else 0
+    return vocab * row_bytes(t, n_embd) + 4 * n_embd + extra + 8
+
+
+def shard_shapes(wl, world, rank):
+    """Per-rank (label, n_out, n_in, kind) of one layer, plus the vocab rows [v0, v0+nv)."""
+    out = []
+    for label, n_out, n_in, kind in wl["proj"]:
+        if world > 1 and wl["tp"]:
+            if kind == "row":
+                out.append((label, n_out // world, n_in, kind))
+            else:
+                out.append((label, n_out, n_in // world, kind))
+        else:
+            out.append((label, n_out, n_in, kind))
+    nv = wl["vocab"] // world if (world > 1 and wl["tp"]) else wl["vocab"]
+    return out, rank * nv if (world > 1 and wl["tp"]) else 0, nv
+
+
+def step_bytes(wl, m):
+    """Algorithmic bytes of one full (unsharded) step."""
+    t = wl["type"]
+    per_layer = sum(linear_alg_bytes(t, n_out, n_in, m) for _, n_out, n_in, _ in wl["proj"])
+    return wl["layers"] * per_layer + m * logits_alg_bytes(t, wl["vocab"], wl["hidden"])
+
+
+# ---- clocks -------------------------------------------------------------------------------------
+
+CLOCK_FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                "clocks_event_reasons.sw_power_cap")
+REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, index: int):
+        self.cmd = ["nvidia-smi", f"--id={index}", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                    "-lms", "100"]
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self, t0: float, t1: float):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        self.proc.terminate()
+        out = self.proc.communicate(timeout=10)[0]
+        sms, maxes, reasons = [], [], set()
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                sm, mx = float(f[1]), float(f[2])
+            except ValueError:
+                continue
+            if not (t0 <= ts <= t1):
+                continue
+            sms.append(sm)
+            maxes.append(mx)
+            for name, val in zip(REASONS, f[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ---- distributed plumbing -----------------------------------------------------------------------
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def peak_hbm():
+    try:
+        return float(json.loads(PEAKS.read_text())["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---- the reference's CPU implementation (baseline arm) ------------------------------------------
+
+
+class RefCPU:
+    def __init__(self):
+        if not (REF_LIB.exists() and REF_DRIVER.exists()):
+            raise FileNotFoundError("oracle/_ref not built")
+        self.lib = ctypes.CDLL(str(REF_LIB))
+        self.drv = ctypes.CDLL(str(REF_DRIVER))
+        vp, i, u = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32
+        self.lib.edgexpu_cpu_linear_quant_batch.argtypes = [vp, vp, vp, u, vp, i, i, i]
+        self.lib.edgexpu_cpu_linear_quant_batch.restype = None
+        self.drv.eoref_logits_greedy.argtypes = [vp, u, vp, i, i, vp, ctypes.POINTER(u), ctypes.POINTER(ctypes.c_float)]
+        self.drv.eoref_logits_greedy.restype = i
+
+    def linear(self, out, x, w, t, m, n_out, n_in):
+        self.lib.edgexpu_cpu_linear_quant_batch(out.ctypes.data, x.ctypes.data, w.ctypes.data, t, None, m, n_out, n_in)
+
+    def logits(self, w, t, h, n_embd, vocab):
+        tok = ctypes.c_uint32()
+        sc = ctypes.c_float()
+        assert self.drv.eoref_logits_greedy(w.ctypes.data, t, h.ctypes.data, n_embd, vocab, None, ctypes.byref(tok),
+                                            ctypes.byref(sc)) == 1
+        return tok.value
+
+
+def host_weight(rng, t, n_out, n_in):
+    import numpy as np
+
+    rb = row_bytes(t, n_in)
+    w = np.frombuffer(rng.bytes(n_out * rb), np.uint8).reshape(n_out, rb).copy()
+    if t == TYPE_Q8_0:
+        blk = w.reshape(n_out, -1, 34)
+        blk[..., 0:2] = rng.uniform(1e-4, 2e-3, blk.shape[:2]).astype(np.float16).view(np.uint8).reshape(blk.shape[:2] + (2,))
+        qs = blk[..., 2:].view(np.int8)
+        qs[qs == -128] = -127
+    else:
+        blk = w.reshape(n_out, -1, 144)
+        blk[..., 0:4] = rng.uniform(1e-4, 1e-3, blk.shape[:2] + (2,)).astype(np.float16).view(np.uint8).reshape(blk.shape[:2] + (4,))
+    return w
+
+
+class CpuWorkload:
+    """The workload (or a whole-layer sample of it) in host memory, run by the reference's CPU code."""
+
+    def __init__(self, wl, m, layers, vocab_rows):
+        import numpy as np
+
+        self.ref = RefCPU()
+        rng = np.random.default_rng(0)
+        self.wl, self.m, self.t = wl, m, wl["type"]
+        self.weights = [(host_weight(rng, self.t, n_out, n_in), n_out, n_in)
+                        for _ in range(layers) for _, n_out, n_in, _k in wl["proj"]]
+        self.vocab_rows = vocab_rows
+        self.lw = host_weight(rng, self.t, vocab_rows, wl["hidden"])
+        self.xs = {n_in: rng.standard_normal((m, n_in)).astype(np.float32) for _, _, n_in, _ in wl["proj"]}
+        self.outs = {n_out: np.empty((m, n_out), np.float32) for _, n_out, _, _ in wl["proj"]}
+        self.h = rng.standard_normal(wl["hidden"]).astype(np.float32)
+        self.nbytes = (sum(linear_alg_bytes(self.t, n_out, n_in, m) for _, n_out, n_in in self.weights)
+                       + m * logits_alg_bytes(self.t, vocab_rows, wl["hidden"]))
+        self.threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+
+    def step(self):
+        for w, n_out, n_in in self.weights:
+            self.ref.linear(self.outs[n_out], self.xs[n_in], w, self.t, self.m, n_out, n_in)
+        for _ in range(self.m):
+            self.ref.logits(self.lw, self.t, self.h, self.wl["hidden"], self.vocab_rows)
+
+
+def cpu_run(wl, m, layers, vocab_rows, min_seconds, min_reps):
+    """Reference CPU GB/s on a sample, median over reps lasting >= min_seconds in total."""
+    w = CpuWorkload(wl, m, layers, vocab_rows)
+    w.step()  # the first call runs the reference's OpenMP thread probe (cpu_kernel.c:28-177)
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < min_reps or time.perf_counter() - t_start < min_seconds:
+        t0 = time.perf_counter()
+        w.step()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return w.nbytes / sec / 1e9, sec, w.nbytes, w.threads
+
+
+def run_reference(args, wl):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    m = args.batch
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    layers = args.ref_layers or wl["layers"]
+    vocab_rows = wl["vocab"] * layers // wl["layers"]
+    try:
+        w = CpuWorkload(wl, m, layers, vocab_rows)
+    except FileNotFoundError as e:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU build missing: {e}"}))
+        return
+    for _ in range(max(1, args.warmup)):  # the first one also runs the reference's thread probe
+        w.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        w.step()
+    sec = (time.perf_counter() - t0) / args.steps
+    gbs = w.nbytes / sec / 1e9
+    sample = (f"{'all' if layers == wl['layers'] else layers} of {wl['layers']} layers + {vocab_rows} of "
+              f"{wl['vocab']} logits rows per step ({w.nbytes} algorithmic bytes), reference AVX2 build with OpenMP")
+    line = {
+        "metric": f"{'Q4_K' if wl['type'] == TYPE_Q4_K else 'Q8_0'} GEMV HBM GB/s ({args.workload}, batch {m})",
+        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong" if wl["tp"] else "weak", "vs_baseline": None,
+        "dtype": "u4/i8 x i8 -> i32 -> f32" if wl["type"] == TYPE_Q4_K else "i8 x i8 -> i32 -> f32",
+        "data": "synthetic (seeded random-init GGUF blocks)", "impl": "reference",
+        "config": {"workload": args.workload, "batch": m, "parallelism": f"cpu ({w.threads} threads)"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": w.threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- our CUDA path ------------------------------------------------------------------------------
+
+
+def run_ours(args, wl):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    pkg = load_pkg()
+    from edgexpu_llm_b200 import synth
+
+    cuda = pkg.load_cuda()
+    host = pkg.load_host()
+    pkg.init(local)
+    dev = torch.device("cuda", local)
+    t = wl["type"]
+    m = args.batch
+    tp = world > 1 and wl["tp"]
+    shapes, v0, nv = shard_shapes(wl, world, rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+
+    # Weights: generated in HBM with the seeded recipe and registered with the library.
+    layers = []
+    for _ in range(wl["layers"]):
+        lay = []
+        for label, n_out, n_in, kind in shapes:
+            buf = synth.torch_weight(t, n_out, n_in, gen, dev)
+            h = pkg.register_weight(buf, t, n_out, n_in)
+            lay.append((label, n_out, n_in, kind, buf, h))
+        layers.append(lay)
+    lbuf = synth.torch_weight(t, nv, wl["hidden"], gen, dev)
+    lh = pkg.register_weight(lbuf, t, nv, wl["hidden"])
+
+    # Activations / outputs (fixed random inputs; in the model these come from the host layer ops).
+    ins = {}
+    for _, n_out, n_in, _k in shapes:
+        if n_in not in ins:
+            ins[n_in] = torch.randn((m, n_in), generator=gen, device=dev, dtype=torch.float32)
+    outs = {label: torch.empty((m, n_out), device=dev, dtype=torch.float32) for label, n_out, _, _ in shapes}
+    hidden = torch.randn(wl["hidden"], generator=gen, device=dev, dtype=torch.float32)
+    keys = torch.zeros(max(1, m), device=dev, dtype=torch.int64)
+    sign = torch.tensor(-(2 ** 63), device=dev, dtype=torch.int64)
+    buf = ctypes.create_string_buffer(512)
+    for n_in in ins:
+        assert cuda.edgexpu_cuda_reserve(m, n_in, buf, 512), buf.value
+
+    def enqueue_step():
+        st = torch.cuda.current_stream().cuda_stream
+        for lay in layers:
+            for label, n_out, n_in, kind, _b, h in lay:
+                o = outs[label]
+                ok = cuda.edgexpu_cuda_linear_quant_batch_dev(o.data_ptr(), ins[n_in].data_ptr(), h, t, None, m, n_out,
+                                                              n_in, st)
+                if not ok:
+                    raise RuntimeError(cuda.edgexpu_cuda_last_error().decode())
+                if tp and kind == "col":
+                    dist.all_reduce(o)
+        for i in range(m):
+            if not cuda.edgexpu_cuda_logits_argmax_dev(lh, t, hidden.data_ptr(), wl["hidden"], nv, None, v0,
+                                                       keys[i:].data_ptr(), st):
+                raise RuntimeError(cuda.edgexpu_cuda_last_error().decode())
+        if tp:
+            keys.bitwise_xor_(sign)  # uint64 order -> int64 order for the max-reduction
+            dist.all_reduce(keys, op=dist.ReduceOp.MAX)
+            keys.bitwise_xor_(sign)
+
+    # Eager warm-up (sizes scratch, sets kernel attributes), then capture one step in a graph.
+    enqueue_step()
+    torch.cuda.synchronize()
+    graph = None
+    cap_stream = torch.cuda.Stream(device=dev)
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap_stream):
+            enqueue_step()
+        torch.cuda.synchronize()
+    except Exception as e:  # noqa: BLE001 -- fall back to eager launches, reported in config
+        graph = None
+        print(f"[bench] graph capture failed ({e}); timing eager launches", file=sys.stderr)
+        torch.cuda.synchronize()
+
+    def one_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            enqueue_step()
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_load0 = time.time()
+    ev0.record()
+    for _ in range(args.steps):
+        one_step()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        dist.barrier()
+    # Keep the same load running (untimed) until clocks have been sampled for >= 2 s.
+    extended = False
+    while time.time() - t_load0 < 2.0:
+        extended = True
+        for _ in range(max(1, args.steps)):
+            one_step()
+        torch.cuda.synchronize()
+    t_load1 = time.time()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop(t_load0, t_load1)
+    clocks["window"] = ("timed region extended by identical untimed steps to 2 s of sampling"
+                        if extended else "timed region")
+
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    total_bytes = step_bytes(wl, m) * (1 if tp else world)
+    value_gbs = total_bytes * args.steps / (ms_max / 1e3) / 1e9
+
+    # Roofline of the dominant kernel (the row-stream GEMV): time each launch of one step's
+    # projections with events on the launching stream, activations pre-quantized.
+    st = torch.cuda.current_stream().cuda_stream
+    xq = {n_in: torch.empty(m * act_bytes(t, n_in) + 64, dtype=torch.uint8, device=dev) for n_in in ins}
+    for n_in in ins:
+        assert cuda.edgexpu_cuda_quantize_dev(t, ins[n_in].data_ptr(), m, n_in, xq[n_in].data_ptr(), st)
+    evs = []
+    launch_bytes = []
+    torch.cuda.synchronize()
+    torch.cuda._sleep(200_000_000)  # ~0.1 s spin: every launch below is queued before the GPU reaches it
+    for lay in layers:
+        for label, n_out, n_in, kind, _b, h in lay:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            assert cuda.edgexpu_cuda_dot_quant_q8_dev(outs[label].data_ptr(), xq[n_in].data_ptr(), h, t, None, m,
+                                                      n_out, n_in, st)
+            b.record()
+            evs.append((a, b))
+            launch_bytes.append(n_out * row_bytes(t, n_in) + m * (act_bytes(t, n_in) + 4 * n_out))
+    torch.cuda.synchronize()
+    kern_ms = [a.elapsed_time(b) for a, b in evs]
+    achieved = sum(launch_bytes) / (sum(kern_ms) / 1e3) / 1e9
+    peak, peak_kind = peak_hbm()
+    traffic = None
+    try:
+        tr = json.loads(TRAFFIC.read_text())
+        traffic = tr.get(args.workload, {}).get(str(world))
+    except (OSError, ValueError):
+        pass
+
+    # End to end through the reference-named host shim: host buffers, H2D/D2H inside the timed region.
+    hx = {n_in: ins[n_in].cpu().numpy() for n_in in ins}
+    hout = {label: np.empty((m, n_out), np.float32) for label, n_out, _, _ in shapes}
+    hh = hidden.cpu().numpy()
+    tok = ctypes.c_uint32()
+    h2d = d2h = 0
+    for _, n_out, n_in, kind in shapes:
+        h2d += 4 * m * n_in * wl["layers"]
+        d2h += (4 * m * n_out + 4) * wl["layers"]
+        if tp and kind == "col":
+            h2d += 4 * m * n_out * wl["layers"]
+            d2h += 4 * m * n_out * wl["layers"]
+    h2d += 4 * wl["hidden"] * m
+    d2h += 12 * m
+    red = {label: torch.empty((m, n_out), device=dev, dtype=torch.float32) for label, n_out, _, k in shapes if k == "col"}
+
+    def e2e_step():
+        for lay in layers:
+            for label, n_out, n_in, kind, _b, h in lay:
+                o = hout[label]
+                host.edgexpu_cpu_linear_quant_batch(o.ctypes.data, hx[n_in].ctypes.data, h, t, None, m, n_out, n_in)
+                if tp and kind == "col":
+                    r = red[label]
+                    r.copy_(torch.from_numpy(o))
+                    dist.all_reduce(r)
+                    o[...] = r.cpu().numpy()
+        for _ in range(m):
+            ok = host.edgexpu_b200_logits_greedy(lh, t, hh.ctypes.data, wl["hidden"], nv, None, ctypes.byref(tok),
+                                                 buf, 512)
+            if not ok:
+                raise RuntimeError(buf.value.decode())
+        err = host.edgexpu_b200_last_error()
+        if err:
+            raise RuntimeError(err.decode())
+
+    host.edgexpu_b200_clear_error()
+    for _ in range(max(1, min(args.warmup, 3))):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    e_steps = max(1, min(args.steps, 10))
+    t0 = time.perf_counter()
+    for _ in range(e_steps):
+        e2e_step()
+    e2e_s = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    e2e_gbs = total_bytes * e_steps / float(e2e_s.item()) / 1e9
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cl = max(1, wl["layers"] // 8)
+            gbs_cpu, sec_cpu, nb_cpu, threads = cpu_run(wl, m, cl, wl["vocab"] * cl // wl["layers"], 10.0, 3)
+            cpu_baseline = {"value": round(gbs_cpu, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                            "sample": f"{cl} of {wl['layers']} layers + {wl['vocab'] * cl // wl['layers']} logits rows "
+                                      f"({nb_cpu} bytes) per rep, median of reps over >= 10 s, reference AVX2 build "
+                                      f"(oracle/_ref) with OpenMP"}
+        except FileNotFoundError as e:
+            cpu_baseline = {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+
+    launches_per_step = wl["layers"] * len(shapes) * 2 + m * (2 if t == TYPE_Q8_0 else 1)
+    line = {
+        "metric": f"{'Q4_K' if t == TYPE_Q4_K else 'Q8_0'} GEMV HBM GB/s ({args.workload}, batch {m})",
+        "value": round(value_gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "dtype": "u4/i8 x i8 -> i32 -> f32" if t == TYPE_Q4_K else "i8 x i8 -> i32 -> f32",
+        "data": "synthetic (seeded random-init GGUF blocks generated in HBM)",
+        "config": {"workload": args.workload, "batch": m,
+                   "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
+                   "bytes_per_step": total_bytes, "l2": "inputs larger than L2 (weights streamed once per step)",
+                   "graph": graph is not None, "tokens_per_s_gemv_only": round(args.steps / (ms_max / 1e3) * m, 2)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "rowstream GEMV (Q4_K x Q8_K)" if t == TYPE_Q4_K else "rowstream GEMV (Q8_0 x Q8_0)",
+                     "launches": len(kern_ms), "peak_source": f"{peak_kind} hbm_gbs"},
+        "cpu_baseline": cpu_baseline,
+        "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "edgexpu_cpu_linear_quant_batch + edgexpu_b200_logits_greedy (host buffers)"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    graph = None
+    torch.cuda.synchronize()
+    pkg.shutdown()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_gemv(args):
+    """Configurations 0 and 2: one GEMV per step (activation quantization included) over the
+    next of `copies` weight copies, so the weights streamed per step always come from HBM."""
+    import math
+
+    import numpy as np
+    import torch
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    pkg = load_pkg()
+    from edgexpu_llm_b200 import synth
+
+    cuda, host = pkg.load_cuda(), pkg.load_host()
+    pkg.init(local)
+    dev = torch.device("cuda", local)
+    t = TYPE_Q4_K if args.wtype == "q4_k" else TYPE_Q8_0
+    n_out, n_in = (int(v) for v in args.shape.split(","))
+    m = args.batch
+    wb = n_out * row_bytes(t, n_in)
+    copies = max(2, math.ceil(args.rotate_bytes / wb))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7 + rank)
+    wbuf = synth.torch_weight(t, n_out * copies, n_in, gen, dev)
+    h0 = pkg.register_weight(wbuf, t, n_out * copies, n_in)
+    x = torch.randn((m, n_in), generator=gen, device=dev, dtype=torch.float32)
+    out = torch.empty((m, n_out), device=dev, dtype=torch.float32)
+    buf = ctypes.create_string_buffer(512)
+    assert cuda.edgexpu_cuda_reserve(m, n_in, buf, 512), buf.value
+
+    def enqueue(k0, k):
+        st = torch.cuda.current_stream().cuda_stream
+        for i in range(k0, k0 + k):
+            if not cuda.edgexpu_cuda_linear_quant_batch_dev(out.data_ptr(), x.data_ptr(), h0 + (i % copies) * wb, t,
+                                                            None, m, n_out, n_in, st):
+                raise RuntimeError(cuda.edgexpu_cuda_last_error().decode())
+
+    enqueue(0, 1)
+    torch.cuda.synchronize()
+    cap = torch.cuda.Stream(device=dev)
+    g_warm, g_timed = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_warm, stream=cap):
+        enqueue(0, max(1, args.warmup))
+    with torch.cuda.graph(g_timed, stream=cap):
+        enqueue(max(1, args.warmup), args.steps)
+    g_warm.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_load0 = time.time()
+    ev0.record()
+    g_timed.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    extended = False
+    while time.time() - t_load0 < 2.0:
+        extended = True
+        g_timed.replay()
+        torch.cuda.synchronize()
+    clocks = sampler.stop(t_load0, time.time())
+    clocks["window"] = ("timed region extended by identical untimed steps to 2 s of sampling"
+                        if extended else "timed region")
+    nbytes = linear_alg_bytes(t, n_out, n_in, m)
+    value = nbytes * args.steps / (ms / 1e3) / 1e9
+
+    # GEMV kernel alone (activations pre-quantized), one event pair per launch.
+    st = torch.cuda.current_stream().cuda_stream
+    xq = torch.empty(m * act_bytes(t, n_in) + 64, dtype=torch.uint8, device=dev)
+    assert cuda.edgexpu_cuda_quantize_dev(t, x.data_ptr(), m, n_in, xq.data_ptr(), st)
+    torch.cuda.synchronize()
+    torch.cuda._sleep(200_000_000)
+    evs = []
+    for i in range(min(copies, 64)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        assert cuda.edgexpu_cuda_dot_quant_q8_dev(out.data_ptr(), xq.data_ptr(), h0 + i * wb, t, None, m, n_out, n_in, st)
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    kbytes = wb + m * (act_bytes(t, n_in) + 4 * n_out)
+    achieved = kbytes / (kern_ms / 1e3) / 1e9
+    peak, peak_kind = peak_hbm()
+
+    # End to end through the reference-named host shim.
+    hx = x.cpu().numpy()
+    hout = np.empty((m, n_out), np.float32)
+    host.edgexpu_b200_clear_error()
+
+    def e2e(i):
+        host.edgexpu_cpu_linear_quant_batch(hout.ctypes.data, hx.ctypes.data, h0 + (i % copies) * wb, t, None, m, n_out,
+                                            n_in)
+
+    for i in range(3):
+        e2e(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e2e(i)
+    e2e_s = time.perf_counter() - t0
+    err = host.edgexpu_b200_last_error()
+    if err:
+        raise RuntimeError(err.decode())
+    line = {
+        "metric": f"{'Q4_K' if t == TYPE_Q4_K else 'Q8_0'} GEMV HBM GB/s ({n_out}x{n_in}, batch {m})",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u4/i8 x i8 -> i32 -> f32" if t == TYPE_Q4_K else "i8 x i8 -> i32 -> f32",
+        "data": "synthetic (seeded random-init GGUF blocks generated in HBM)",
+        "config": {"workload": "gemv", "type": args.wtype, "n_out": n_out, "n_in": n_in, "batch": m,
+                   "weight_copies": copies, "l2": f"rotating {copies} weight copies ({copies * wb} bytes) > L2",
+                   "parallelism": "single"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "kernel_us": round(kern_ms * 1e3, 3),
+                     "peak_source": f"{peak_kind} hbm_gbs"},
+        "cpu_baseline": None,
+        "e2e": {"value": round(nbytes * args.steps / e2e_s / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": 4 * m * n_in, "d2h_bytes_per_step": 4 * m * n_out + 4,
+                "path": "edgexpu_cpu_linear_quant_batch (host buffers)"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    del g_warm, g_timed
+    torch.cuda.synchronize()
+    pkg.shutdown()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gemv"], default="llama3_8b_q4k_decode")
+    ap.add_argument("--wtype", choices=["q4_k", "q8_0"], default="q4_k", help="gemv workload: weight type")
+    ap.add_argument("--shape", default="14336,4096", help="gemv workload: n_out,n_in")
+    ap.add_argument("--rotate-bytes", type=float, default=512e6, help="gemv workload: total bytes of weight copies")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ref-layers", type=int, default=0, help="reference arm: layers per step (0 = all)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.workload == "gemv":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the gemv workload has no reference arm; "
+                                                                  "use the decode workloads"}))
+            return
+        run_gemv(args)
+        return
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()

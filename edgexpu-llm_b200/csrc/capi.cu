@@ -82,7 +82,9 @@ size_t act_row_bytes_of(uint32_t type, int n) {
   return static_cast<size_t>(n / ex::QK_K) * ex::Q8_K_BYTES;
 }
 
-cudaStream_t pick(void* stream) { return stream != nullptr ? static_cast<cudaStream_t>(stream) : g.stream; }
+// NULL selects the CUDA default stream (the convention of every CUDA API, and the handle torch
+// reports for its default stream); the library's own stream only serves the synchronous calls.
+cudaStream_t pick(void* stream) { return static_cast<cudaStream_t>(stream); }
 
 int need_ready(char* error, size_t error_size) {
   if (!g.ready) return fail(error, error_size, "edgexpu_cuda_init has not been called");
@@ -146,19 +148,15 @@ int lookup(const uint8_t* weight, uint32_t type, int n_out, int n_in, char* erro
   return 1;
 }
 
-int run_linear_dev(float* out, const float* x, const uint8_t* weight, uint32_t type, const float* bias, int m,
-                   int n_out, int n_in, cudaStream_t st, char* error, size_t error_size) {
-  if (out == nullptr || x == nullptr || weight == nullptr || m <= 0 || n_out <= 0 || n_in <= 0)
-    return fail(error, error_size, "invalid arguments");
-  if (!lookup(weight, type, n_out, n_in, error, error_size)) return 0;
+// One row-stream launch per chunk of <= max_m activation rows.  act is either fp32 rows [m][n_in]
+// (act_f32: the kernel quantizes them) or pre-quantized GGUF rows [m][act_row_bytes].
+int run_rows_dev(float* out, const void* act, bool act_f32, const uint8_t* weight, uint32_t type, const float* bias,
+                 int m, int n_out, int n_in, cudaStream_t st, char* error, size_t error_size) {
   const size_t qb = act_row_bytes_of(type, n_in);
-  if (!grow_dev(g.xq, static_cast<size_t>(m) * qb + 64, st, error, error_size)) return 0;
-  uint8_t* xq = static_cast<uint8_t*>(g.xq.p);
+  const size_t stride = act_f32 ? static_cast<size_t>(n_in) * 4 : qb;
   const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
   const int max_m = ex::rowstream_max_m(fmt, n_in, g.info);
   if (max_m <= 0) return fail(error, error_size, "n_in %d too large for the shared-memory activation tile", n_in);
-  EX_CUDA(type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n_in, xq, st) : ex::launch_quantize_q8_k(x, m, n_in, xq, st),
-          error, error_size);
   for (int t0 = 0; t0 < m; t0 += max_m) {
     ex::RowStreamArgs a{};
     a.fmt = fmt;
@@ -169,8 +167,9 @@ int run_linear_dev(float* out, const float* x, const uint8_t* weight, uint32_t t
     a.row_bytes = static_cast<int>(row_bytes_of(type, n_in));
     a.K = n_in;
     a.m = std::min(max_m, m - t0);
-    a.act = xq + static_cast<size_t>(t0) * qb;
+    a.act = static_cast<const uint8_t*>(act) + static_cast<size_t>(t0) * stride;
     a.act_row_bytes = static_cast<int>(qb);
+    a.act_f32 = act_f32;
     a.bias = bias;
     a.out = out + static_cast<size_t>(t0) * n_out;
     a.out_stride = n_out;
@@ -178,6 +177,24 @@ int run_linear_dev(float* out, const float* x, const uint8_t* weight, uint32_t t
     EX_CUDA(ex::launch_rowstream(a, g.info, st), error, error_size);
   }
   return 1;
+}
+
+int run_linear_dev(float* out, const float* x, const uint8_t* weight, uint32_t type, const float* bias, int m,
+                   int n_out, int n_in, cudaStream_t st, char* error, size_t error_size) {
+  if (out == nullptr || x == nullptr || weight == nullptr || m <= 0 || n_out <= 0 || n_in <= 0)
+    return fail(error, error_size, "invalid arguments");
+  if (!lookup(weight, type, n_out, n_in, error, error_size)) return 0;
+  const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  // cpu_kernel.c:577-631: every activation row is quantized once, then each weight row is dotted
+  // against every quantized row.  Small batches quantize inside the GEMV launch itself.
+  if (ex::rowstream_quantizes_itself(fmt, m))
+    return run_rows_dev(out, x, true, weight, type, bias, m, n_out, n_in, st, error, error_size);
+  const size_t qb = act_row_bytes_of(type, n_in);
+  if (!grow_dev(g.xq, static_cast<size_t>(m) * qb + 64, st, error, error_size)) return 0;
+  uint8_t* xq = static_cast<uint8_t*>(g.xq.p);
+  EX_CUDA(type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n_in, xq, st) : ex::launch_quantize_q8_k(x, m, n_in, xq, st),
+          error, error_size);
+  return run_rows_dev(out, xq, false, weight, type, bias, m, n_out, n_in, st, error, error_size);
 }
 
 int run_logits_dev(const uint8_t* weight, uint32_t type, const float* hidden, int n_embd, int vocab, const float* bias,
@@ -198,18 +215,16 @@ int run_logits_dev(const uint8_t* weight, uint32_t type, const float* hidden, in
   a.bias = bias;
   a.key = key;
   a.status = g.d_status;
+  a.act = hidden;
+  a.act_f32 = true;
   if (type == ex::TYPE_Q8_0) {
-    // native.c:2317-2319: Q8_0-class logits weights see a Q8_0-quantized hidden state.
-    const size_t qb = act_row_bytes_of(type, n_embd);
-    if (!grow_dev(g.xq, qb + 64, st, error, error_size)) return 0;
-    EX_CUDA(ex::launch_quantize_q8_0(hidden, 1, n_embd, static_cast<uint8_t*>(g.xq.p), st), error, error_size);
+    // native.c:2317-2319: Q8_0-class logits weights see a Q8_0-quantized hidden state (the
+    // kernel quantizes it in its prologue).
     a.fmt = ex::Fmt::Q8_0xQ8_0;
-    a.act = g.xq.p;
-    a.act_row_bytes = static_cast<int>(qb);
+    a.act_row_bytes = static_cast<int>(act_row_bytes_of(type, n_embd));
   } else {
     // logit_dot_row native.c:445-462 -> dot_q4_k gguf_quant.c:704-752: fp32 hidden state.
     a.fmt = ex::Fmt::Q4_KxF32;
-    a.act = hidden;
     a.act_row_bytes = n_embd * 4;
   }
   if (ex::rowstream_max_m(a.fmt, n_embd, g.info) < 1) return fail(error, error_size, "n_embd %d too large", n_embd);
@@ -451,6 +466,16 @@ int edgexpu_cuda_linear_quant_batch_dev(float* out, const float* x, const uint8_
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   if (!need_ready(nullptr, 0)) return 0;
   return run_linear_dev(out, x, weight, type, bias, m, n_out, n_in, pick(stream), nullptr, 0);
+}
+
+int edgexpu_cuda_dot_quant_q8_dev(float* out, const uint8_t* xq, const uint8_t* weight, uint32_t type, const float* bias,
+                                  int m, int n_out, int n_in, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(nullptr, 0)) return 0;
+  if (out == nullptr || xq == nullptr || weight == nullptr || m <= 0 || n_out <= 0 || n_in <= 0)
+    return fail(nullptr, 0, "invalid arguments");
+  if (!lookup(weight, type, n_out, n_in, nullptr, 0)) return 0;
+  return run_rows_dev(out, xq, false, weight, type, bias, m, n_out, n_in, pick(stream), nullptr, 0);
 }
 
 int edgexpu_cuda_logits_argmax_dev(const uint8_t* weight, uint32_t type, const float* hidden, int n_embd, int vocab,

@@ -34,8 +34,9 @@ struct RowStreamArgs {
   int row_bytes;
   int K;
   int m;                  // activation rows (tokens)
-  const void* act;        // quantized activations [m][act_row_bytes], or fp32 [m][K] for Q4_KxF32
+  const void* act;        // quantized GGUF activations [m][act_row_bytes], or fp32 [m][K] (act_f32)
   int act_row_bytes;
+  bool act_f32;           // Q8 formats: the kernel quantizes fp32 rows itself (m <= 2); Q4_KxF32: always
   const float* bias;      // [n_rows] or nullptr
   float* out;             // Store: [m][out_stride]
   long long out_stride;
@@ -51,6 +52,9 @@ struct DeviceInfo {
 
 // Largest number of activation rows one row-stream launch keeps in shared memory for this K.
 int rowstream_max_m(Fmt fmt, int K, const DeviceInfo& dev);
+
+// True when a launch with m activation rows quantizes fp32 activations in its own prologue.
+bool rowstream_quantizes_itself(Fmt fmt, int m);
 
 cudaError_t launch_rowstream(const RowStreamArgs& a, const DeviceInfo& dev, cudaStream_t st);
 

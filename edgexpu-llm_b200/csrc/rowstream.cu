@@ -7,35 +7,43 @@
 // and three epilogues: store rows (cpu_kernel.c:545-644), greedy argmax over rows
 // (native.c:2355-2397), or per-block int32 partials (test hook for bit-exactness).
 //
-// Design (HBM-bound streaming):
+// Design (HBM-bound streaming, batch 1-8):
 //   * grid = one CTA per SM (persistent); CTA c takes tiles c, c+grid, ...; a tile is R whole
-//     rows, i.e. one contiguous byte range of the row-major GGUF tensor.
+//     rows, i.e. one contiguous byte range (up to 32 KB) of the row-major GGUF tensor.
 //   * warp 0, lane 0 is the producer: it moves each tile into a ring of shared-memory stages
 //     with a 1-D TMA bulk copy (cp.async.bulk, L2 evict-first hint) that completes on the
 //     stage's "full" mbarrier.  Misaligned starts are rounded down to 16 bytes and the
-//     in-stage offset is applied by the consumers.
-//   * warps 1..8 are consumers: the quantized activations live in shared memory for the whole
-//     kernel; each (row, block) work item is one thread; integer dots use dp4a; per-block
-//     floats go to a small partials buffer and each row is summed in a fixed order
-//     (deterministic results), then stored or folded into the argmax key.
+//     in-stage offset is applied by the consumers.  The producer starts streaming weights at
+//     once; only the consumers depend on the activations.
+//   * warps 1..15 are consumers.  They first bring the activations into shared memory: for
+//     small batches they quantize the fp32 rows themselves (Q8_0 / Q8_K, same arithmetic as the
+//     standalone quantizer), otherwise they copy pre-quantized GGUF blocks.  The layout is
+//     "unit-interleaved": 16-byte chunk j of work unit u of token t sits at (t*J + j)*U + u, so
+//     the lanes of a warp, which hold consecutive units, read consecutive chunks.
+//   * rows are dealt round-robin over the consumer warps along the CTA's tile sequence; a warp
+//     computes a whole row (lane = work unit: a Q8_0 block or half a Q4_K super-block; integer
+//     dots use dp4a), sums its lanes with a fixed shuffle tree (deterministic results), stores
+//     the row or folds it into the argmax key, and releases a stage once done with its rows in
+//     it.  No CTA-wide barrier sits in the loop, so warps overlap each other's latency.
 //   * every mbarrier wait is bounded; a timeout sets a status bit, raises a CTA-wide abort
 //     flag, and the producer still waits (bounded) for its in-flight copies before exiting.
-#include <cstdio>
-
 #include "common.cuh"
 #include "launch.h"
+#include "quant.cuh"
 
 namespace ex {
 namespace {
 
-constexpr int CONSUMER_WARPS = 8;
+constexpr int CONSUMER_WARPS = 15;  // + 1 producer warp = 16 warps, 4 per SM sub-partition (128 registers each)
 constexpr int CONSUMERS = CONSUMER_WARPS * 32;
 constexpr int THREADS = CONSUMERS + 32;
-constexpr int STAGE_TARGET = 16384;
+constexpr int STAGE_TARGET = 32768;
 constexpr int MAX_STAGES = 8;
 constexpr int BAR_BYTES = 256;        // full[8], empty[8], abort flag
-constexpr int ACT_BUDGET = 100 * 1024;
+constexpr int ACT_BUDGET = 96 * 1024;
 constexpr int STAGE_SLACK = 48;       // alignment round-down (<16) + over-read of the last block
+constexpr int MAX_M = 8;              // activation rows (tokens) per launch; the host splits more
+constexpr int PROLOGUE_QUANT_MAX_M = 2;
 
 struct Layout {
   int tile_rows;
@@ -43,13 +51,34 @@ struct Layout {
   int stage_bytes;
   int n_stages;
   int act_off;
-  int part_off;
-  int part_stride;  // floats per partials buffer
   int stage_off;
   int smem_total;
 };
 
-__device__ __forceinline__ int blocks_per_row(Fmt f, int K) { return f == Fmt::Q8_0xQ8_0 ? K / QK8_0 : K / QK_K; }
+// ---- activation layout in shared memory ----------------------------------------------------------
+//   Q8_0 x Q8_0 : unit = block (U = K/32): q chunks (t*2 + j)*U + u, then d[t*U + u]
+//   Q4_K x Q8_K : unit = half super-block (U = K/128): q chunks (t*8 + j)*U + u, then bsum chunks
+//                 [t*U + u] (4 ints: sub-blocks 4h..4h+3), then d[t*(U/2) + sb]
+//   Q4_K x fp32 : unit = half super-block: x chunks (t*32 + j)*U + u, then sum chunks [t*U + u]
+//                 (4 floats: sub-block sums)
+__host__ __device__ __forceinline__ int units_per_row(Fmt f, int K) { return f == Fmt::Q8_0xQ8_0 ? K / QK8_0 : K / 128; }
+
+__host__ __device__ __forceinline__ int act_bytes_total(Fmt f, int K, int m) {
+  const int U = units_per_row(f, K);
+  if (f == Fmt::Q8_0xQ8_0) return m * U * 32 + m * U * 4;
+  if (f == Fmt::Q4_KxQ8_K) return m * U * 128 + m * U * 16 + m * (U / 2) * 4;
+  return m * U * 512 + m * U * 16;
+}
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  // unsigned bytes of a times signed bytes of b, accumulated into c
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Bounded mbarrier wait that also gives up as soon as another thread raised the abort flag.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -64,87 +93,127 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   }
 }
 
-// ---- activation prologue: quantized (or fp32) activations -> shared memory -------------------
+// ---- activation prologue ---------------------------------------------------------------------------
 
 __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct) {
-  const int K = a.K;
+  const int K = a.K, m = a.m, lane = ct & 31, cw = ct >> 5;
+  const int U = units_per_row(a.fmt, K);
   if (a.fmt == Fmt::Q8_0xQ8_0) {
-    const int nb = K / QK8_0;
-    int8_t* xs = reinterpret_cast<int8_t*>(act);
-    float* xd = reinterpret_cast<float*>(act + ((a.m * K + 15) & ~15));
-    const uint8_t* src = static_cast<const uint8_t*>(a.act);
-    const int total = a.m * nb * 17;  // 17 half-words per 34-byte block
-    for (int i = ct; i < total; i += CONSUMERS) {
-      const int t = i / (nb * 17);
-      const int rem = i - t * nb * 17;
-      const int b = rem / 17, hw = rem - b * 17;
-      const uint16_t v = *reinterpret_cast<const uint16_t*>(src + static_cast<size_t>(t) * a.act_row_bytes +
-                                                            b * Q8_0_BYTES + hw * 2);
-      if (hw == 0) {
-        xd[t * nb + b] = fp16_bits_to_float(v);
-      } else {
-        *reinterpret_cast<uint16_t*>(xs + t * K + b * QK8_0 + (hw - 1) * 2) = v;
+    int4* xq = reinterpret_cast<int4*>(act);
+    float* xd = reinterpret_cast<float*>(act + m * U * 32);
+    if (a.act_f32) {  // quantize in place: one warp per block (quant.cuh)
+      const float* x = static_cast<const float*>(a.act);
+      for (int blk = cw; blk < m * U; blk += CONSUMER_WARPS) {
+        const int t = blk / U, b = blk - t * U;
+        uint32_t dbits;
+        const int q = warp_q8_0(x[static_cast<size_t>(t) * K + b * QK8_0 + lane], &dbits);
+        // lane i holds element i: gather 4 consecutive lanes into one word
+        const int q1 = __shfl_down_sync(0xFFFFFFFFu, q, 1), q2 = __shfl_down_sync(0xFFFFFFFFu, q, 2),
+                  q3 = __shfl_down_sync(0xFFFFFFFFu, q, 3);
+        if ((lane & 3) == 0) {
+          reinterpret_cast<uint32_t*>(xq + (t * 2 + (lane >> 4)) * U + b)[(lane >> 2) & 3] = pack4_i8(q, q1, q2, q3);
+        }
+        if (lane == 0) xd[t * U + b] = fp16_bits_to_float(dbits);
+      }
+    } else {  // pre-quantized GGUF Q8_0 rows: 17 half-words per 34-byte block
+      const uint8_t* src = static_cast<const uint8_t*>(a.act);
+      for (int i = ct; i < m * U * 17; i += CONSUMERS) {
+        const int t = i / (U * 17), rem = i - t * U * 17, b = rem / 17, hw = rem - b * 17;
+        const uint16_t v = *reinterpret_cast<const uint16_t*>(src + static_cast<size_t>(t) * a.act_row_bytes +
+                                                              b * Q8_0_BYTES + hw * 2);
+        if (hw == 0) {
+          xd[t * U + b] = fp16_bits_to_float(v);
+        } else {
+          const int e = (hw - 1) * 2;  // element offset inside the block
+          reinterpret_cast<uint16_t*>(xq + (t * 2 + (e >> 4)) * U + b)[(e & 15) >> 1] = v;
+        }
       }
     }
   } else if (a.fmt == Fmt::Q4_KxQ8_K) {
-    const int nb = K / QK_K;
-    int8_t* xs = reinterpret_cast<int8_t*>(act);
-    float* xd = reinterpret_cast<float*>(act + a.m * K);
-    int* xbs = reinterpret_cast<int*>(act + a.m * K + ((a.m * nb * 4 + 15) & ~15));
-    const uint8_t* src = static_cast<const uint8_t*>(a.act);
-    const int total = a.m * nb * 73;  // 73 words per 292-byte block
-    for (int i = ct; i < total; i += CONSUMERS) {
-      const int t = i / (nb * 73);
-      const int rem = i - t * nb * 73;
-      const int b = rem / 73, wi = rem - b * 73;
-      const uint32_t v = *reinterpret_cast<const uint32_t*>(src + static_cast<size_t>(t) * a.act_row_bytes +
-                                                            b * Q8_K_BYTES + wi * 4);
-      if (wi == 0) {
-        xd[t * nb + b] = __uint_as_float(v);
-      } else if (wi <= 64) {
-        *reinterpret_cast<uint32_t*>(xs + t * K + b * QK_K + (wi - 1) * 4) = v;
-      } else {
-        const int lo = static_cast<int16_t>(v & 0xFFFFu), hi = static_cast<int16_t>(v >> 16);
-        xbs[(t * nb + b) * 8 + (wi - 65)] = lo + hi;  // bsum of sub-block (wi-65): groups 2j, 2j+1
+    const int nb = U / 2;
+    int4* xq = reinterpret_cast<int4*>(act);
+    int* xb = reinterpret_cast<int*>(act + m * U * 128);
+    float* xd = reinterpret_cast<float*>(act + m * U * 128 + m * U * 16);
+    if (a.act_f32) {  // quantize in place: one warp per 256-block (quant.cuh)
+      const float* x = static_cast<const float*>(a.act);
+      for (int blk = cw; blk < m * nb; blk += CONSUMER_WARPS) {
+        const int t = blk / nb, sb = blk - t * nb;
+        const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * K + sb * QK_K + lane * 8);
+        const float4 v0 = src[0], v1 = src[1];
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        int q[8], gsum;
+        const float d = warp_q8_k(v, q, &gsum);
+        // lane l holds elements 8l..8l+7: unit h = l/16, chunk j = (l%16)/2, half (l&1)
+        const int u = 2 * sb + (lane >> 4), j = (lane & 15) >> 1;
+        uint2* dst = reinterpret_cast<uint2*>(xq + (t * 8 + j) * U + u) + (lane & 1);
+        *dst = make_uint2(pack4_i8(q[0], q[1], q[2], q[3]), pack4_i8(q[4], q[5], q[6], q[7]));
+        // sub-block (32 elements) sums: lanes 4s .. 4s+3 (gsum already covers lane pairs)
+        const int s32 = gsum + __shfl_down_sync(0xFFFFFFFFu, gsum, 2);
+        if ((lane & 3) == 0) xb[(t * U + u) * 4 + ((lane >> 2) & 3)] = s32;
+        if (lane == 0) xd[t * nb + sb] = d;
+      }
+    } else {  // pre-quantized GGUF Q8_K rows: 73 words per 292-byte block
+      const uint8_t* src = static_cast<const uint8_t*>(a.act);
+      for (int i = ct; i < m * nb * 73; i += CONSUMERS) {
+        const int t = i / (nb * 73), rem = i - t * nb * 73, sb = rem / 73, wi = rem - sb * 73;
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(src + static_cast<size_t>(t) * a.act_row_bytes +
+                                                              sb * Q8_K_BYTES + wi * 4);
+        if (wi == 0) {
+          xd[t * nb + sb] = __uint_as_float(v);
+        } else if (wi <= 64) {
+          const int e = (wi - 1) * 4;  // element offset inside the super-block
+          const int u = 2 * sb + (e >> 7), j = (e & 127) >> 4;
+          reinterpret_cast<uint32_t*>(xq + (t * 8 + j) * U + u)[(e & 15) >> 2] = v;
+        } else {
+          const int s = wi - 65;  // sub-block s: bsum groups 2s, 2s+1
+          const int lo = static_cast<int16_t>(v & 0xFFFFu), hi = static_cast<int16_t>(v >> 16);
+          xb[(t * U + 2 * sb + (s >> 2)) * 4 + (s & 3)] = lo + hi;
+        }
       }
     }
-  } else {
-    float* xf = reinterpret_cast<float*>(act);
-    float* xsx = xf + a.m * K;
-    const float* src = static_cast<const float*>(a.act);
-    const int n4 = a.m * K / 4;
-    for (int i = ct; i < n4; i += CONSUMERS) {
-      reinterpret_cast<float4*>(xf)[i] = reinterpret_cast<const float4*>(src)[i];
+  } else {  // fp32 activations for the Q4_K logits path
+    const float* x = static_cast<const float*>(a.act);
+    float4* xf = reinterpret_cast<float4*>(act);
+    float* xs = reinterpret_cast<float*>(act + m * U * 512);
+    for (int i = ct; i < m * U * 32; i += CONSUMERS) {  // i = source float4 index
+      const int t = i / (U * 32), rem = i - t * U * 32, u = rem >> 5, j = rem & 31;
+      xf[(t * 32 + j) * U + u] = reinterpret_cast<const float4*>(x)[i];
     }
-    const int nsub = a.m * K / 32;
-    for (int i = ct; i < nsub; i += CONSUMERS) {
-      const float4* p = reinterpret_cast<const float4*>(src + static_cast<size_t>(i) * 32);
+    for (int i = ct; i < m * U * 4; i += CONSUMERS) {  // sub-block sums, sequential order
+      const float4* p = reinterpret_cast<const float4*>(x + static_cast<size_t>(i) * 32);
       float s = 0.0f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float4 v = p[j];
+      for (int k = 0; k < 8; ++k) {
+        const float4 v = p[k];
         s += v.x;
         s += v.y;
         s += v.z;
         s += v.w;
       }
-      xsx[i] = s;
+      const int t = i / (U * 4), rem = i - t * U * 4;
+      xs[(t * U + (rem >> 2)) * 4 + (rem & 3)] = s;
     }
   }
 }
 
-// ---- per-tile compute ------------------------------------------------------------------------
+// ---- per-row compute: one warp per row, lane = work unit ------------------------------------------
 
-// Q8_0 weight block (34 B, only 2-byte aligned inside the stage) x Q8_0 activation block.
-template <RowOut MODE>
-__device__ __forceinline__ void tile_q8_0(const RowStreamArgs& a, const uint8_t* act, const uint8_t* tb, int nr,
-                                          long long r0, float* pb, int part_stride, int ct) {
-  const int K = a.K, nb = K / QK8_0, items = nr * nb;
-  const int8_t* xs = reinterpret_cast<const int8_t*>(act);
-  const float* xd = reinterpret_cast<const float*>(act + ((a.m * K + 15) & ~15));
-  for (int item = ct; item < items; item += CONSUMERS) {
-    const int r = item / nb, b = item - r * nb;
-    const uint8_t* p = tb + static_cast<size_t>(r) * a.row_bytes + b * Q8_0_BYTES;
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// Q8_0 weight row x Q8_0 activations.  Blocks are 34 B, so inside the stage they are only
+// 2-byte aligned: read the 9 covering words and realign.
+template <RowOut MODE, int MTOK>
+__device__ __forceinline__ void row_q8_0(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
+                                         long long row, float (&acc)[MTOK], int lane) {
+  const int U = a.K / QK8_0;
+  const int4* xq = reinterpret_cast<const int4*>(act);
+  const float* xd = reinterpret_cast<const float*>(act + a.m * U * 32);
+  for (int b = lane; b < U; b += 32) {
+    const uint8_t* p = rowp + b * Q8_0_BYTES;
     const bool odd = (reinterpret_cast<uintptr_t>(p) & 2u) != 0;  // rows and blocks have even sizes
     const uint32_t* w = reinterpret_cast<const uint32_t*>(p - (odd ? 2 : 0));
     uint32_t wv[9];
@@ -155,22 +224,23 @@ __device__ __forceinline__ void tile_q8_0(const RowStreamArgs& a, const uint8_t*
 #pragma unroll
     for (int i = 0; i < 8; ++i) q[i] = static_cast<int>(odd ? wv[i + 1] : __funnelshift_r(wv[i], wv[i + 1], 16));
     const float dw = fp16_bits_to_float(dbits);
-    for (int t = 0; t < a.m; ++t) {
-      const int4* xv = reinterpret_cast<const int4*>(xs + t * K + b * QK8_0);
-      const int4 x0 = xv[0], x1 = xv[1];
-      int ip = dp4a(q[0], x0.x, 0);
-      ip = dp4a(q[1], x0.y, ip);
-      ip = dp4a(q[2], x0.z, ip);
-      ip = dp4a(q[3], x0.w, ip);
-      ip = dp4a(q[4], x1.x, ip);
-      ip = dp4a(q[5], x1.y, ip);
-      ip = dp4a(q[6], x1.z, ip);
-      ip = dp4a(q[7], x1.w, ip);
-      if constexpr (MODE == RowOut::Partials) {
-        a.partials[(static_cast<size_t>(t) * a.n_rows + r0 + r) * nb + b] = ip;
-      } else {
-        // gguf_dot_q8.c:475-476: d_w * d_x * (float)ip
-        pb[t * part_stride + r * nb + b] = (dw * xd[t * nb + b]) * static_cast<float>(ip);
+#pragma unroll
+    for (int t = 0; t < MTOK; ++t) {
+      if (MTOK == 1 || t < a.m) {
+        const int4 x0 = xq[(t * 2) * U + b], x1 = xq[(t * 2 + 1) * U + b];
+        int ip = dp4a(q[0], x0.x, 0);
+        ip = dp4a(q[1], x0.y, ip);
+        ip = dp4a(q[2], x0.z, ip);
+        ip = dp4a(q[3], x0.w, ip);
+        ip = dp4a(q[4], x1.x, ip);
+        ip = dp4a(q[5], x1.y, ip);
+        ip = dp4a(q[6], x1.z, ip);
+        ip = dp4a(q[7], x1.w, ip);
+        if constexpr (MODE == RowOut::Partials) {
+          a.partials[(static_cast<size_t>(t) * a.n_rows + row) * U + b] = ip;
+        } else {
+          acc[t] += (dw * xd[t * U + b]) * static_cast<float>(ip);  // gguf_dot_q8.c:475-476
+        }
       }
     }
   }
@@ -189,85 +259,88 @@ __device__ __forceinline__ void q4k_scales_half(uint32_t s0, uint32_t s1, uint32
   }
 }
 
-// Q4_K weight x Q8_K activation.  A work item is half a super-block (4 sub-blocks, 64 quant
-// bytes); the two halves of a super-block sit in adjacent lanes and are combined in int32
-// before the float step, so every per-block int32 (sumi, summ) equals the reference's.
-template <RowOut MODE>
-__device__ __forceinline__ void tile_q4k_q8k(const RowStreamArgs& a, const uint8_t* act, const uint8_t* tb, int nr,
-                                             long long r0, float* pb, int part_stride, int ct) {
-  const int K = a.K, nb = K / QK_K, U = 2 * nb, items = nr * U;
-  const int lane = ct & 31;
-  const int8_t* xs = reinterpret_cast<const int8_t*>(act);
-  const float* xd = reinterpret_cast<const float*>(act + a.m * K);
-  const int* xbs = reinterpret_cast<const int*>(act + a.m * K + ((a.m * nb * 4 + 15) & ~15));
-  for (int base = ct - lane; base < items; base += CONSUMERS) {
-    const int item = base + lane;
-    const bool live = item < items;
-    int r = 0, sb = 0, h = 0;
+// Load half h of super-block sb of a Q4_K row: header (d, dmin, scales) and 64 quant bytes.
+__device__ __forceinline__ void q4k_load_half(const uint8_t* rowp, int sb, int h, uint4& hdr, uint32_t (&qw)[16]) {
+  const uint8_t* blk = rowp + sb * Q4_K_BYTES;
+  hdr = *reinterpret_cast<const uint4*>(blk);
+  const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 64 * h);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 v = qp[i];
+    qw[4 * i + 0] = v.x;
+    qw[4 * i + 1] = v.y;
+    qw[4 * i + 2] = v.z;
+    qw[4 * i + 3] = v.w;
+  }
+}
+
+// Q4_K weight row x Q8_K activations.  A lane takes half a super-block u = 2*sb + h (4
+// sub-blocks, 64 quant bytes); the halves of one super-block sit in adjacent lanes and are
+// combined in int32 before the float step, so every per-block (sumi, summ) equals the
+// reference's int32 values.  High nibbles are used in place (byte & 0xF0 = 16*q) with an
+// unsigned-by-signed dp4a and the exact sum is shifted down by 4 afterwards.
+template <RowOut MODE, int MTOK>
+__device__ __forceinline__ void row_q4k_q8k(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
+                                            long long row, float (&acc)[MTOK], int lane) {
+  const int U = a.K / 128, nb = U / 2;
+  const int4* xq = reinterpret_cast<const int4*>(act);
+  const int4* xb = reinterpret_cast<const int4*>(act + a.m * U * 128);
+  const float* xd = reinterpret_cast<const float*>(act + a.m * U * 128 + a.m * U * 16);
+  for (int u0 = 0; u0 < U; u0 += 32) {
+    const int u = u0 + lane;
+    const bool live = u < U;
+    const int sb = u >> 1, h = u & 1;
     uint4 hdr = make_uint4(0, 0, 0, 0);
     uint32_t qw[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) qw[i] = 0;
-    if (live) {
-      r = item / U;
-      const int u = item - r * U;
-      sb = u >> 1;
-      h = u & 1;
-      const uint8_t* blk = tb + static_cast<size_t>(r) * a.row_bytes + sb * Q4_K_BYTES;
-      hdr = *reinterpret_cast<const uint4*>(blk);
-      const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 64 * h);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 v = qp[i];
-        qw[4 * i + 0] = v.x;
-        qw[4 * i + 1] = v.y;
-        qw[4 * i + 2] = v.z;
-        qw[4 * i + 3] = v.w;
-      }
-    }
+    if (live) q4k_load_half(rowp, sb, h, hdr, qw);
     uint32_t sc4, mn4;
     q4k_scales_half(hdr.y, hdr.z, hdr.w, h, sc4, mn4);
     const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
-    for (int t = 0; t < a.m; ++t) {
-      int sumi = 0, summ = 0;
-      if (live) {
-        const int4* xv = reinterpret_cast<const int4*>(xs + t * K + sb * QK_K + 128 * h);
-        int ip[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {  // quant group 2h+g: low nibbles -> ip[2g], high -> ip[2g+1]
+    for (int t = 0; t < MTOK; ++t) {
+      if (MTOK == 1 || t < a.m) {  // warp-uniform
+        int sumi = 0, summ = 0;
+        if (live) {
+          int ip[4] = {0, 0, 0, 0};
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int4 xl = xv[4 * g + c];      // elements 64g + 16c .. +16 (low-nibble sub-block)
-            const int4 xh = xv[4 * g + 2 + c];  // elements 64g + 32 + 16c .. +16 (high-nibble sub-block)
-            const uint32_t w0 = qw[8 * g + 4 * c + 0], w1 = qw[8 * g + 4 * c + 1];
-            const uint32_t w2 = qw[8 * g + 4 * c + 2], w3 = qw[8 * g + 4 * c + 3];
-            ip[2 * g] = dp4a(static_cast<int>(w0 & 0x0F0F0F0Fu), xl.x, ip[2 * g]);
-            ip[2 * g] = dp4a(static_cast<int>(w1 & 0x0F0F0F0Fu), xl.y, ip[2 * g]);
-            ip[2 * g] = dp4a(static_cast<int>(w2 & 0x0F0F0F0Fu), xl.z, ip[2 * g]);
-            ip[2 * g] = dp4a(static_cast<int>(w3 & 0x0F0F0F0Fu), xl.w, ip[2 * g]);
-            ip[2 * g + 1] = dp4a(static_cast<int>((w0 >> 4) & 0x0F0F0F0Fu), xh.x, ip[2 * g + 1]);
-            ip[2 * g + 1] = dp4a(static_cast<int>((w1 >> 4) & 0x0F0F0F0Fu), xh.y, ip[2 * g + 1]);
-            ip[2 * g + 1] = dp4a(static_cast<int>((w2 >> 4) & 0x0F0F0F0Fu), xh.z, ip[2 * g + 1]);
-            ip[2 * g + 1] = dp4a(static_cast<int>((w3 >> 4) & 0x0F0F0F0Fu), xh.w, ip[2 * g + 1]);
+          for (int j = 0; j < 8; ++j) {  // chunk j: group g = j/4; j%4 < 2 low nibbles, else high
+            const int4 x = xq[(t * 8 + j) * U + u];
+            const int g = j >> 2, c = j & 1;
+            const uint32_t* w = qw + 8 * g + 4 * c;
+            if ((j & 2) == 0) {
+              ip[2 * g] = dp4a(static_cast<int>(w[0] & 0x0F0F0F0Fu), x.x, ip[2 * g]);
+              ip[2 * g] = dp4a(static_cast<int>(w[1] & 0x0F0F0F0Fu), x.y, ip[2 * g]);
+              ip[2 * g] = dp4a(static_cast<int>(w[2] & 0x0F0F0F0Fu), x.z, ip[2 * g]);
+              ip[2 * g] = dp4a(static_cast<int>(w[3] & 0x0F0F0F0Fu), x.w, ip[2 * g]);
+            } else {
+              ip[2 * g + 1] = dp4a_us(w[0] & 0xF0F0F0F0u, x.x, ip[2 * g + 1]);
+              ip[2 * g + 1] = dp4a_us(w[1] & 0xF0F0F0F0u, x.y, ip[2 * g + 1]);
+              ip[2 * g + 1] = dp4a_us(w[2] & 0xF0F0F0F0u, x.z, ip[2 * g + 1]);
+              ip[2 * g + 1] = dp4a_us(w[3] & 0xF0F0F0F0u, x.w, ip[2 * g + 1]);
+            }
           }
+          ip[1] >>= 4;  // exact: the sums of 16*q*x are multiples of 16
+          ip[3] >>= 4;
+          const int4 bs = xb[t * U + u];
+          sumi = static_cast<int>(sc4 & 0xFFu) * ip[0] + static_cast<int>((sc4 >> 8) & 0xFFu) * ip[1] +
+                 static_cast<int>((sc4 >> 16) & 0xFFu) * ip[2] + static_cast<int>(sc4 >> 24) * ip[3];
+          summ = static_cast<int>(mn4 & 0xFFu) * bs.x + static_cast<int>((mn4 >> 8) & 0xFFu) * bs.y +
+                 static_cast<int>((mn4 >> 16) & 0xFFu) * bs.z + static_cast<int>(mn4 >> 24) * bs.w;
         }
-        const int4 bs = *reinterpret_cast<const int4*>(xbs + (t * nb + sb) * 8 + 4 * h);
-        sumi = static_cast<int>(sc4 & 0xFFu) * ip[0] + static_cast<int>((sc4 >> 8) & 0xFFu) * ip[1] +
-               static_cast<int>((sc4 >> 16) & 0xFFu) * ip[2] + static_cast<int>(sc4 >> 24) * ip[3];
-        summ = static_cast<int>(mn4 & 0xFFu) * bs.x + static_cast<int>((mn4 >> 8) & 0xFFu) * bs.y +
-               static_cast<int>((mn4 >> 16) & 0xFFu) * bs.z + static_cast<int>(mn4 >> 24) * bs.w;
-      }
-      sumi += __shfl_xor_sync(0xFFFFFFFFu, sumi, 1);
-      summ += __shfl_xor_sync(0xFFFFFFFFu, summ, 1);
-      if (live && h == 0) {
-        if constexpr (MODE == RowOut::Partials) {
-          int32_t* pp = a.partials + ((static_cast<size_t>(t) * a.n_rows + r0 + r) * nb + sb) * 2;
-          pp[0] = sumi;
-          pp[1] = summ;
-        } else {
-          // gguf_dot_q8.c:619-620 and :640/:661: d = d_x*d_w, dmin = -d_x*dmin_w per super-block.
-          const float dx = xd[t * nb + sb];
-          pb[t * part_stride + r * nb + sb] = (dx * dw) * static_cast<float>(sumi) - (dx * dmw) * static_cast<float>(summ);
+        sumi += __shfl_xor_sync(0xFFFFFFFFu, sumi, 1);
+        summ += __shfl_xor_sync(0xFFFFFFFFu, summ, 1);
+        if (live && h == 0) {
+          if constexpr (MODE == RowOut::Partials) {
+            int32_t* pp = a.partials + ((static_cast<size_t>(t) * a.n_rows + row) * nb + sb) * 2;
+            pp[0] = sumi;
+            pp[1] = summ;
+          } else {
+            // gguf_dot_q8.c:619-620, :640, :661: d = d_x*d_w and dmin = -d_x*dmin_w per super-block.
+            const float dx = xd[t * nb + sb];
+            acc[t] += (dx * dw) * static_cast<float>(sumi) - (dx * dmw) * static_cast<float>(summ);
+          }
         }
       }
     }
@@ -275,77 +348,58 @@ __device__ __forceinline__ void tile_q4k_q8k(const RowStreamArgs& a, const uint8
 }
 
 __device__ __forceinline__ float nib_f(uint32_t masked, int k) {
-  // byte k of a word whose bytes are 0..15, as an exact float: 2^23 + v, minus 2^23.
+  // byte k of a word whose bytes are 0..15, as an exact float: (2^23 + v) - 2^23.
   return __uint_as_float(__byte_perm(masked, 0x4B000000u, 0x7440u | static_cast<uint32_t>(k))) - 8388608.0f;
 }
 
-// Q4_K weight x fp32 activation (the reference's logits path for non-Q8_0 weights).
-template <RowOut MODE>
-__device__ __forceinline__ void tile_q4k_f32(const RowStreamArgs& a, const uint8_t* act, const uint8_t* tb, int nr,
-                                             float* pb, int part_stride, int ct) {
-  const int K = a.K, nb = K / QK_K, U = 2 * nb, items = nr * U;
-  const int lane = ct & 31;
-  const float* xf = reinterpret_cast<const float*>(act);
-  const float* xsx = xf + a.m * K;
-  for (int base = ct - lane; base < items; base += CONSUMERS) {
-    const int item = base + lane;
-    const bool live = item < items;
-    int r = 0, sb = 0, h = 0;
-    uint4 hdr = make_uint4(0, 0, 0, 0);
+// Q4_K weight row x fp32 activations (the reference's logits path for non-Q8_0 weights).
+template <RowOut MODE, int MTOK>
+__device__ __forceinline__ void row_q4k_f32(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
+                                            float (&acc)[MTOK], int lane) {
+  const int U = a.K / 128;
+  const float4* xf = reinterpret_cast<const float4*>(act);
+  const float4* xs = reinterpret_cast<const float4*>(act + a.m * U * 512);
+  for (int u0 = 0; u0 < U; u0 += 32) {
+    const int u = u0 + lane;
+    if (u >= U) break;
+    const int sb = u >> 1, h = u & 1;
+    uint4 hdr;
     uint32_t qw[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) qw[i] = 0;
-    if (live) {
-      r = item / U;
-      const int u = item - r * U;
-      sb = u >> 1;
-      h = u & 1;
-      const uint8_t* blk = tb + static_cast<size_t>(r) * a.row_bytes + sb * Q4_K_BYTES;
-      hdr = *reinterpret_cast<const uint4*>(blk);
-      const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 64 * h);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 v = qp[i];
-        qw[4 * i + 0] = v.x;
-        qw[4 * i + 1] = v.y;
-        qw[4 * i + 2] = v.z;
-        qw[4 * i + 3] = v.w;
-      }
-    }
+    q4k_load_half(rowp, sb, h, hdr, qw);
     uint32_t sc4, mn4;
     q4k_scales_half(hdr.y, hdr.z, hdr.w, h, sc4, mn4);
     const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
-    for (int t = 0; t < a.m; ++t) {
-      float acc = 0.0f;
-      if (live) {
-        const float* xr = xf + t * K + sb * QK_K + 128 * h;
-        const float* sx = xsx + t * (K / 32) + sb * 8 + 4 * h;
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {  // sub-block 4h+s: group 2h+(s>>1), nibble half (s&1)
+    for (int t = 0; t < MTOK; ++t) {
+      if (MTOK == 1 || t < a.m) {
+        const float4 sx = xs[t * U + u];
+        const float sxs[4] = {sx.x, sx.y, sx.z, sx.w};
+        float c = 0.0f;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {  // sub-block 4h+s: group s>>1, nibble half (s&1)
           float qx = 0.0f;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const uint32_t mw = (qw[8 * (s >> 1) + i] >> (4 * (s & 1))) & 0x0F0F0F0Fu;
-            const float4 xv = *reinterpret_cast<const float4*>(xr + 32 * s + 4 * i);
-            qx = fmaf(nib_f(mw, 0), xv.x, qx);
-            qx = fmaf(nib_f(mw, 1), xv.y, qx);
-            qx = fmaf(nib_f(mw, 2), xv.z, qx);
-            qx = fmaf(nib_f(mw, 3), xv.w, qx);
+            const float4 x4 = xf[(t * 32 + 8 * s + i) * U + u];
+            qx = fmaf(nib_f(mw, 0), x4.x, qx);
+            qx = fmaf(nib_f(mw, 1), x4.y, qx);
+            qx = fmaf(nib_f(mw, 2), x4.z, qx);
+            qx = fmaf(nib_f(mw, 3), x4.w, qx);
           }
           const float d1 = dw * static_cast<float>((sc4 >> (8 * s)) & 0xFFu);
           const float m1 = dmw * static_cast<float>((mn4 >> (8 * s)) & 0xFFu);
-          acc += d1 * qx - m1 * sx[s];  // gguf_quant.c:744/746
+          c += d1 * qx - m1 * sxs[s];  // gguf_quant.c:744/746
         }
+        acc[t] += c;
       }
-      acc += __shfl_xor_sync(0xFFFFFFFFu, acc, 1);
-      if (live && h == 0) pb[t * part_stride + r * nb + sb] = acc;
     }
   }
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------
 
-template <Fmt F, RowOut MODE>
+template <Fmt F, RowOut MODE, int MTOK>
 __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamArgs a, const Layout L) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -363,16 +417,20 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
     fence_mbar_init();
   }
   __syncthreads();
+  // Dependent launches may start their weight prefetch as soon as every CTA of this grid runs;
+  // they wait (griddepcontrol.wait) for this grid to finish before touching its outputs.
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane != 0) return;
-    // ---------------- producer ----------------
+    // ---------------- producer (weights only: never waits on the previous grid) ----------------
     const uint64_t pol = l2_evict_first_policy();
     long long it = 0;
+    int s = 0;
+    uint32_t ephase = 1;  // iteration it >= S waits for completion (it/S - 1) of empty[s]: parity (it/S - 1) & 1
     for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x, ++it) {
-      const int s = static_cast<int>(it % S);
       if (it >= S) {
-        if (!wait_or_abort(&empty[s], static_cast<uint32_t>((it / S - 1) & 1), abort_flag)) {
+        if (!wait_or_abort(&empty[s], ephase, abort_flag)) {
           atomicOr(a.status, ST_TIMEOUT_EMPTY);
           *abort_flag = 1;
           break;
@@ -385,6 +443,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
       const uint32_t bytes = static_cast<uint32_t>((start - al + nr * a.row_bytes + 15) & ~15ull);
       mbar_arrive_expect_tx(&full[s], bytes);
       bulk_g2s(smem + L.stage_off + s * L.stage_bytes, reinterpret_cast<const void*>(al), bytes, &full[s], pol);
+      if (++s == S) {
+        s = 0;
+        ephase ^= 1u;
+      }
     }
     // Drain: the last copies issued into each stage must land before the CTA may exit.
     for (long long j = (it > S ? it - S : 0); j < it; ++j) {
@@ -394,161 +456,156 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   }
 
   // ---------------- consumers ----------------
-  const int ct = threadIdx.x - 32;
-  const int cw = ct >> 5;
+  const int cw = warp - 1;
   uint8_t* act = smem + L.act_off;
-  float* part = reinterpret_cast<float*>(smem + L.part_off);
-  load_act(a, act, ct);
+  griddep_wait();  // the activations may be the previous grid's output
+  load_act(a, act, threadIdx.x - 32);
   named_bar_sync(1, CONSUMERS);
 
-  const int nb = blocks_per_row(F, a.K);
   unsigned long long best = 0ull;
   bool dead = false;
-  long long it = 0;
-  for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x, ++it) {
-    const int s = static_cast<int>(it % S);
-    if (!dead && !wait_or_abort(&full[s], static_cast<uint32_t>((it / S) & 1), abort_flag)) {
+  int s = 0;
+  uint32_t fphase = 0;
+  int first = cw;  // row of the current tile that belongs to this warp (round-robin over the CTA's rows)
+  for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
+    if (!dead && !wait_or_abort(&full[s], fphase, abort_flag)) {
       atomicOr(a.status, ST_TIMEOUT_FULL);
       *abort_flag = 1;
       dead = true;
     }
     const long long r0 = tile * L.tile_rows;
     const int nr = static_cast<int>(min(static_cast<long long>(L.tile_rows), a.n_rows - r0));
-    float* pb = part + (it & 1) * L.part_stride;
     if (!dead) {
       const uintptr_t start = reinterpret_cast<uintptr_t>(a.w) + static_cast<uintptr_t>(r0) * a.row_bytes;
       const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + (start & 15u);
-      if constexpr (F == Fmt::Q8_0xQ8_0) {
-        tile_q8_0<MODE>(a, act, tb, nr, r0, pb, L.tile_rows * nb, ct);
-      } else if constexpr (F == Fmt::Q4_KxQ8_K) {
-        tile_q4k_q8k<MODE>(a, act, tb, nr, r0, pb, L.tile_rows * nb, ct);
-      } else {
-        tile_q4k_f32<MODE>(a, act, tb, nr, pb, L.tile_rows * nb, ct);
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    if constexpr (MODE != RowOut::Partials) {
-      named_bar_sync(1, CONSUMERS);
-      if (!dead) {
-        for (int r = cw; r < nr; r += CONSUMER_WARPS) {
-          for (int t = 0; t < a.m; ++t) {
-            float v = 0.0f;
-            for (int b = lane; b < nb; b += 32) v += pb[t * L.tile_rows * nb + r * nb + b];
+      for (int r = first; r < nr; r += CONSUMER_WARPS) {
+        float acc[MTOK];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-            if (lane == 0) {
-              const long long row = r0 + r;
-              const float y = (a.bias != nullptr ? a.bias[row] : 0.0f) + v;  // cpu_kernel.c:596-597
-              if constexpr (MODE == RowOut::Store) {
-                a.out[static_cast<size_t>(t) * a.out_stride + row] = y;
-              } else {
-                const unsigned long long k = argmax_key(y, static_cast<uint32_t>(a.row0 + row));
-                best = k > best ? k : best;
-              }
+        for (int t = 0; t < MTOK; ++t) acc[t] = 0.0f;
+        const uint8_t* rowp = tb + static_cast<size_t>(r) * a.row_bytes;
+        if constexpr (F == Fmt::Q8_0xQ8_0) {
+          row_q8_0<MODE, MTOK>(a, act, rowp, r0 + r, acc, lane);
+        } else if constexpr (F == Fmt::Q4_KxQ8_K) {
+          row_q4k_q8k<MODE, MTOK>(a, act, rowp, r0 + r, acc, lane);
+        } else {
+          row_q4k_f32<MODE, MTOK>(a, act, rowp, acc, lane);
+        }
+        if constexpr (MODE != RowOut::Partials) {
+          const long long row = r0 + r;
+          float mine = 0.0f;
+#pragma unroll
+          for (int t = 0; t < MTOK; ++t) {
+            if (MTOK == 1 || t < a.m) {
+              const float v = warp_sum(acc[t]);
+              if (lane == t) mine = v;
+            }
+          }
+          if (lane < a.m) {
+            const float y = (a.bias != nullptr ? a.bias[row] : 0.0f) + mine;  // cpu_kernel.c:596-597
+            if constexpr (MODE == RowOut::Store) {
+              a.out[static_cast<size_t>(lane) * a.out_stride + row] = y;
+            } else {
+              const unsigned long long k = argmax_key(y, static_cast<uint32_t>(a.row0 + row));
+              best = k > best ? k : best;
             }
           }
         }
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    first = ((first - nr) % CONSUMER_WARPS + CONSUMER_WARPS) % CONSUMER_WARPS;
+    if (++s == S) {
+      s = 0;
+      fphase ^= 1u;
+    }
   }
   if constexpr (MODE == RowOut::Argmax) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+      best = other > best ? other : best;
+    }
     if (lane == 0 && best != 0ull) atomicMax(a.key, best);
   }
 }
 
-template <Fmt F, RowOut MODE>
+template <Fmt F, RowOut MODE, int MTOK>
 cudaError_t launch_impl(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
-  static int configured_smem = 0;  // per instantiation; the host API is single-threaded per process
-  auto kern = rowstream_kernel<F, MODE>;
+  static int configured_smem = 0;  // per instantiation; the host API serialises its callers
+  auto kern = rowstream_kernel<F, MODE, MTOK>;
   if (L.smem_total > configured_smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_total);
     if (e != cudaSuccess) return e;
     configured_smem = L.smem_total;
   }
-  kern<<<grid, THREADS, L.smem_total, st>>>(a, L);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = L.smem_total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a, L);
 }
 
-int act_bytes_per_row(Fmt f, int K) {
-  switch (f) {
-    case Fmt::Q8_0xQ8_0:
-      return K + 4 * (K / QK8_0);
-    case Fmt::Q4_KxQ8_K:
-      return K + 4 * (K / QK_K) + 32 * (K / QK_K);
-    default:
-      return 4 * K + 4 * (K / 32);
-  }
-}
-
-int act_bytes_total(Fmt f, int K, int m) {
-  if (f == Fmt::Q8_0xQ8_0) return ((m * K + 15) & ~15) + m * (K / QK8_0) * 4;
-  if (f == Fmt::Q4_KxQ8_K) return m * K + ((m * (K / QK_K) * 4 + 15) & ~15) + m * (K / QK_K) * 32;
-  return 4 * m * K + 4 * m * (K / 32);
+template <Fmt F, RowOut MODE>
+cudaError_t launch_mtok(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
+  if (a.m <= 1) return launch_impl<F, MODE, 1>(a, L, grid, st);
+  if (a.m <= 2) return launch_impl<F, MODE, 2>(a, L, grid, st);
+  if (a.m <= 4) return launch_impl<F, MODE, 4>(a, L, grid, st);
+  return launch_impl<F, MODE, 8>(a, L, grid, st);
 }
 
 }  // namespace
 
 int rowstream_max_m(Fmt fmt, int K, const DeviceInfo& dev) {
   (void)dev;
-  const int per = act_bytes_per_row(fmt, K) + 64;
-  return per > ACT_BUDGET ? 0 : ACT_BUDGET / per;
+  const int per = act_bytes_total(fmt, K, 1) + 64;
+  const int m = per > ACT_BUDGET ? 0 : ACT_BUDGET / per;
+  return m < MAX_M ? m : MAX_M;
 }
+
+bool rowstream_quantizes_itself(Fmt fmt, int m) { return fmt != Fmt::Q4_KxF32 && m <= PROLOGUE_QUANT_MAX_M; }
 
 cudaError_t launch_rowstream(const RowStreamArgs& a, const DeviceInfo& dev, cudaStream_t st) {
   if (a.n_rows <= 0 || a.m <= 0) return cudaSuccess;
-  const int nb = a.fmt == Fmt::Q8_0xQ8_0 ? a.K / QK8_0 : a.K / QK_K;
+  if (a.m > MAX_M || a.K % (a.fmt == Fmt::Q8_0xQ8_0 ? QK8_0 : QK_K) != 0) return cudaErrorInvalidValue;
   Layout L{};
   L.stage_bytes = STAGE_TARGET;
   if (a.row_bytes + STAGE_SLACK > L.stage_bytes) L.stage_bytes = (a.row_bytes + STAGE_SLACK + 127) & ~127;
   const int r_cap = (L.stage_bytes - STAGE_SLACK) / a.row_bytes;
-  long long r_want = (a.n_rows + 4LL * dev.sm_count - 1) / (4LL * dev.sm_count);
+  long long r_want = (a.n_rows + 3LL * dev.sm_count - 1) / (3LL * dev.sm_count);
   if (r_want < 1) r_want = 1;
   L.tile_rows = static_cast<int>(r_want < r_cap ? r_want : r_cap);
+  L.n_tiles = (a.n_rows + L.tile_rows - 1) / L.tile_rows;
   const int act = (act_bytes_total(a.fmt, a.K, a.m) + 127) & ~127;
   L.act_off = BAR_BYTES;
-  L.part_off = L.act_off + act;
-  int S = 0;
-  for (;;) {  // shrink the tile until the partials buffer leaves room for >= 2 stages
-    L.part_stride = a.m * L.tile_rows * nb;
-    const int part = (2 * L.part_stride * 4 + 127) & ~127;
-    L.stage_off = L.part_off + part;
-    S = (dev.max_smem_optin - L.stage_off) / L.stage_bytes;
-    if (S >= 2 || L.tile_rows == 1) break;
-    L.tile_rows = (L.tile_rows + 1) / 2;
-  }
-  L.n_tiles = (a.n_rows + L.tile_rows - 1) / L.tile_rows;
+  L.stage_off = L.act_off + act;
+  int S = (dev.max_smem_optin - L.stage_off) / L.stage_bytes;
   if (S > MAX_STAGES) S = MAX_STAGES;
   if (S < 2) return cudaErrorInvalidConfiguration;
   L.n_stages = S;
   L.smem_total = L.stage_off + S * L.stage_bytes;
   const int grid = static_cast<int>(L.n_tiles < dev.sm_count ? L.n_tiles : dev.sm_count);
 
-#define EX_DISPATCH_MODE(FMT)                                                 \
-  switch (a.mode) {                                                           \
-    case RowOut::Store:                                                       \
-      return launch_impl<FMT, RowOut::Store>(a, L, grid, st);                 \
-    case RowOut::Argmax:                                                      \
-      return launch_impl<FMT, RowOut::Argmax>(a, L, grid, st);                \
-    default:                                                                  \
-      return launch_impl<FMT, RowOut::Partials>(a, L, grid, st);              \
-  }
   switch (a.fmt) {
     case Fmt::Q8_0xQ8_0:
-      EX_DISPATCH_MODE(Fmt::Q8_0xQ8_0)
+      if (a.mode == RowOut::Store) return launch_mtok<Fmt::Q8_0xQ8_0, RowOut::Store>(a, L, grid, st);
+      if (a.mode == RowOut::Argmax) return launch_mtok<Fmt::Q8_0xQ8_0, RowOut::Argmax>(a, L, grid, st);
+      return launch_mtok<Fmt::Q8_0xQ8_0, RowOut::Partials>(a, L, grid, st);
     case Fmt::Q4_KxQ8_K:
-      EX_DISPATCH_MODE(Fmt::Q4_KxQ8_K)
+      if (a.mode == RowOut::Store) return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::Store>(a, L, grid, st);
+      if (a.mode == RowOut::Argmax) return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::Argmax>(a, L, grid, st);
+      return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::Partials>(a, L, grid, st);
     default:
-      switch (a.mode) {
-        case RowOut::Store:
-          return launch_impl<Fmt::Q4_KxF32, RowOut::Store>(a, L, grid, st);
-        case RowOut::Argmax:
-          return launch_impl<Fmt::Q4_KxF32, RowOut::Argmax>(a, L, grid, st);
-        default:
-          return cudaErrorInvalidValue;
-      }
+      if (a.mode == RowOut::Store) return launch_mtok<Fmt::Q4_KxF32, RowOut::Store>(a, L, grid, st);
+      if (a.mode == RowOut::Argmax) return launch_mtok<Fmt::Q4_KxF32, RowOut::Argmax>(a, L, grid, st);
+      return cudaErrorInvalidValue;
   }
-#undef EX_DISPATCH_MODE
 }
 
 }  // namespace ex

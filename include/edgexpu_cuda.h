@@ -3,7 +3,7 @@
  * EdgeXPU-LLM's quantized matrix-product path.
  *
  * Plain C types only (no CUDA or torch types): pointers, sizes, and `void *stream` (a
- * cudaStream_t, or NULL for the library's own stream).  Every entry point returns 1 on
+ * cudaStream_t; NULL is the CUDA default stream).  Every entry point returns 1 on
  * success and 0 on failure; failures also leave a message in `error` (when given) and in
  * edgexpu_cuda_last_error().  There is no CPU fallback: without a CUDA device every call
  * fails.
@@ -13,6 +13,8 @@
  *                                     (and edgexpu_cpu_linear_quant    include/edgexpu/cpu_kernel.h:60-68)
  *   edgexpu_cuda_quantize_q8_0        edgexpu_gguf_quantize_q8_0       include/edgexpu/gguf_quant.h:80-81
  *   edgexpu_cuda_quantize_q8_k        edgexpu_gguf_quantize_q8_k       include/edgexpu/gguf_quant.h:85-86
+ *   edgexpu_cuda_dot_quant_q8_dev     edgexpu_gguf_dot_quant_q8 / _q8k include/edgexpu/gguf_quant.h:90-102
+ *                                     (all rows of a tensor in one call)
  *   edgexpu_cuda_logits_argmax        greedy branch of sample_next_token src/native.c:2355-2400
  *                                     (chunk loop + logit_score src/native.c:500-514)
  *   edgexpu_cuda_upload_weight        per-token staging of load_qweight src/native.c:593-655,
@@ -90,6 +92,13 @@ int edgexpu_cuda_quantize_dev(uint32_t weight_type, const float *x, int m, int n
 
 int edgexpu_cuda_linear_quant_batch_dev(float *out, const float *x, const uint8_t *weight, uint32_t type,
                                         const float *bias, int m, int n_out, int n_in, void *stream);
+
+/* Rows of pre-quantized activations (xq: m rows of Q8_0 or Q8_K blocks, as from
+ * edgexpu_cuda_quantize_dev) against n_out weight rows: the batched counterpart of
+ * edgexpu_gguf_dot_quant_q8 / _q8k (include/edgexpu/gguf_quant.h:90-102) with the linear
+ * epilogue, out[t*n_out + o] = bias[o] + dot(W_o, xq_t). */
+int edgexpu_cuda_dot_quant_q8_dev(float *out, const uint8_t *xq, const uint8_t *weight, uint32_t type,
+                                  const float *bias, int m, int n_out, int n_in, void *stream);
 
 /* Writes the argmax key of rows [0, vocab) of `weight` into *key (device).  The key packs the
  * order-preserving bits of the best score (high word) and 0xFFFFFFFF - (row0 + row) (low
