@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "../../include/edgexpu_cuda.h"
+#include "capi_internal.h"
 #include "common.cuh"
 #include "launch.h"
 
@@ -524,3 +525,26 @@ int edgexpu_cuda_stream_sync(void* stream, char* error, size_t error_size) {
 }
 
 }  // extern "C"
+
+namespace ex {
+
+std::recursive_mutex& api_mutex() { return g_mu; }
+int api_ready(char* error, size_t error_size) { return need_ready(error, error_size); }
+int api_lookup(const uint8_t* weight, uint32_t type, int n_out, int n_in, char* error, size_t error_size) {
+  return lookup(weight, type, n_out, n_in, error, error_size);
+}
+int api_fail(char* error, size_t error_size, const char* fmt, ...) {
+  char msg[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(msg, sizeof msg, fmt, ap);
+  va_end(ap);
+  return fail(error, error_size, "%s", msg);
+}
+const DeviceInfo& api_device_info() { return g.info; }
+int api_device() { return g.device; }
+uint32_t* api_status_word() { return g.d_status; }
+size_t api_row_bytes(uint32_t type, int n) { return row_bytes_of(type, n); }
+size_t api_act_row_bytes(uint32_t type, int n) { return act_row_bytes_of(type, n); }
+
+}  // namespace ex

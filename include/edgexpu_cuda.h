@@ -93,6 +93,19 @@ int edgexpu_cuda_quantize_dev(uint32_t weight_type, const float *x, int m, int n
 int edgexpu_cuda_linear_quant_batch_dev(float *out, const float *x, const uint8_t *weight, uint32_t type,
                                         const float *bias, int m, int n_out, int n_in, void *stream);
 
+/* Same result as edgexpu_cuda_linear_quant_batch_dev, but the call allocates no memory: no
+ * cudaMalloc, no cudaFree, no allocating library routine.  It has no counterpart in the reference;
+ * it is for callers that cannot allocate once running -- code recorded into a CUDA graph, runtimes
+ * whose HBM budget is fixed at model load, and decode loops that must not risk the device-wide
+ * synchronisation an allocation or free can cause.  The quantized activations go to one fixed
+ * 1 MiB device array compiled into the library (held on every GPU that loads it until exit), so
+ * m * (quantized row bytes) must fit in 1 MiB (e.g. 224 rows of 4096 for Q4_K, 60 rows of 16384
+ * for Q8_0); larger batches are rejected with an error.  The first call on a device looks up the
+ * array's device address; make it before any stream capture.  All calls share the array, so calls
+ * whose GPU work overlaps (two streams at once) race and must be serialised by the caller. */
+int edgexpu_cuda_linear_quant_batch_noalloc(float *out, const float *x, const uint8_t *weight, uint32_t type,
+                                            const float *bias, int m, int n_out, int n_in, void *stream);
+
 /* Rows of pre-quantized activations (xq: m rows of Q8_0 or Q8_K blocks, as from
  * edgexpu_cuda_quantize_dev) against n_out weight rows: the batched counterpart of
  * edgexpu_gguf_dot_quant_q8 / _q8k (include/edgexpu/gguf_quant.h:90-102) with the linear
