@@ -45,6 +45,7 @@ PEAKS = ROOT / "MEASURED_PEAKS.json"
 TRAFFIC = ROOT / "profiles" / "traffic.json"
 
 TYPE_Q8_0, TYPE_Q4_K = 8, 12
+GROUP_WITH_PREV = {"attn_k", "attn_v", "ffn_up"}  # read the same activations as the projection before
 FALLBACK_HBM_GBS = 6650.0
 
 WORKLOADS = {
@@ -334,6 +335,22 @@ def run_ours(args, wl):
             h = pkg.register_weight(buf, t, n_out, n_in)
             lay.append((label, n_out, n_in, kind, buf, h))
         layers.append(lay)
+    # Launch groups of one layer: projections that read the same activations go in one launch
+    # (q|k|v and gate|up); o and down each follow their own input.
+    groups = []
+    for i, (label, n_out, n_in, kind) in enumerate(shapes):
+        if groups and label in GROUP_WITH_PREV and shapes[groups[-1][-1]][3] == "row" and kind == "row":
+            groups[-1].append(i)
+        else:
+            groups.append([i])
+    P = ctypes.c_void_p * 4
+    I4 = ctypes.c_int * 4
+    group_args = []  # per layer, per group: ctypes arrays for the multi-tensor call
+    for lay in layers:
+        ga = []
+        for grp in groups:
+            ga.append((len(grp), P(), P(*[lay[i][5] for i in grp]), I4(*[lay[i][1] for i in grp]), grp))
+        group_args.append(ga)
     lbuf = synth.torch_weight(t, nv, wl["hidden"], gen, dev)
     lh = pkg.register_weight(lbuf, t, nv, wl["hidden"])
 
@@ -343,6 +360,10 @@ def run_ours(args, wl):
         if n_in not in ins:
             ins[n_in] = torch.randn((m, n_in), generator=gen, device=dev, dtype=torch.float32)
     outs = {label: torch.empty((m, n_out), device=dev, dtype=torch.float32) for label, n_out, _, _ in shapes}
+    for ga in group_args:
+        for n_t, out_arr, _w, _n, grp in ga:
+            for j, i in enumerate(grp):
+                out_arr[j] = outs[shapes[i][0]].data_ptr()
     hidden = torch.randn(wl["hidden"], generator=gen, device=dev, dtype=torch.float32)
     keys = torch.zeros(max(1, m), device=dev, dtype=torch.int64)
     sign = torch.tensor(-(2 ** 63), device=dev, dtype=torch.int64)
@@ -350,17 +371,24 @@ def run_ours(args, wl):
     for n_in in ins:
         assert cuda.edgexpu_cuda_reserve(m, n_in, buf, 512), buf.value
 
-    def enqueue_step():
-        st = torch.cuda.current_stream().cuda_stream
-        for lay in layers:
-            for label, n_out, n_in, kind, _b, h in lay:
-                o = outs[label]
-                ok = cuda.edgexpu_cuda_linear_quant_batch_dev(o.data_ptr(), ins[n_in].data_ptr(), h, t, None, m, n_out,
-                                                              n_in, st)
+    def enqueue_gemvs(st, collectives):
+        for lay, ga in zip(layers, group_args):
+            for n_t, out_arr, w_arr, n_arr, grp in ga:
+                label, n_out, n_in, kind = shapes[grp[0]]
+                if n_t == 1:
+                    ok = cuda.edgexpu_cuda_linear_quant_batch_dev(out_arr[0], ins[n_in].data_ptr(), w_arr[0], t, None, m,
+                                                                  n_out, n_in, st)
+                else:
+                    ok = cuda.edgexpu_cuda_linear_quant_multi_dev(n_t, out_arr, w_arr, n_arr, None, t,
+                                                                  ins[n_in].data_ptr(), m, n_in, st)
                 if not ok:
                     raise RuntimeError(cuda.edgexpu_cuda_last_error().decode())
-                if tp and kind == "col":
-                    dist.all_reduce(o)
+                if collectives and tp and kind == "col":
+                    dist.all_reduce(outs[label])
+
+    def enqueue_step():
+        st = torch.cuda.current_stream().cuda_stream
+        enqueue_gemvs(st, True)
         for i in range(m):
             if not cuda.edgexpu_cuda_logits_argmax_dev(lh, t, hidden.data_ptr(), wl["hidden"], nv, None, v0,
                                                        keys[i:].data_ptr(), st):
@@ -432,28 +460,26 @@ def run_ours(args, wl):
     total_bytes = step_bytes(wl, m) * (1 if tp else world)
     value_gbs = total_bytes * args.steps / (ms_max / 1e3) / 1e9
 
-    # Roofline of the dominant kernel (the row-stream GEMV): time each launch of one step's
-    # projections with events on the launching stream, activations pre-quantized.
-    st = torch.cuda.current_stream().cuda_stream
-    xq = {n_in: torch.empty(m * act_bytes(t, n_in) + 64, dtype=torch.uint8, device=dev) for n_in in ins}
-    for n_in in ins:
-        assert cuda.edgexpu_cuda_quantize_dev(t, ins[n_in].data_ptr(), m, n_in, xq[n_in].data_ptr(), st)
-    evs = []
-    launch_bytes = []
+    # Roofline of the dominant kernel (the row-stream GEMV): the step's GEMV launches alone (no
+    # collectives, no logits) captured in one graph and timed with events on its stream.
+    g_k = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_k, stream=cap_stream):
+        enqueue_gemvs(torch.cuda.current_stream().cuda_stream, False)
+    for _ in range(3):
+        g_k.replay()
     torch.cuda.synchronize()
-    torch.cuda._sleep(200_000_000)  # ~0.1 s spin: every launch below is queued before the GPU reaches it
-    for lay in layers:
-        for label, n_out, n_in, kind, _b, h in lay:
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            assert cuda.edgexpu_cuda_dot_quant_q8_dev(outs[label].data_ptr(), xq[n_in].data_ptr(), h, t, None, m,
-                                                      n_out, n_in, st)
-            b.record()
-            evs.append((a, b))
-            launch_bytes.append(n_out * row_bytes(t, n_in) + m * (act_bytes(t, n_in) + 4 * n_out))
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k_reps = max(3, min(args.steps, 20))
+    ka.record()
+    for _ in range(k_reps):
+        g_k.replay()
+    kb.record()
     torch.cuda.synchronize()
-    kern_ms = [a.elapsed_time(b) for a, b in evs]
-    achieved = sum(launch_bytes) / (sum(kern_ms) / 1e3) / 1e9
+    kern_s = ka.elapsed_time(kb) / 1e3 / k_reps
+    kern_launches = wl["layers"] * len(groups)
+    kern_bytes = wl["layers"] * sum(linear_alg_bytes(t, n_out, n_in, m) for _, n_out, n_in, _k in shapes)
+    achieved = kern_bytes / kern_s / 1e9
+    del g_k
     peak, peak_kind = peak_hbm()
     traffic = None
     try:
@@ -523,7 +549,7 @@ def run_ours(args, wl):
         except FileNotFoundError as e:
             cpu_baseline = {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
 
-    launches_per_step = wl["layers"] * len(shapes) * 2 + m * (2 if t == TYPE_Q8_0 else 1)
+    launches_per_step = wl["layers"] * len(groups) + m  # one GEMV launch per group + the logits kernel
     line = {
         "metric": f"{'Q4_K' if t == TYPE_Q4_K else 'Q8_0'} GEMV HBM GB/s ({args.workload}, batch {m})",
         "value": round(value_gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -538,7 +564,8 @@ def run_ours(args, wl):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "rowstream GEMV (Q4_K x Q8_K)" if t == TYPE_Q4_K else "rowstream GEMV (Q8_0 x Q8_0)",
-                     "launches": len(kern_ms), "peak_source": f"{peak_kind} hbm_gbs"},
+                     "launches": kern_launches, "avg_launch_us": round(kern_s / kern_launches * 1e6, 3),
+                     "peak_source": f"{peak_kind} hbm_gbs"},
         "cpu_baseline": cpu_baseline,
         "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "edgexpu_cpu_linear_quant_batch + edgexpu_b200_logits_greedy (host buffers)"},
@@ -623,21 +650,28 @@ def run_gemv(args):
     nbytes = linear_alg_bytes(t, n_out, n_in, m)
     value = nbytes * args.steps / (ms / 1e3) / 1e9
 
-    # GEMV kernel alone (activations pre-quantized), one event pair per launch.
+    # GEMV kernel alone (activations pre-quantized): a graph of launches over the weight copies,
+    # timed with events on its stream (single event pairs are too coarse for microsecond kernels).
     st = torch.cuda.current_stream().cuda_stream
     xq = torch.empty(m * act_bytes(t, n_in) + 64, dtype=torch.uint8, device=dev)
     assert cuda.edgexpu_cuda_quantize_dev(t, x.data_ptr(), m, n_in, xq.data_ptr(), st)
     torch.cuda.synchronize()
-    torch.cuda._sleep(200_000_000)
-    evs = []
-    for i in range(min(copies, 64)):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        assert cuda.edgexpu_cuda_dot_quant_q8_dev(out.data_ptr(), xq.data_ptr(), h0 + i * wb, t, None, m, n_out, n_in, st)
-        b.record()
-        evs.append((a, b))
+    n_k = max(args.steps, copies)
+    g_k = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_k, stream=cap):
+        sk = torch.cuda.current_stream().cuda_stream
+        for i in range(n_k):
+            assert cuda.edgexpu_cuda_dot_quant_q8_dev(out.data_ptr(), xq.data_ptr(), h0 + (i % copies) * wb, t, None, m,
+                                                      n_out, n_in, sk)
+    g_k.replay()
     torch.cuda.synchronize()
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    ka, kb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ka.record()
+    g_k.replay()
+    kb.record()
+    torch.cuda.synchronize()
+    kern_ms = ka.elapsed_time(kb) / n_k
+    del g_k
     kbytes = wb + m * (act_bytes(t, n_in) + 4 * n_out)
     achieved = kbytes / (kern_ms / 1e3) / 1e9
     peak, peak_kind = peak_hbm()

@@ -52,6 +52,8 @@ _CUDA_SIGS = {
         _c_int, [_c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp, ctypes.POINTER(_c_u32), _c_f32p, _c_str, _c_sz]),
     "edgexpu_cuda_quantize_dev": (_c_int, [_c_u32, _c_vp, _c_int, _c_int, _c_vp, _c_vp]),
     "edgexpu_cuda_linear_quant_batch_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int, _c_vp]),
+    "edgexpu_cuda_linear_quant_multi_dev": (
+        _c_int, [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp]),
     "edgexpu_cuda_linear_quant_batch_noalloc": (
         _c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int, _c_vp]),
     "edgexpu_cuda_dot_quant_q8_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int, _c_vp]),

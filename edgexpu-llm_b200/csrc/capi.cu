@@ -469,6 +469,53 @@ int edgexpu_cuda_linear_quant_batch_dev(float* out, const float* x, const uint8_
   return run_linear_dev(out, x, weight, type, bias, m, n_out, n_in, pick(stream), nullptr, 0);
 }
 
+int edgexpu_cuda_linear_quant_multi_dev(int n, float* const* outs, const uint8_t* const* weights, const int* n_outs,
+                                        const float* const* biases, uint32_t type, const float* x, int m, int n_in,
+                                        void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(nullptr, 0)) return 0;
+  if (n < 1 || n > ex::MAX_SEGS || outs == nullptr || weights == nullptr || n_outs == nullptr || x == nullptr || m <= 0 ||
+      n_in <= 0)
+    return fail(nullptr, 0, "multi linear: invalid arguments (1..%d tensors)", ex::MAX_SEGS);
+  for (int i = 0; i < n; ++i) {
+    if (outs[i] == nullptr || n_outs[i] <= 0) return fail(nullptr, 0, "multi linear: invalid tensor %d", i);
+    if (!lookup(weights[i], type, n_outs[i], n_in, nullptr, 0)) return 0;
+  }
+  cudaStream_t st = pick(stream);
+  const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  const size_t qb = act_row_bytes_of(type, n_in);
+  const bool fused = ex::rowstream_quantizes_itself(fmt, m);
+  const uint8_t* act = reinterpret_cast<const uint8_t*>(x);
+  if (!fused) {
+    if (!grow_dev(g.xq, static_cast<size_t>(m) * qb + 64, st, nullptr, 0)) return 0;
+    EX_CUDA(type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n_in, static_cast<uint8_t*>(g.xq.p), st)
+                                  : ex::launch_quantize_q8_k(x, m, n_in, static_cast<uint8_t*>(g.xq.p), st),
+            nullptr, 0);
+    act = static_cast<const uint8_t*>(g.xq.p);
+  }
+  const size_t stride = fused ? static_cast<size_t>(n_in) * 4 : qb;
+  const int max_m = ex::rowstream_max_m(fmt, n_in, g.info);
+  if (max_m <= 0) return fail(nullptr, 0, "n_in %d too large for the shared-memory activation tile", n_in);
+  for (int t0 = 0; t0 < m; t0 += max_m) {
+    ex::RowStreamArgs a{};
+    a.fmt = fmt;
+    a.mode = ex::RowOut::Store;
+    a.row_bytes = static_cast<int>(row_bytes_of(type, n_in));
+    a.K = n_in;
+    a.m = std::min(max_m, m - t0);
+    a.act = act + static_cast<size_t>(t0) * stride;
+    a.act_row_bytes = static_cast<int>(qb);
+    a.act_f32 = fused;
+    a.status = g.d_status;
+    a.n_seg = n;
+    for (int i = 0; i < n; ++i)
+      a.seg[i] = ex::RowSeg{weights[i], n_outs[i], biases != nullptr ? biases[i] : nullptr,
+                            outs[i] + static_cast<size_t>(t0) * n_outs[i], 0};
+    EX_CUDA(ex::launch_rowstream(a, g.info, st), nullptr, 0);
+  }
+  return 1;
+}
+
 int edgexpu_cuda_dot_quant_q8_dev(float* out, const uint8_t* xq, const uint8_t* weight, uint32_t type, const float* bias,
                                   int m, int n_out, int n_in, void* stream) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);

@@ -25,6 +25,17 @@ enum class Fmt : int {
   Q4_KxF32 = 2,   // Q4_K weight . fp32 activation   (gguf_quant.c:704-752, logits path)
 };
 
+// One weight tensor of a grouped launch: the segments share K, the weight type and the
+// activations, and each writes its own output (row stride = its n_rows).
+struct RowSeg {
+  const uint8_t* w;
+  long long n_rows;
+  const float* bias;
+  float* out;
+  long long tile0;        // first tile of this segment (filled by launch_rowstream)
+};
+constexpr int MAX_SEGS = 4;
+
 struct RowStreamArgs {
   Fmt fmt;
   RowOut mode;
@@ -43,6 +54,8 @@ struct RowStreamArgs {
   unsigned long long* key;  // Argmax
   int32_t* partials;      // Partials: Q8_0 [m][n_rows][nb]; Q4_K [m][n_rows][nb][2] (sumi, summ)
   uint32_t* status;       // device-visible status word
+  int n_seg;              // 0: one tensor (w, n_rows, bias, out, out_stride); 1..MAX_SEGS: seg[] (Store only)
+  RowSeg seg[MAX_SEGS];
 };
 
 struct DeviceInfo {

@@ -44,6 +44,7 @@ constexpr int ACT_BUDGET = 96 * 1024;
 constexpr int STAGE_SLACK = 48;       // alignment round-down (<16) + over-read of the last block
 constexpr int MAX_M = 8;              // activation rows (tokens) per launch; the host splits more
 constexpr int PROLOGUE_QUANT_MAX_M = 2;
+constexpr int PRO_BATCH = 4;          // activation blocks a consumer warp loads before quantizing them
 
 struct Layout {
   int tile_rows;
@@ -85,7 +86,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
     if ((i & 31u) == 0) {
       if (*abort_flag) return false;
       if (global_ns() - t0 > WAIT_LIMIT_NS) return false;
@@ -101,19 +102,35 @@ __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct) {
   if (a.fmt == Fmt::Q8_0xQ8_0) {
     int4* xq = reinterpret_cast<int4*>(act);
     float* xd = reinterpret_cast<float*>(act + m * U * 32);
-    if (a.act_f32) {  // quantize in place: one warp per block (quant.cuh)
+    if (a.act_f32) {  // quantize in place: one warp per block (quant.cuh), loads of a batch issued first
       const float* x = static_cast<const float*>(a.act);
-      for (int blk = cw; blk < m * U; blk += CONSUMER_WARPS) {
-        const int t = blk / U, b = blk - t * U;
-        uint32_t dbits;
-        const int q = warp_q8_0(x[static_cast<size_t>(t) * K + b * QK8_0 + lane], &dbits);
-        // lane i holds element i: gather 4 consecutive lanes into one word
-        const int q1 = __shfl_down_sync(0xFFFFFFFFu, q, 1), q2 = __shfl_down_sync(0xFFFFFFFFu, q, 2),
-                  q3 = __shfl_down_sync(0xFFFFFFFFu, q, 3);
-        if ((lane & 3) == 0) {
-          reinterpret_cast<uint32_t*>(xq + (t * 2 + (lane >> 4)) * U + b)[(lane >> 2) & 3] = pack4_i8(q, q1, q2, q3);
+      const int nblk = m * U;
+      for (int base = cw; base < nblk; base += PRO_BATCH * CONSUMER_WARPS) {
+        float v[PRO_BATCH];
+#pragma unroll
+        for (int k = 0; k < PRO_BATCH; ++k) {
+          const int blk = base + k * CONSUMER_WARPS;
+          if (blk < nblk) {
+            const int t = blk / U, b = blk - t * U;
+            v[k] = x[static_cast<size_t>(t) * K + b * QK8_0 + lane];
+          }
         }
-        if (lane == 0) xd[t * U + b] = fp16_bits_to_float(dbits);
+#pragma unroll
+        for (int k = 0; k < PRO_BATCH; ++k) {
+          const int blk = base + k * CONSUMER_WARPS;
+          if (blk < nblk) {  // warp-uniform
+            const int t = blk / U, b = blk - t * U;
+            uint32_t dbits;
+            const int q = warp_q8_0(v[k], &dbits);
+            // lane i holds element i: gather 4 consecutive lanes into one word
+            const int q1 = __shfl_down_sync(0xFFFFFFFFu, q, 1), q2 = __shfl_down_sync(0xFFFFFFFFu, q, 2),
+                      q3 = __shfl_down_sync(0xFFFFFFFFu, q, 3);
+            if ((lane & 3) == 0) {
+              reinterpret_cast<uint32_t*>(xq + (t * 2 + (lane >> 4)) * U + b)[(lane >> 2) & 3] = pack4_i8(q, q1, q2, q3);
+            }
+            if (lane == 0) xd[t * U + b] = fp16_bits_to_float(dbits);
+          }
+        }
       }
     } else {  // pre-quantized GGUF Q8_0 rows: 17 half-words per 34-byte block
       const uint8_t* src = static_cast<const uint8_t*>(a.act);
@@ -134,23 +151,40 @@ __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct) {
     int4* xq = reinterpret_cast<int4*>(act);
     int* xb = reinterpret_cast<int*>(act + m * U * 128);
     float* xd = reinterpret_cast<float*>(act + m * U * 128 + m * U * 16);
-    if (a.act_f32) {  // quantize in place: one warp per 256-block (quant.cuh)
+    if (a.act_f32) {  // quantize in place: one warp per 256-block (quant.cuh), loads of a batch issued first
       const float* x = static_cast<const float*>(a.act);
-      for (int blk = cw; blk < m * nb; blk += CONSUMER_WARPS) {
-        const int t = blk / nb, sb = blk - t * nb;
-        const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * K + sb * QK_K + lane * 8);
-        const float4 v0 = src[0], v1 = src[1];
-        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        int q[8], gsum;
-        const float d = warp_q8_k(v, q, &gsum);
-        // lane l holds elements 8l..8l+7: unit h = l/16, chunk j = (l%16)/2, half (l&1)
-        const int u = 2 * sb + (lane >> 4), j = (lane & 15) >> 1;
-        uint2* dst = reinterpret_cast<uint2*>(xq + (t * 8 + j) * U + u) + (lane & 1);
-        *dst = make_uint2(pack4_i8(q[0], q[1], q[2], q[3]), pack4_i8(q[4], q[5], q[6], q[7]));
-        // sub-block (32 elements) sums: lanes 4s .. 4s+3 (gsum already covers lane pairs)
-        const int s32 = gsum + __shfl_down_sync(0xFFFFFFFFu, gsum, 2);
-        if ((lane & 3) == 0) xb[(t * U + u) * 4 + ((lane >> 2) & 3)] = s32;
-        if (lane == 0) xd[t * nb + sb] = d;
+      const int nblk = m * nb;
+      for (int base = cw; base < nblk; base += PRO_BATCH * CONSUMER_WARPS) {
+        float4 ld[PRO_BATCH][2];
+#pragma unroll
+        for (int k = 0; k < PRO_BATCH; ++k) {
+          const int blk = base + k * CONSUMER_WARPS;
+          if (blk < nblk) {
+            const int t = blk / nb, sb = blk - t * nb;
+            const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * K + sb * QK_K + lane * 8);
+            ld[k][0] = src[0];
+            ld[k][1] = src[1];
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < PRO_BATCH; ++k) {
+          const int blk = base + k * CONSUMER_WARPS;
+          if (blk < nblk) {  // warp-uniform
+            const int t = blk / nb, sb = blk - t * nb;
+            const float v[8] = {ld[k][0].x, ld[k][0].y, ld[k][0].z, ld[k][0].w,
+                                ld[k][1].x, ld[k][1].y, ld[k][1].z, ld[k][1].w};
+            int q[8], gsum;
+            const float d = warp_q8_k(v, q, &gsum);
+            // lane l holds elements 8l..8l+7: unit h = l/16, chunk j = (l%16)/2, half (l&1)
+            const int u = 2 * sb + (lane >> 4), j = (lane & 15) >> 1;
+            uint2* dst = reinterpret_cast<uint2*>(xq + (t * 8 + j) * U + u) + (lane & 1);
+            *dst = make_uint2(pack4_i8(q[0], q[1], q[2], q[3]), pack4_i8(q[4], q[5], q[6], q[7]));
+            // sub-block (32 elements) sums: lanes 4s .. 4s+3 (gsum already covers lane pairs)
+            const int s32 = gsum + __shfl_down_sync(0xFFFFFFFFu, gsum, 2);
+            if ((lane & 3) == 0) xb[(t * U + u) * 4 + ((lane >> 2) & 3)] = s32;
+            if (lane == 0) xd[t * nb + sb] = d;
+          }
+        }
       }
     } else {  // pre-quantized GGUF Q8_K rows: 73 words per 292-byte block
       const uint8_t* src = static_cast<const uint8_t*>(a.act);
@@ -204,11 +238,40 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Activations of one lane's work unit held in registers for the whole kernel.  Used when a
+// single token is streamed and a row fits in one warp pass (U <= 32: Q8_0 K <= 1024, Q4_K K <= 4096):
+// the lane then owns the same unit in every row, so its activation chunks never change.
+struct XRegs {
+  int4 q[8];  // Q8_K: the unit's 8 chunks; Q8_0: q[0..1]
+  int4 b;     // Q8_K: bsums of the unit's 4 sub-blocks
+  float d;    // activation scale of the unit's block
+};
+
+__device__ __forceinline__ void load_xregs(Fmt f, const RowStreamArgs& a, const uint8_t* act, int lane, XRegs& xr) {
+  const int U = units_per_row(f, a.K);
+  xr.b = make_int4(0, 0, 0, 0);
+  xr.d = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) xr.q[j] = make_int4(0, 0, 0, 0);
+  if (lane >= U) return;
+  const int4* xq = reinterpret_cast<const int4*>(act);
+  if (f == Fmt::Q8_0xQ8_0) {
+    xr.q[0] = xq[lane];
+    xr.q[1] = xq[U + lane];
+    xr.d = reinterpret_cast<const float*>(act + U * 32)[lane];
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xr.q[j] = xq[j * U + lane];
+    xr.b = reinterpret_cast<const int4*>(act + U * 128)[lane];
+    xr.d = reinterpret_cast<const float*>(act + U * 128 + U * 16)[lane >> 1];
+  }
+}
+
 // Q8_0 weight row x Q8_0 activations.  Blocks are 34 B, so inside the stage they are only
 // 2-byte aligned: read the 9 covering words and realign.
-template <RowOut MODE, int MTOK>
+template <RowOut MODE, int MTOK, bool XREG>
 __device__ __forceinline__ void row_q8_0(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
-                                         long long row, float (&acc)[MTOK], int lane) {
+                                         long long row, float (&acc)[MTOK], int lane, const XRegs& xr) {
   const int U = a.K / QK8_0;
   const int4* xq = reinterpret_cast<const int4*>(act);
   const float* xd = reinterpret_cast<const float*>(act + a.m * U * 32);
@@ -227,7 +290,7 @@ __device__ __forceinline__ void row_q8_0(const RowStreamArgs& a, const uint8_t* 
 #pragma unroll
     for (int t = 0; t < MTOK; ++t) {
       if (MTOK == 1 || t < a.m) {
-        const int4 x0 = xq[(t * 2) * U + b], x1 = xq[(t * 2 + 1) * U + b];
+        const int4 x0 = XREG ? xr.q[0] : xq[(t * 2) * U + b], x1 = XREG ? xr.q[1] : xq[(t * 2 + 1) * U + b];
         int ip = dp4a(q[0], x0.x, 0);
         ip = dp4a(q[1], x0.y, ip);
         ip = dp4a(q[2], x0.z, ip);
@@ -239,7 +302,7 @@ __device__ __forceinline__ void row_q8_0(const RowStreamArgs& a, const uint8_t* 
         if constexpr (MODE == RowOut::Partials) {
           a.partials[(static_cast<size_t>(t) * a.n_rows + row) * U + b] = ip;
         } else {
-          acc[t] += (dw * xd[t * U + b]) * static_cast<float>(ip);  // gguf_dot_q8.c:475-476
+          acc[t] += (dw * (XREG ? xr.d : xd[t * U + b])) * static_cast<float>(ip);  // gguf_dot_q8.c:475-476
         }
       }
     }
@@ -279,9 +342,9 @@ __device__ __forceinline__ void q4k_load_half(const uint8_t* rowp, int sb, int h
 // combined in int32 before the float step, so every per-block (sumi, summ) equals the
 // reference's int32 values.  High nibbles are used in place (byte & 0xF0 = 16*q) with an
 // unsigned-by-signed dp4a and the exact sum is shifted down by 4 afterwards.
-template <RowOut MODE, int MTOK>
+template <RowOut MODE, int MTOK, bool XREG>
 __device__ __forceinline__ void row_q4k_q8k(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
-                                            long long row, float (&acc)[MTOK], int lane) {
+                                            long long row, float (&acc)[MTOK], int lane, const XRegs& xr) {
   const int U = a.K / 128, nb = U / 2;
   const int4* xq = reinterpret_cast<const int4*>(act);
   const int4* xb = reinterpret_cast<const int4*>(act + a.m * U * 128);
@@ -306,7 +369,7 @@ __device__ __forceinline__ void row_q4k_q8k(const RowStreamArgs& a, const uint8_
           int ip[4] = {0, 0, 0, 0};
 #pragma unroll
           for (int j = 0; j < 8; ++j) {  // chunk j: group g = j/4; j%4 < 2 low nibbles, else high
-            const int4 x = xq[(t * 8 + j) * U + u];
+            const int4 x = XREG ? xr.q[j] : xq[(t * 8 + j) * U + u];
             const int g = j >> 2, c = j & 1;
             const uint32_t* w = qw + 8 * g + 4 * c;
             if ((j & 2) == 0) {
@@ -323,7 +386,7 @@ __device__ __forceinline__ void row_q4k_q8k(const RowStreamArgs& a, const uint8_
           }
           ip[1] >>= 4;  // exact: the sums of 16*q*x are multiples of 16
           ip[3] >>= 4;
-          const int4 bs = xb[t * U + u];
+          const int4 bs = XREG ? xr.b : xb[t * U + u];
           sumi = static_cast<int>(sc4 & 0xFFu) * ip[0] + static_cast<int>((sc4 >> 8) & 0xFFu) * ip[1] +
                  static_cast<int>((sc4 >> 16) & 0xFFu) * ip[2] + static_cast<int>(sc4 >> 24) * ip[3];
           summ = static_cast<int>(mn4 & 0xFFu) * bs.x + static_cast<int>((mn4 >> 8) & 0xFFu) * bs.y +
@@ -338,7 +401,7 @@ __device__ __forceinline__ void row_q4k_q8k(const RowStreamArgs& a, const uint8_
             pp[1] = summ;
           } else {
             // gguf_dot_q8.c:619-620, :640, :661: d = d_x*d_w and dmin = -d_x*dmin_w per super-block.
-            const float dx = xd[t * nb + sb];
+            const float dx = XREG ? xr.d : xd[t * nb + sb];
             acc[t] += (dx * dw) * static_cast<float>(sumi) - (dx * dmw) * static_cast<float>(summ);
           }
         }
@@ -399,7 +462,33 @@ __device__ __forceinline__ void row_q4k_f32(const RowStreamArgs& a, const uint8_
 
 // ---- the kernel ---------------------------------------------------------------------------------
 
-template <Fmt F, RowOut MODE, int MTOK>
+// Tile -> (segment, first row, rows, weight base, output, bias, output stride).
+struct TileRef {
+  const uint8_t* w;
+  const float* bias;
+  float* out;
+  long long stride;
+  long long r0;
+  int nr;
+};
+
+__device__ __forceinline__ TileRef tile_ref(const RowStreamArgs& a, const Layout& L, long long tile) {
+  int s = 0;
+#pragma unroll
+  for (int i = 1; i < MAX_SEGS; ++i)
+    if (i < a.n_seg && tile >= a.seg[i].tile0) s = i;
+  const RowSeg& g = a.seg[s];
+  TileRef t;
+  t.w = g.w;
+  t.bias = g.bias;
+  t.out = g.out;
+  t.stride = a.n_seg > 1 ? g.n_rows : a.out_stride;
+  t.r0 = (tile - g.tile0) * L.tile_rows;
+  t.nr = static_cast<int>(min(static_cast<long long>(L.tile_rows), g.n_rows - t.r0));
+  return t;
+}
+
+template <Fmt F, RowOut MODE, int MTOK, bool XREG>
 __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamArgs a, const Layout L) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -408,10 +497,13 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = L.n_stages;
 
+  // Tile slot r belongs to consumer warp (it*R + r) % CONSUMER_WARPS, so min(R, CONSUMER_WARPS)
+  // warps release each stage.
+  const int R = L.tile_rows;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], CONSUMER_WARPS);
+      mbar_init(&empty[s], R < CONSUMER_WARPS ? R : CONSUMER_WARPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -436,11 +528,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
           break;
         }
       }
-      const long long r0 = tile * L.tile_rows;
-      const long long nr = min(static_cast<long long>(L.tile_rows), a.n_rows - r0);
-      const uintptr_t start = reinterpret_cast<uintptr_t>(a.w) + static_cast<uintptr_t>(r0) * a.row_bytes;
+      const TileRef tr = tile_ref(a, L, tile);
+      const uintptr_t start = reinterpret_cast<uintptr_t>(tr.w) + static_cast<uintptr_t>(tr.r0) * a.row_bytes;
       const uintptr_t al = start & ~static_cast<uintptr_t>(15);
-      const uint32_t bytes = static_cast<uint32_t>((start - al + nr * a.row_bytes + 15) & ~15ull);
+      const uint32_t bytes = static_cast<uint32_t>((start - al + static_cast<long long>(tr.nr) * a.row_bytes + 15) & ~15ull);
       mbar_arrive_expect_tx(&full[s], bytes);
       bulk_g2s(smem + L.stage_off + s * L.stage_bytes, reinterpret_cast<const void*>(al), bytes, &full[s], pol);
       if (++s == S) {
@@ -462,59 +553,66 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   load_act(a, act, threadIdx.x - 32);
   named_bar_sync(1, CONSUMERS);
 
+  XRegs xr;
+  if constexpr (XREG) load_xregs(F, a, act, lane, xr);
+
   unsigned long long best = 0ull;
   bool dead = false;
   int s = 0;
   uint32_t fphase = 0;
-  int first = cw;  // row of the current tile that belongs to this warp (round-robin over the CTA's rows)
+  const int step = R % CONSUMER_WARPS;
+  int first = cw;  // first slot of this warp in the current tile: (cw - it*R) mod CONSUMER_WARPS
   for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
-    if (!dead && !wait_or_abort(&full[s], fphase, abort_flag)) {
-      atomicOr(a.status, ST_TIMEOUT_FULL);
-      *abort_flag = 1;
-      dead = true;
-    }
-    const long long r0 = tile * L.tile_rows;
-    const int nr = static_cast<int>(min(static_cast<long long>(L.tile_rows), a.n_rows - r0));
-    if (!dead) {
-      const uintptr_t start = reinterpret_cast<uintptr_t>(a.w) + static_cast<uintptr_t>(r0) * a.row_bytes;
-      const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + (start & 15u);
-      for (int r = first; r < nr; r += CONSUMER_WARPS) {
-        float acc[MTOK];
+    if (first < R) {  // this warp owns at least one slot of the tile
+      if (!dead && !wait_or_abort(&full[s], fphase, abort_flag)) {
+        atomicOr(a.status, ST_TIMEOUT_FULL);
+        *abort_flag = 1;
+        dead = true;
+      }
+      if (!dead) {
+        const TileRef tr = tile_ref(a, L, tile);
+        const long long r0 = tr.r0;
+        const uintptr_t start = reinterpret_cast<uintptr_t>(tr.w) + static_cast<uintptr_t>(r0) * a.row_bytes;
+        const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + (start & 15u);
+        for (int r = first; r < tr.nr; r += CONSUMER_WARPS) {
+          float acc[MTOK];
 #pragma unroll
-        for (int t = 0; t < MTOK; ++t) acc[t] = 0.0f;
-        const uint8_t* rowp = tb + static_cast<size_t>(r) * a.row_bytes;
-        if constexpr (F == Fmt::Q8_0xQ8_0) {
-          row_q8_0<MODE, MTOK>(a, act, rowp, r0 + r, acc, lane);
-        } else if constexpr (F == Fmt::Q4_KxQ8_K) {
-          row_q4k_q8k<MODE, MTOK>(a, act, rowp, r0 + r, acc, lane);
-        } else {
-          row_q4k_f32<MODE, MTOK>(a, act, rowp, acc, lane);
-        }
-        if constexpr (MODE != RowOut::Partials) {
-          const long long row = r0 + r;
-          float mine = 0.0f;
-#pragma unroll
-          for (int t = 0; t < MTOK; ++t) {
-            if (MTOK == 1 || t < a.m) {
-              const float v = warp_sum(acc[t]);
-              if (lane == t) mine = v;
-            }
+          for (int t = 0; t < MTOK; ++t) acc[t] = 0.0f;
+          const uint8_t* rowp = tb + static_cast<size_t>(r) * a.row_bytes;
+          if constexpr (F == Fmt::Q8_0xQ8_0) {
+            row_q8_0<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
+          } else if constexpr (F == Fmt::Q4_KxQ8_K) {
+            row_q4k_q8k<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
+          } else {
+            row_q4k_f32<MODE, MTOK>(a, act, rowp, acc, lane);
           }
-          if (lane < a.m) {
-            const float y = (a.bias != nullptr ? a.bias[row] : 0.0f) + mine;  // cpu_kernel.c:596-597
-            if constexpr (MODE == RowOut::Store) {
-              a.out[static_cast<size_t>(lane) * a.out_stride + row] = y;
-            } else {
-              const unsigned long long k = argmax_key(y, static_cast<uint32_t>(a.row0 + row));
-              best = k > best ? k : best;
+          if constexpr (MODE != RowOut::Partials) {
+            const long long row = r0 + r;
+            float mine = 0.0f;
+#pragma unroll
+            for (int t = 0; t < MTOK; ++t) {
+              if (MTOK == 1 || t < a.m) {
+                const float v = warp_sum(acc[t]);
+                if (lane == t) mine = v;
+              }
+            }
+            if (lane < a.m) {
+              const float y = (tr.bias != nullptr ? tr.bias[row] : 0.0f) + mine;  // cpu_kernel.c:596-597
+              if constexpr (MODE == RowOut::Store) {
+                tr.out[static_cast<size_t>(lane) * tr.stride + row] = y;
+              } else {
+                const unsigned long long k = argmax_key(y, static_cast<uint32_t>(a.row0 + row));
+                best = k > best ? k : best;
+              }
             }
           }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    first = ((first - nr) % CONSUMER_WARPS + CONSUMER_WARPS) % CONSUMER_WARPS;
+    first -= step;
+    if (first < 0) first += CONSUMER_WARPS;
     if (++s == S) {
       s = 0;
       fphase ^= 1u;
@@ -530,10 +628,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   }
 }
 
-template <Fmt F, RowOut MODE, int MTOK>
+template <Fmt F, RowOut MODE, int MTOK, bool XREG = false>
 cudaError_t launch_impl(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
   static int configured_smem = 0;  // per instantiation; the host API serialises its callers
-  auto kern = rowstream_kernel<F, MODE, MTOK>;
+  auto kern = rowstream_kernel<F, MODE, MTOK, XREG>;
   if (L.smem_total > configured_smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_total);
     if (e != cudaSuccess) return e;
@@ -554,6 +652,9 @@ cudaError_t launch_impl(const RowStreamArgs& a, const Layout& L, int grid, cudaS
 
 template <Fmt F, RowOut MODE>
 cudaError_t launch_mtok(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
+  if constexpr (F != Fmt::Q4_KxF32) {
+    if (a.m == 1 && units_per_row(F, a.K) <= 32) return launch_impl<F, MODE, 1, true>(a, L, grid, st);
+  }
   if (a.m <= 1) return launch_impl<F, MODE, 1>(a, L, grid, st);
   if (a.m <= 2) return launch_impl<F, MODE, 2>(a, L, grid, st);
   if (a.m <= 4) return launch_impl<F, MODE, 4>(a, L, grid, st);
@@ -571,7 +672,16 @@ int rowstream_max_m(Fmt fmt, int K, const DeviceInfo& dev) {
 
 bool rowstream_quantizes_itself(Fmt fmt, int m) { return fmt != Fmt::Q4_KxF32 && m <= PROLOGUE_QUANT_MAX_M; }
 
-cudaError_t launch_rowstream(const RowStreamArgs& a, const DeviceInfo& dev, cudaStream_t st) {
+cudaError_t launch_rowstream(const RowStreamArgs& in, const DeviceInfo& dev, cudaStream_t st) {
+  RowStreamArgs a = in;
+  if (a.n_seg <= 0) {  // one tensor: it is segment 0
+    a.n_seg = 1;
+    a.seg[0] = RowSeg{a.w, a.n_rows, a.bias, a.out, 0};
+  } else {
+    if (a.n_seg > MAX_SEGS || a.mode != RowOut::Store) return cudaErrorInvalidValue;
+    a.n_rows = 0;
+    for (int i = 0; i < a.n_seg; ++i) a.n_rows += a.seg[i].n_rows;
+  }
   if (a.n_rows <= 0 || a.m <= 0) return cudaSuccess;
   if (a.m > MAX_M || a.K % (a.fmt == Fmt::Q8_0xQ8_0 ? QK8_0 : QK_K) != 0) return cudaErrorInvalidValue;
   Layout L{};
@@ -581,7 +691,11 @@ cudaError_t launch_rowstream(const RowStreamArgs& a, const DeviceInfo& dev, cuda
   long long r_want = (a.n_rows + 3LL * dev.sm_count - 1) / (3LL * dev.sm_count);
   if (r_want < 1) r_want = 1;
   L.tile_rows = static_cast<int>(r_want < r_cap ? r_want : r_cap);
-  L.n_tiles = (a.n_rows + L.tile_rows - 1) / L.tile_rows;
+  L.n_tiles = 0;
+  for (int i = 0; i < a.n_seg; ++i) {  // tiles never straddle two tensors
+    a.seg[i].tile0 = L.n_tiles;
+    L.n_tiles += (a.seg[i].n_rows + L.tile_rows - 1) / L.tile_rows;
+  }
   const int act = (act_bytes_total(a.fmt, a.K, a.m) + 127) & ~127;
   L.act_off = BAR_BYTES;
   L.stage_off = L.act_off + act;

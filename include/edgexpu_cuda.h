@@ -93,6 +93,15 @@ int edgexpu_cuda_quantize_dev(uint32_t weight_type, const float *x, int m, int n
 int edgexpu_cuda_linear_quant_batch_dev(float *out, const float *x, const uint8_t *weight, uint32_t type,
                                         const float *bias, int m, int n_out, int n_in, void *stream);
 
+/* n (1..4) tensors that read the same activations (q/k/v, or gate/up) in ONE launch:
+ * outs[i][t*n_outs[i] + o] = biases[i][o] + dot(W_i,o, quantize(x_t)).  Same results as n calls of
+ * edgexpu_cuda_linear_quant_batch_dev; the reference makes those n calls one by one
+ * (native.c:2530-2532, :2576-2577), a single launch streams all n weight tensors back to back.
+ * outs, weights, n_outs and biases are host arrays of n entries (biases may be NULL). */
+int edgexpu_cuda_linear_quant_multi_dev(int n, float *const *outs, const uint8_t *const *weights, const int *n_outs,
+                                        const float *const *biases, uint32_t type, const float *x, int m, int n_in,
+                                        void *stream);
+
 /* Same result as edgexpu_cuda_linear_quant_batch_dev, but the call allocates no memory: no
  * cudaMalloc, no cudaFree, no allocating library routine.  It has no counterpart in the reference;
  * it is for callers that cannot allocate once running -- code recorded into a CUDA graph, runtimes

@@ -315,3 +315,39 @@ def test_logits_ties_bias_and_shards(gpu, port):
         assert gpu.key_to_id(k) == tok_o
     finally:
         gpu.free_weight(h)
+
+
+@pytest.mark.parametrize("wtype,m", [(TYPE_Q4_K, 1), (TYPE_Q4_K, 5), (TYPE_Q8_0, 2)])
+def test_multi_tensor_launch_equals_separate_calls(gpu, port, wtype, m):
+    """q/k/v-style grouped launch: one kernel over several weight tensors sharing x."""
+    torch = _torch()
+    s = _synth()
+    rng = np.random.default_rng(40 + m)
+    n_in = 1024 if wtype == TYPE_Q4_K else 576
+    shapes = [512, 128, 128] if wtype == TYPE_Q4_K else [576, 192]
+    ws = [s.weight(rng, wtype, n, n_in) for n in shapes]
+    hs = [gpu.upload_weight(w, wtype, n, n_in) for w, n in zip(ws, shapes)]
+    try:
+        x_np = s.activations(rng, m, n_in)
+        x = torch.from_numpy(x_np).cuda()
+        bias = [torch.from_numpy(rng.standard_normal(n).astype(np.float32)).cuda() for n in shapes]
+        outs = [torch.full((m, n), float("nan"), device="cuda") for n in shapes]
+        refs = [torch.full((m, n), float("nan"), device="cuda") for n in shapes]
+        cuda = gpu.load_cuda()
+        k = len(shapes)
+        P = ctypes.c_void_p * k
+        ok = cuda.edgexpu_cuda_linear_quant_multi_dev(
+            k, P(*[o.data_ptr() for o in outs]), P(*hs), (ctypes.c_int * k)(*shapes), P(*[b.data_ptr() for b in bias]),
+            wtype, x.data_ptr(), m, n_in, _stream())
+        assert ok, cuda.edgexpu_cuda_last_error()
+        for r, h, n, b in zip(refs, hs, shapes, bias):
+            assert cuda.edgexpu_cuda_linear_quant_batch_dev(r.data_ptr(), x.data_ptr(), h, wtype, b.data_ptr(), m, n,
+                                                            n_in, _stream())
+        _sync(gpu)
+        for o, r, w, n, b in zip(outs, refs, ws, shapes, bias):
+            np.testing.assert_array_equal(o.cpu().numpy(), r.cpu().numpy())
+            want = port.linear(x_np, w, wtype, n, b.cpu().numpy())
+            assert_close(o.cpu().numpy(), want, port.linear_bound(x_np, w, wtype, n), 1e-6)
+    finally:
+        for h in hs:
+            gpu.free_weight(h)
