@@ -183,10 +183,21 @@ def peak_hbm():
 # ---- the reference's CPU implementation (baseline arm) ------------------------------------------
 
 
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
 class RefCPU:
     def __init__(self):
         if not (REF_LIB.exists() and REF_DRIVER.exists()):
             raise FileNotFoundError("oracle/_ref not built")
+        # The reference's OpenMP loops run on every host core (torchrun exports OMP_NUM_THREADS=1;
+        # the reference honours the variable instead of probing, cpu_kernel.c:53-57).  libgomp reads
+        # it when it loads, i.e. at the CDLL below.
+        os.environ["OMP_NUM_THREADS"] = str(host_threads())
         self.lib = ctypes.CDLL(str(REF_LIB))
         self.drv = ctypes.CDLL(str(REF_DRIVER))
         vp, i, u = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32
@@ -240,7 +251,7 @@ class CpuWorkload:
         self.h = rng.standard_normal(wl["hidden"]).astype(np.float32)
         self.nbytes = (sum(linear_alg_bytes(self.t, n_out, n_in, m) for _, n_out, n_in in self.weights)
                        + m * logits_alg_bytes(self.t, vocab_rows, wl["hidden"]))
-        self.threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+        self.threads = int(os.environ["OMP_NUM_THREADS"])
 
     def step(self):
         for w, n_out, n_in in self.weights:
@@ -268,7 +279,6 @@ def run_reference(args, wl):
     if rank != 0:
         return
     m = args.batch
-    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
     layers = args.ref_layers or wl["layers"]
     vocab_rows = wl["vocab"] * layers // wl["layers"]
     try:
