@@ -180,11 +180,43 @@ int run_rows_dev(float* out, const void* act, bool act_f32, const uint8_t* weigh
   return 1;
 }
 
+// Prefill-sized Q4_K batches run as a tensor-core GEMM (gemm_tc.cu).
+bool use_tc(uint32_t type, int m, int n_in) { return type == ex::TYPE_Q4_K && m >= ex::TC_MIN_M && n_in % ex::QK_K == 0; }
+
+// Pack m activation rows (fp32 x, or Q8_K rows xq) into the GEMM's tile layout in g.xq.
+int tc_pack(const float* x, const uint8_t* xq, int m, int n_in, cudaStream_t st, char* error, size_t error_size) {
+  if (!grow_dev(g.xq, ex::tc_act_bytes(m, n_in) + 64, st, error, error_size)) return 0;
+  uint8_t* act = static_cast<uint8_t*>(g.xq.p);
+  EX_CUDA(x != nullptr ? ex::launch_tc_pack_f32(x, m, n_in, act, st) : ex::launch_tc_pack_q8k(xq, m, n_in, act, st),
+          error, error_size);
+  return 1;
+}
+
+int tc_gemm(float* out, int32_t* partials, const uint8_t* weight, const float* bias, int m, int n_out, int n_in,
+            cudaStream_t st, char* error, size_t error_size) {
+  ex::TcGemmArgs a{};
+  a.w = weight;
+  a.n_rows = n_out;
+  a.K = n_in;
+  a.act = static_cast<const uint8_t*>(g.xq.p);
+  a.m = m;
+  a.bias = bias;
+  a.out = out;
+  a.out_stride = n_out;
+  a.partials = partials;
+  a.status = g.d_status;
+  EX_CUDA(ex::launch_tc_gemm(a, g.info, st), error, error_size);
+  return 1;
+}
+
 int run_linear_dev(float* out, const float* x, const uint8_t* weight, uint32_t type, const float* bias, int m,
                    int n_out, int n_in, cudaStream_t st, char* error, size_t error_size) {
   if (out == nullptr || x == nullptr || weight == nullptr || m <= 0 || n_out <= 0 || n_in <= 0)
     return fail(error, error_size, "invalid arguments");
   if (!lookup(weight, type, n_out, n_in, error, error_size)) return 0;
+  if (use_tc(type, m, n_in))
+    return tc_pack(x, nullptr, m, n_in, st, error, error_size) &&
+           tc_gemm(out, nullptr, weight, bias, m, n_out, n_in, st, error, error_size);
   const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
   // cpu_kernel.c:577-631: every activation row is quantized once, then each weight row is dotted
   // against every quantized row.  Small batches quantize inside the GEMV launch itself.
@@ -482,6 +514,14 @@ int edgexpu_cuda_linear_quant_multi_dev(int n, float* const* outs, const uint8_t
     if (!lookup(weights[i], type, n_outs[i], n_in, nullptr, 0)) return 0;
   }
   cudaStream_t st = pick(stream);
+  if (use_tc(type, m, n_in)) {  // one packing of the activations, one GEMM per tensor
+    if (!tc_pack(x, nullptr, m, n_in, st, nullptr, 0)) return 0;
+    for (int i = 0; i < n; ++i)
+      if (!tc_gemm(outs[i], nullptr, weights[i], biases != nullptr ? biases[i] : nullptr, m, n_outs[i], n_in, st,
+                   nullptr, 0))
+        return 0;
+    return 1;
+  }
   const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
   const size_t qb = act_row_bytes_of(type, n_in);
   const bool fused = ex::rowstream_quantizes_itself(fmt, m);
@@ -523,6 +563,9 @@ int edgexpu_cuda_dot_quant_q8_dev(float* out, const uint8_t* xq, const uint8_t* 
   if (out == nullptr || xq == nullptr || weight == nullptr || m <= 0 || n_out <= 0 || n_in <= 0)
     return fail(nullptr, 0, "invalid arguments");
   if (!lookup(weight, type, n_out, n_in, nullptr, 0)) return 0;
+  if (use_tc(type, m, n_in))
+    return tc_pack(nullptr, xq, m, n_in, pick(stream), nullptr, 0) &&
+           tc_gemm(out, nullptr, weight, bias, m, n_out, n_in, pick(stream), nullptr, 0);
   return run_rows_dev(out, xq, false, weight, type, bias, m, n_out, n_in, pick(stream), nullptr, 0);
 }
 
@@ -540,6 +583,9 @@ int edgexpu_cuda_block_partials_dev(int32_t* partials, const uint8_t* xq, const 
   if (!need_ready(nullptr, 0)) return 0;
   if (partials == nullptr || xq == nullptr || m <= 0) return fail(nullptr, 0, "invalid arguments");
   if (!lookup(weight, type, n_out, n_in, nullptr, 0)) return 0;
+  if (use_tc(type, m, n_in))
+    return tc_pack(nullptr, xq, m, n_in, pick(stream), nullptr, 0) &&
+           tc_gemm(nullptr, partials, weight, nullptr, m, n_out, n_in, pick(stream), nullptr, 0);
   ex::RowStreamArgs a{};
   a.fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
   a.mode = ex::RowOut::Partials;
@@ -561,7 +607,8 @@ int edgexpu_cuda_reserve(int m, int n_in, char* error, size_t error_size) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   if (!need_ready(error, error_size)) return 0;
   if (m <= 0 || n_in <= 0) return fail(error, error_size, "invalid arguments");
-  const size_t need = static_cast<size_t>(m) * std::max(act_row_bytes_of(ex::TYPE_Q8_0, n_in), act_row_bytes_of(ex::TYPE_Q4_K, n_in)) + 64;
+  size_t need = static_cast<size_t>(m) * std::max(act_row_bytes_of(ex::TYPE_Q8_0, n_in), act_row_bytes_of(ex::TYPE_Q4_K, n_in)) + 64;
+  if (use_tc(ex::TYPE_Q4_K, m, n_in)) need = std::max(need, ex::tc_act_bytes(m, n_in) + 64);
   return grow_dev(g.xq, need, g.stream, error, error_size);
 }
 

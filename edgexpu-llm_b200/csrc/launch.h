@@ -71,4 +71,32 @@ bool rowstream_quantizes_itself(Fmt fmt, int m);
 
 cudaError_t launch_rowstream(const RowStreamArgs& a, const DeviceInfo& dev, cudaStream_t st);
 
+// ---- tensor-core GEMM (gemm_tc.cu): Q4_K weights x Q8_K activations for prefill batches ----
+
+// Smallest batch routed to the tensor-core GEMM instead of the row-stream GEMV.
+constexpr int TC_MIN_M = 64;
+
+// Bytes of the packed activations of m rows of length K (swizzled int8 tiles + per-block d).
+size_t tc_act_bytes(int m, int K);
+
+// fp32 rows -> packed activations, quantized exactly as edgexpu_gguf_quantize_q8_k.
+cudaError_t launch_tc_pack_f32(const float* x, int m, int K, uint8_t* act, cudaStream_t st);
+// Q8_K rows (GGUF blocks) -> packed activations.
+cudaError_t launch_tc_pack_q8k(const uint8_t* xq, int m, int K, uint8_t* act, cudaStream_t st);
+
+struct TcGemmArgs {
+  const uint8_t* w;      // Q4_K rows, 16-byte aligned, row_bytes = K/256*144
+  int n_rows;
+  int K;
+  const uint8_t* act;    // packed activations of m rows
+  int m;
+  const float* bias;     // nullable
+  float* out;            // out[t*out_stride + row]
+  long long out_stride;
+  int32_t* partials;     // non-null: (sumi, summ) per [t][row][super-block] instead of out
+  uint32_t* status;      // device status word
+};
+
+cudaError_t launch_tc_gemm(const TcGemmArgs& a, const DeviceInfo& dev, cudaStream_t st);
+
 }  // namespace ex

@@ -81,19 +81,6 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// Bounded mbarrier wait that also gives up as soon as another thread raised the abort flag.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
-    if ((i & 31u) == 0) {
-      if (*abort_flag) return false;
-      if (global_ns() - t0 > WAIT_LIMIT_NS) return false;
-    }
-  }
-}
-
 // ---- activation prologue ---------------------------------------------------------------------------
 
 __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct) {
@@ -306,19 +293,6 @@ __device__ __forceinline__ void row_q8_0(const RowStreamArgs& a, const uint8_t* 
         }
       }
     }
-  }
-}
-
-// Unpack the four 6-bit (scale, min) pairs of sub-blocks 4h..4h+3 (get_scale_min_k4,
-// gguf_quant.c:212-220) from the 12 scale bytes held as words s0, s1, s2.
-__device__ __forceinline__ void q4k_scales_half(uint32_t s0, uint32_t s1, uint32_t s2, int h, uint32_t& sc4,
-                                                uint32_t& mn4) {
-  if (h == 0) {
-    sc4 = s0 & 0x3F3F3F3Fu;
-    mn4 = s1 & 0x3F3F3F3Fu;
-  } else {
-    sc4 = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
-    mn4 = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
   }
 }
 

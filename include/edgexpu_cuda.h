@@ -73,7 +73,9 @@ int edgexpu_cuda_quantize_q8_k(const float *x, int n, uint8_t *dst, char *error,
 
 /* out[t*n_out + o] = bias[o] + dot(W_o, quantize(x_t)) for t < m, o < n_out; x is [m][n_in]
  * row-major, out is [m][n_out]; bias may be NULL.  Q8_0 weights use Q8_0 activations, Q4_K
- * weights use Q8_K activations (cpu_kernel.c:577-631). */
+ * weights use Q8_K activations (cpu_kernel.c:577-631).  Batches of up to 63 rows stream the
+ * weight once through the GEMV kernel; Q4_K batches of 64 rows and more (prefill) run as a
+ * tensor-core GEMM (tcgen05 kind::i8) with the same integer partials. */
 int edgexpu_cuda_linear_quant_batch(float *out, const float *x, const uint8_t *weight, uint32_t type,
                                     const float *bias, int m, int n_out, int n_in, char *error,
                                     size_t error_size);
@@ -128,8 +130,8 @@ int edgexpu_cuda_dot_quant_q8_dev(float *out, const uint8_t *xq, const uint8_t *
 int edgexpu_cuda_logits_argmax_dev(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
                                    const float *bias, int64_t row0, uint64_t *key, void *stream);
 
-/* Test hook: per-block int32 partials of the production kernel.  xq holds m pre-quantized
- * activation rows.  Q8_0: partials[t][o][b] = ip.  Q4_K: partials[t][o][b][2] = (sumi, summ). */
+/* Test hook: per-block int32 partials of the production kernel (the GEMV, or for Q4_K with
+ * m >= 64 the tensor-core GEMM).  xq holds m pre-quantized activation rows.  Q8_0: partials[t][o][b] = ip.  Q4_K: partials[t][o][b][2] = (sumi, summ). */
 int edgexpu_cuda_block_partials_dev(int32_t *partials, const uint8_t *xq, const uint8_t *weight, uint32_t type,
                                     int m, int n_out, int n_in, void *stream);
 
