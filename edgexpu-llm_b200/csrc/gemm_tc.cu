@@ -1,39 +1,47 @@
 // gemm_tc.cu -- Q4_K weight x Q8_K activation GEMM on the 5th-generation tensor cores
-// (tcgen05.mma kind::i8, operand A and the accumulators in tensor memory) for prefill-sized
-// batches: the batched form of dot_q4_k_q8_k (src/gguf_dot_q8.c:603-762) that
+// (tcgen05.mma kind::i8, int32 accumulators in tensor memory) for prefill-sized batches: the
+// batched form of dot_q4_k_q8_k (src/gguf_dot_q8.c:603-762) that
 // edgexpu_cpu_linear_quant_batch (src/cpu_kernel.c:545-644) runs per row and token.
 //
 // Arithmetic.  Per super-block the reference computes, in int32,
 //   sumi = sum_j sc_j * sum_{l<32} q4 * q8      summ = sum_j m_j * (bsum_2j + bsum_2j+1)
-// and then acc += d_x*d_w*sumi - d_x*dmin_w*summ (gguf_dot_q8.c:711-759).  The folded weight
-// v = sc_j * q4 lies in [0, 945] (10 bits), so it is split into v = 256*h + l with l in
-// [-128, 127] and h in [0, 4], and three int8 contractions over the super-block run on the
-// tensor cores into three int32 accumulators:
-//   L = sum l*q8,   H = sum h*q8,   M = sum m_j*q8      =>  sumi = L + 256*H,  summ = M.
-// All three are exact integer sums, so (sumi, summ) equal the reference's int32 values.
+// and then acc += d_x*d_w*sumi - d_x*dmin_w*summ (gguf_dot_q8.c:711-759).
+//  * sumi on the tensor cores.  The folded weight v = sc_j * q4 lies in [0, 945] (10 bits); it
+//    is split into v = 256*h + l with l in [-128, 127] and h in [0, 4], and two int8
+//    contractions over the super-block accumulate L = sum l*q8 and H = sum h*q8 in int32, so
+//    sumi = L + 256*H exactly.
+//  * summ on the CUDA cores.  It has only 8 terms per super-block: m_j (6-bit, unsigned) times
+//    the 32-element activation sums S_j (13-bit, signed).  The packing kernel splits every S_j
+//    into 7-bit digits S = 128*Sh + Sl, and four dp4a give summ exactly.
 //
-// Float conversion without I2F.  Every accumulator starts at the bit pattern 0x4B400000
+// Float conversion without I2F.  The L and H accumulators start at the bit pattern 0x4B400000
 // (1.5 * 2^23 as a float) instead of 0; the MMA adds exact int32 products to it, and since
-// |L| <= 128*127*256 < 2^22 (likewise H, M), the float value of the bits is 1.5*2^23 + L
-// exactly.  The epilogue therefore converts with one FADD per accumulator.
+// |L| <= 128*127*256 < 2^22 (likewise H and summ), the float value of the bits is
+// 1.5*2^23 + L exactly, so the epilogue converts with one FADD.
 //
-// Tile: 128 weight rows (tensor-memory lanes, MMA M) x 64 tokens (MMA N); K advances one
-// Q4_K nibble group (64 elements) per A chunk.  Tensor-memory columns (of 512):
-//   [0,192)   accumulator buffer 0: L [0,64) H [64,128) M [128,192)
-//   [192,384) accumulator buffer 1
-//   [384,432) A chunk buffer 0: L [0,16) H [16,32) M [32,48)  (4 int8 per column, K-major)
-//   [448,496) A chunk buffer 1
-// Two accumulator buffers let the epilogue drain super-block s while the MMAs of s+1 run.
+// Shapes.  A tcgen05.mma of M = 128, K = 32 takes about the same time for every N up to 256
+// (measured on B200), so the tile is 128 weight rows x 128 tokens with N = 128 MMAs: 16 MMAs
+// per super-block and tile.  Tensor-memory columns (of 512):
+//   [0,128) L  [128,256) H    accumulator buffer 0
+//   [256,384) L [384,512) H   accumulator buffer 1
+// Two buffers let the epilogue drain super-block s while the MMAs of s+1 run.  Operands come
+// from shared memory: A (the expanded weight, L and H parts) and B (activations) are K-major
+// tiles with the 128-byte swizzle, one K-half (128 elements) per pipeline stage.
 //
-// Warp roles (18 warps):
+// Warp roles (22 warps):
 //   0      producer: 2-D TMA of the raw Q4_K super-block of 128 rows (tensor map, zero-filled
-//          past the last row) and 1-D bulk copies of pre-swizzled activation tiles
+//          past the last row), bulk copies of activation tiles and per-token scale data
 //   1      tensor-memory allocation and the single-thread MMA issuer
-//   2..9   converters: expand nibbles and 6-bit scales into the L/H/M int8 operand and store
-//          it to tensor memory (2 warps per 32-lane quadrant, one per A buffer)
-//   10..17 epilogue: drain accumulators, scale, accumulate in fp32 registers, store
+//   2..5   converters: one weight row per thread, nibbles and 6-bit scales -> L/H tiles
+//   6..21  epilogue: 4 warps per 32-lane quadrant, 32 tokens each: drain accumulators (loads
+//          of the next 8-token group in flight while the current one is computed), mins term,
+//          scale, accumulate in fp32 registers, store
+// The epilogue is the busiest role (about 12 operations per output and super-block), so it
+// gets most of the warps; 4 warps per quadrant and 8-token load groups measured fastest.
 // Every wait is bounded; a timeout sets a status bit, raises the CTA abort flag and all roles
-// fall through to teardown (bulk copies drained, MMAs committed, tensor memory freed).
+// fall through to teardown (copies drained, MMAs committed, tensor memory freed).  The kernel
+// needs a whole SM (about 196 KB of shared memory), so the 512-column tensor-memory allocation
+// is never contended by another CTA.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -47,23 +55,32 @@
 namespace ex {
 namespace {
 
-constexpr int TC_BM = 128;
-constexpr int TC_BN = 64;
-constexpr int B_TILE_BYTES = TC_BN * 128;   // 64 tokens x 128 K-bytes, 128-byte swizzle, K-major
-constexpr int RAW_BYTES = TC_BM * Q4_K_BYTES;  // one super-block of 128 rows: 18432
-constexpr int NB_STAGES = 8;
-constexpr int NR_STAGES = 4;
-constexpr int N_CONV_WARPS = 8;
-constexpr int N_EPI_WARPS = 8;
+constexpr int TC_BM = 128;                       // weight rows per tile (MMA M)
+constexpr int TC_BN = 128;                       // tokens per tile (MMA N)
+constexpr int KH_BYTES = 128;                    // K elements (int8 bytes) per stage
+constexpr int A_TILE = TC_BM * KH_BYTES;         // 16 KB, one part (L or H) of a stage
+constexpr int B_TILE = TC_BN * KH_BYTES;         // 16 KB
+constexpr int RAW_BYTES = TC_BM * Q4_K_BYTES;    // one super-block of 128 rows: 18432
+constexpr int AUX_DX = TC_BN * 4;                // d of 128 tokens
+constexpr int AUX_BYTES = AUX_DX + TC_BN * 16;   // + 16 bytes of sub-block-sum digits per token
+constexpr int N_STAGES = 3;
+constexpr int NR_STAGES = 2;
+constexpr int NX_STAGES = 4;
+constexpr int N_CONV_WARPS = 4;
+#ifndef EX_TC_EPI_PER_Q
+#define EX_TC_EPI_PER_Q 4
+#endif
+constexpr int EPI_PER_Q = EX_TC_EPI_PER_Q;       // epilogue warps per 32-lane quadrant
+constexpr int N_EPI_WARPS = 4 * EPI_PER_Q;
+constexpr int EPI_TOK = TC_BN / EPI_PER_Q;       // tokens per epilogue warp
+constexpr int EG = 8;                            // tokens per tensor-memory load group
 constexpr int WARP_PROD = 0;
 constexpr int WARP_MMA = 1;
 constexpr int WARP_CONV0 = 2;
 constexpr int WARP_EPI0 = WARP_CONV0 + N_CONV_WARPS;
 constexpr int TC_THREADS = 32 * (WARP_EPI0 + N_EPI_WARPS);
 
-constexpr uint32_t ACC_COLS = 3 * TC_BN;
-constexpr uint32_t A_COL0 = 384;
-constexpr uint32_t A_BUF_STRIDE = 64;
+constexpr uint32_t ACC_COLS = 2 * TC_BN;         // L and H of one buffer
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_BIAS = 0x4B400000u;
 constexpr float ACC_BIAS_F = 12582912.0f;
@@ -74,20 +91,24 @@ constexpr uint32_t IDESC_I8 = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(TC_
                               (uint32_t(TC_BM >> 4) << 24);
 
 struct SmemLayout {
-  static constexpr int B_OFF = 0;
-  static constexpr int R_OFF = B_OFF + NB_STAGES * B_TILE_BYTES;
-  static constexpr int BAR_OFF = R_OFF + NR_STAGES * RAW_BYTES;
-  static constexpr int N_BARS = 2 * NB_STAGES + 2 * NR_STAGES + 8 + 1;
+  static constexpr int A_OFF = 0;                                  // [stage][L, H] 32 KB
+  static constexpr int B_OFF = A_OFF + N_STAGES * 2 * A_TILE;      // [stage] 16 KB
+  static constexpr int R_OFF = B_OFF + N_STAGES * B_TILE;          // [raw stage] 18 KB
+  static constexpr int X_OFF = R_OFF + NR_STAGES * RAW_BYTES;      // [aux stage] 2.5 KB
+  static constexpr int BAR_OFF = X_OFF + NX_STAGES * AUX_BYTES;
+  static constexpr int N_BARS = 3 * N_STAGES + 2 * NR_STAGES + 2 * NX_STAGES + 4 + 1;
   static constexpr int MISC_OFF = BAR_OFF + 8 * N_BARS;
   static constexpr int BYTES = MISC_OFF + 16;
   static constexpr int ALLOC = BYTES + 1024;  // base rounded up to 1024 for the swizzled tiles
 };
+static_assert(SmemLayout::ALLOC > 116 * 1024, "one CTA per SM keeps the tensor-memory allocation uncontended");
+static_assert(SmemLayout::ALLOC <= 227 * 1024, "shared memory per CTA");
 
 struct TcKernelArgs {
   int n_rows, row_bytes, nb, m, n_tt, n_rt;
-  const uint8_t* w;       // Q4_K rows (for d/dmin in the epilogue)
-  const uint8_t* bt;      // activation tiles [n_tt][nb][2][8 KB]
-  const float* dx;        // [n_tt][nb][64]
+  const uint8_t* w;       // Q4_K rows (header of each super-block for the epilogue)
+  const uint8_t* bt;      // activation tiles [n_tt][nb][2][16 KB]
+  const uint8_t* aux;     // [n_tt][nb][AUX_BYTES]: d[128] floats, digits[128][4] words
   const float* bias;
   float* out;
   long long out_stride;
@@ -111,13 +132,13 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t addr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(addr), "r"(ncols) : "memory");
 }
 
-// D[tmem] (+)= A[tmem] x B[smem descriptor]
-__device__ __forceinline__ void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t acc) {
+// D[tmem] += A[smem descriptor] x B[smem descriptor]
+__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %3, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %4, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(acc), "r"(IDESC_I8)
+      "setp.ne.b32 p, 1, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(IDESC_I8)
       : "memory");
 }
 
@@ -137,14 +158,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t addr, const uint32_t (&v)[8]) 
   asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(addr), "r"(v[0]),
                "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                : "memory");
-}
-__device__ __forceinline__ void tmem_st16(uint32_t addr, const uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16};" ::"r"(addr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -172,18 +185,30 @@ __device__ __forceinline__ uint64_t l2_evict_last_policy() {
   return p;
 }
 
-// Byte of the packed activation tile holding K-byte kb (0..127) of token row r (0..63).
-__host__ __device__ __forceinline__ int sw128_offset(int r, int kb) {
-  return (r >> 3) * 1024 + (r & 7) * 128 + ((((kb >> 4) ^ (r & 7)) & 7) << 4) + (kb & 15);
+// Generic-proxy shared-memory writes become visible to the tensor cores (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk c (K-bytes 16c..16c+15) of row r in a 128-byte-swizzled K-major tile.
+__host__ __device__ __forceinline__ int sw128_chunk(int r, int c) {
+  return (r >> 3) * 1024 + (r & 7) * 128 + (((c ^ r) & 7) << 4);
+}
+
+// Unsigned bytes of a times signed bytes of b, accumulated into c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
 }
 
 // ---- activation packing -------------------------------------------------------------------------
 // One warp per (token, super-block): Q8_K-quantize 256 values (bit-exact with
-// edgexpu_gguf_quantize_q8_k) or copy them from a Q8_K row, and scatter the int8 values into
-// the two swizzled K-half tiles; lane 0 stores d.  Rows past m are written as zeros.
+// edgexpu_gguf_quantize_q8_k) or take them from a Q8_K row, scatter the int8 values into the two
+// swizzled K-half tiles, and store d and the 7-bit digits of the eight 32-element sums
+// (S_j = bsum_2j + bsum_2j+1 = 128*Sh_j + Sl_j).  Rows past m are written as zeros.
 template <bool FROM_F32>
 __global__ void __launch_bounds__(256) tc_pack_kernel(const float* __restrict__ x, const uint8_t* __restrict__ xq,
-                                                      int m, int K, uint8_t* __restrict__ bt, float* __restrict__ dx) {
+                                                      int m, int K, uint8_t* __restrict__ bt,
+                                                      uint8_t* __restrict__ aux) {
   const int nb = K / QK_K;
   const int lane = threadIdx.x & 31;
   const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -193,6 +218,7 @@ __global__ void __launch_bounds__(256) tc_pack_kernel(const float* __restrict__ 
   const int tt = t / TC_BN, r = t % TC_BN;
   uint32_t w0 = 0, w1 = 0;
   float d = 0.0f;
+  int s8 = 0;  // this lane's share of its 32-element sum
   if (t < m) {
     if constexpr (FROM_F32) {
       const float4* src = reinterpret_cast<const float4*>(x + (size_t)t * K + (size_t)sb * QK_K + lane * 8);
@@ -202,18 +228,41 @@ __global__ void __launch_bounds__(256) tc_pack_kernel(const float* __restrict__ 
       d = warp_q8_k(v, q, &gs);
       w0 = pack4_i8(q[0], q[1], q[2], q[3]);
       w1 = pack4_i8(q[4], q[5], q[6], q[7]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s8 += q[i];
     } else {
       const uint8_t* blk = xq + ((size_t)t * nb + sb) * Q8_K_BYTES;
       const uint32_t* qw = reinterpret_cast<const uint32_t*>(blk + 4 + lane * 8);
       w0 = qw[0];
       w1 = qw[1];
       d = *reinterpret_cast<const float*>(blk);
+      // the block's own int16 bsums, as the reference's summ reads them (gguf_dot_q8.c:745-750)
+      if ((lane & 3) == 0) {
+        const int16_t* bs = reinterpret_cast<const int16_t*>(blk + 260);
+        s8 = (int)bs[lane >> 1] + (int)bs[(lane >> 1) + 1];
+      }
     }
   }
   const int kh = lane >> 4, kb = (lane & 15) * 8;
-  uint8_t* tile = bt + (((size_t)tt * nb + sb) * 2 + kh) * B_TILE_BYTES;
-  *reinterpret_cast<uint2*>(tile + sw128_offset(r, kb)) = make_uint2(w0, w1);
-  if (lane == 0) dx[((size_t)tt * nb + sb) * TC_BN + r] = d;
+  uint8_t* tile = bt + (((size_t)tt * nb + sb) * 2 + kh) * B_TILE;
+  *reinterpret_cast<uint2*>(tile + sw128_chunk(r, kb >> 4) + (kb & 15)) = make_uint2(w0, w1);
+  // 32-element sums: lanes 4j..4j+3 hold sub-block j
+  int s32 = s8 + __shfl_xor_sync(0xFFFFFFFFu, s8, 1);
+  s32 += __shfl_xor_sync(0xFFFFFFFFu, s32, 2);
+  const uint32_t lo = static_cast<uint32_t>(s32 & 127), hi = static_cast<uint32_t>((s32 >> 7) & 0xFF);
+  // digits of a token: words [Sl0..3][Sl4..7][Sh0..3][Sh4..7]
+  uint32_t dig[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t l = __shfl_sync(0xFFFFFFFFu, lo, 4 * j), h = __shfl_sync(0xFFFFFFFFu, hi, 4 * j);
+    dig[j >> 2] |= l << (8 * (j & 3));
+    dig[2 + (j >> 2)] |= h << (8 * (j & 3));
+  }
+  if (lane == 0) {
+    uint8_t* xa = aux + ((size_t)tt * nb + sb) * AUX_BYTES;
+    reinterpret_cast<float*>(xa)[r] = d;
+    *reinterpret_cast<uint4*>(xa + AUX_DX + r * 16) = make_uint4(dig[0], dig[1], dig[2], dig[3]);
+  }
 }
 
 // ---- the GEMM ---------------------------------------------------------------------------------------
@@ -230,6 +279,20 @@ __device__ __forceinline__ void expand4(uint32_t x, uint32_t sc, uint32_t& lo, u
   lo = __byte_perm(v0, v1, 0x6420) ^ 0x80808080u;
 }
 
+// Bounded busy wait without the suspend hint, for the single-thread MMA issuer whose handoffs
+// are on the critical path.
+__device__ __forceinline__ bool spin_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > WAIT_LIMIT_NS) return false;
+    }
+  }
+}
+
 // Bounded wait whose outcome is the same for every lane of the warp (the tcgen05 ld/st that
 // follow are warp-collective); returns converged.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -242,20 +305,25 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, uint32_t* 
   atomicOr(status, bit);
 }
 
+// PARTIALS: write the exact (sumi, summ) per block instead of the fp32 outputs (test hook).
+template <bool PARTIALS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap wmap, const TcKernelArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ast = smem + SmemLayout::A_OFF;
   uint8_t* bst = smem + SmemLayout::B_OFF;
   uint8_t* rst = smem + SmemLayout::R_OFF;
+  uint8_t* xst = smem + SmemLayout::X_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::BAR_OFF);
-  uint64_t* b_full = bars;
-  uint64_t* b_empty = b_full + NB_STAGES;
-  uint64_t* r_full = b_empty + NB_STAGES;
+  uint64_t* a_full = bars;                // A tiles of a stage written (4 converter warps)
+  uint64_t* b_full = a_full + N_STAGES;   // B tile of a stage landed (producer, tx bytes)
+  uint64_t* empty = b_full + N_STAGES;    // the MMAs of a stage completed
+  uint64_t* r_full = empty + N_STAGES;
   uint64_t* r_empty = r_full + NR_STAGES;
-  uint64_t* a_full = r_empty + NR_STAGES;
-  uint64_t* a_empty = a_full + 2;
-  uint64_t* acc_full = a_empty + 2;
+  uint64_t* x_full = r_empty + NR_STAGES;
+  uint64_t* x_empty = x_full + NX_STAGES;
+  uint64_t* acc_full = x_empty + NX_STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* fin = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SmemLayout::MISC_OFF);
@@ -263,17 +331,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NB_STAGES; ++i) {
+    for (int i = 0; i < N_STAGES; ++i) {
+      mbar_init(&a_full[i], N_CONV_WARPS);
       mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], 1);
+      mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < NR_STAGES; ++i) {
       mbar_init(&r_full[i], 1);
       mbar_init(&r_empty[i], N_CONV_WARPS);
     }
+    for (int i = 0; i < NX_STAGES; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], N_EPI_WARPS);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&a_full[i], 4);
-      mbar_init(&a_empty[i], 1);
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], N_EPI_WARPS);
     }
@@ -281,7 +352,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == WARP_MMA) {
+  if (warp == WARP_MMA) {  // warp 1 has not diverged: the warp-collective allocation is converged
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
@@ -296,12 +367,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == WARP_PROD) {
     if (lane == 0) {
       const uint64_t pol = l2_evict_last_policy();
-      uint32_t bs = 0, bph = 0, rs = 0, rph = 0;
-      long long b_issued = 0, r_issued = 0;
+      uint32_t s = 0, ph = 0, rs = 0, rph = 0, xs = 0, xph = 0;
+      long long b_issued = 0, r_issued = 0, x_issued = 0;
       bool ok = true;
       for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
         const int rt = (int)(tile / n_tt), tt = (int)(tile % n_tt);
-        const uint8_t* src = a.bt + (size_t)tt * nb * 2 * B_TILE_BYTES;
         for (int sb = 0; ok && sb < nb; ++sb) {
           if (!wait_or_abort(&r_empty[rs], rph ^ 1u, abort_flag)) {
             ok = false;
@@ -314,18 +384,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             rs = 0;
             rph ^= 1u;
           }
+          if (!wait_or_abort(&x_empty[xs], xph ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&x_full[xs], AUX_BYTES);
+          bulk_g2s(xst + xs * AUX_BYTES, a.aux + ((size_t)tt * nb + sb) * AUX_BYTES, AUX_BYTES, &x_full[xs], pol);
+          ++x_issued;
+          if (++xs == NX_STAGES) {
+            xs = 0;
+            xph ^= 1u;
+          }
           for (int kh = 0; kh < 2; ++kh) {
-            if (!wait_or_abort(&b_empty[bs], bph ^ 1u, abort_flag)) {
+            if (!wait_or_abort(&empty[s], ph ^ 1u, abort_flag)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&b_full[bs], B_TILE_BYTES);
-            bulk_g2s(bst + bs * B_TILE_BYTES, src + ((size_t)sb * 2 + kh) * B_TILE_BYTES, B_TILE_BYTES, &b_full[bs],
-                     pol);
+            mbar_arrive_expect_tx(&b_full[s], B_TILE);
+            bulk_g2s(bst + s * B_TILE, a.bt + (((size_t)tt * nb + sb) * 2 + kh) * B_TILE, B_TILE, &b_full[s], pol);
             ++b_issued;
-            if (++bs == NB_STAGES) {
-              bs = 0;
-              bph ^= 1u;
+            if (++s == N_STAGES) {
+              s = 0;
+              ph ^= 1u;
             }
           }
         }
@@ -333,55 +413,46 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!ok) raise_abort(abort_flag, a.status, ST_TIMEOUT_EMPTY);
       // No copy may still be landing in shared memory when the CTA exits.
       bool drained = true;
-      for (long long n = b_issued - NB_STAGES; n < b_issued; ++n)
-        if (n >= 0 && !mbar_wait(&b_full[n % NB_STAGES], (uint32_t)((n / NB_STAGES) & 1))) drained = false;
+      for (long long n = b_issued - N_STAGES; n < b_issued; ++n)
+        if (n >= 0 && !mbar_wait(&b_full[n % N_STAGES], (uint32_t)((n / N_STAGES) & 1))) drained = false;
       for (long long n = r_issued - NR_STAGES; n < r_issued; ++n)
         if (n >= 0 && !mbar_wait(&r_full[n % NR_STAGES], (uint32_t)((n / NR_STAGES) & 1))) drained = false;
+      for (long long n = x_issued - NX_STAGES; n < x_issued; ++n)
+        if (n >= 0 && !mbar_wait(&x_full[n % NX_STAGES], (uint32_t)((n / NX_STAGES) & 1))) drained = false;
       if (!drained) atomicOr(a.status, ST_TIMEOUT_DRAIN);
     }
   } else if (warp == WARP_MMA) {
     if (lane == 0) {
-      uint32_t bs = 0, bph = 0, g = 0, accb = 0;
+      uint32_t s = 0, ph = 0, accb = 0;
       bool ok = true;
       for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
         for (int sb = 0; ok && sb < nb; ++sb) {
           const uint32_t ab = accb & 1u;
-          if (!wait_or_abort(&acc_empty[ab], (accb >> 1) & 1u, abort_flag)) {
+          if (!spin_wait(&acc_empty[ab], (accb >> 1) & 1u, abort_flag)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t d_col = tmem + ab * ACC_COLS;
-          for (int c = 0; c < 4; ++c) {
-            if ((c & 1) == 0) {
-              if (!wait_or_abort(&b_full[bs], bph, abort_flag)) {
-                ok = false;
-                break;
-              }
-            }
-            const uint32_t ai = g & 1u;
-            if (!wait_or_abort(&a_full[ai], (g >> 1) & 1u, abort_flag)) {
+          const uint32_t d_l = tmem + ab * ACC_COLS, d_h = d_l + TC_BN;
+          for (int kh = 0; kh < 2; ++kh) {
+            if (!spin_wait(&b_full[s], ph, abort_flag) || !spin_wait(&a_full[s], ph, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t a_col = tmem + A_COL0 + ai * A_BUF_STRIDE;
-            const uint64_t bdesc = sw128_desc(smem_u32(bst + bs * B_TILE_BYTES));
+            const uint64_t al = sw128_desc(smem_u32(ast + s * 2 * A_TILE));
+            const uint64_t ah = sw128_desc(smem_u32(ast + s * 2 * A_TILE + A_TILE));
+            const uint64_t bd = sw128_desc(smem_u32(bst + s * B_TILE));
 #pragma unroll
-            for (int ks = 0; ks < 2; ++ks) {
-              const uint64_t bd = bdesc + (uint64_t)((((c & 1) * 2 + ks) * 32) >> 4);
-#pragma unroll
-              for (int p = 0; p < 3; ++p) mma_i8_ts(d_col + p * TC_BN, a_col + p * 16 + ks * 8, bd, 1u);
+            for (int ks = 0; ks < KH_BYTES / 32; ++ks) {
+              const uint64_t k = (uint64_t)((ks * 32) >> 4);
+              mma_i8_ss(d_l, al + k, bd + k);
+              mma_i8_ss(d_h, ah + k, bd + k);
             }
-            tc_commit(&a_empty[ai]);
-            if (c & 1) {
-              tc_commit(&b_empty[bs]);
-              if (++bs == NB_STAGES) {
-                bs = 0;
-                bph ^= 1u;
-              }
+            tc_commit(&empty[s]);
+            if (++s == N_STAGES) {
+              s = 0;
+              ph ^= 1u;
             }
-            ++g;
           }
           if (!ok) break;
           tc_commit(&acc_full[ab]);
@@ -394,12 +465,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!mbar_wait(fin, 0)) atomicOr(a.status, ST_TIMEOUT_DRAIN);
     }
   } else if (warp < WARP_EPI0) {
-    // Converters: quadrant q owns tensor-memory lanes (= tile rows) 32q..32q+31; set i fills
-    // A buffer i, i.e. chunks c = i and i + 2 of every super-block.
-    const int q = warp & 3, i = (warp - WARP_CONV0) >> 2;
-    const int r = 32 * q + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + A_COL0 + (uint32_t)i * A_BUF_STRIDE;
-    uint32_t rs = 0, rph = 0, uses = 0;
+    // Converters: thread = one weight row of the tile; per stage (K-half) 64 nibble bytes ->
+    // 128 bytes of L and 128 bytes of H in the swizzled A tiles.
+    const int r = 32 * (warp - WARP_CONV0) + lane;
+    uint32_t s = 0, ph = 0, rs = 0, rph = 0;
     bool ok = true;
     for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
       for (int sb = 0; ok && sb < nb; ++sb) {
@@ -409,36 +478,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         const uint8_t* raw = rst + rs * RAW_BYTES + r * Q4_K_BYTES;
         const uint4 hdr = *reinterpret_cast<const uint4*>(raw);
-        for (int c = i; c < 4; c += 2) {
-          const uint4 n0 = *reinterpret_cast<const uint4*>(raw + 16 + 32 * c);
-          const uint4 n1 = *reinterpret_cast<const uint4*>(raw + 32 + 32 * c);
+        for (int kh = 0; kh < 2; ++kh) {
           uint32_t sc4, mn4;
-          q4k_scales_half(hdr.y, hdr.z, hdr.w, c >> 1, sc4, mn4);
-          const int sh = 16 * (c & 1);
-          const uint32_t sc_lo = (sc4 >> sh) & 0xFFu, sc_hi = (sc4 >> (sh + 8)) & 0xFFu;
-          const uint32_t m_lo = ((mn4 >> sh) & 0xFFu) * 0x01010101u, m_hi = ((mn4 >> (sh + 8)) & 0xFFu) * 0x01010101u;
-          const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
-          uint32_t L[16], H[16], M[16];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            expand4(nw[k] & 0x0F0F0F0Fu, sc_lo, L[k], H[k]);
-            expand4((nw[k] >> 4) & 0x0F0F0F0Fu, sc_hi, L[8 + k], H[8 + k]);
-            M[k] = m_lo;
-            M[8 + k] = m_hi;
-          }
-          if (!warp_wait(&a_empty[i], (uses & 1u) ^ 1u, abort_flag)) {
+          q4k_scales_half(hdr.y, hdr.z, hdr.w, kh, sc4, mn4);
+          const uint4* qp = reinterpret_cast<const uint4*>(raw + 16 + 64 * kh);
+          if (!warp_wait(&empty[s], ph ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          tmem_st16(lane_base + 0, L);
-          tmem_st16(lane_base + 16, H);
-          tmem_st16(lane_base + 32, M);
-          tmem_wait_st();
-          tc_fence_before();
+          uint8_t* al = ast + s * 2 * A_TILE;
+          uint8_t* ah = al + A_TILE;
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {  // nibble group: low nibbles = sub-block 2g, high = 2g + 1
+            const uint4 n0 = qp[2 * g], n1 = qp[2 * g + 1];
+            const uint32_t nw[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+            const uint32_t sc_lo = (sc4 >> (16 * g)) & 0xFFu, sc_hi = (sc4 >> (16 * g + 8)) & 0xFFu;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {  // K-bytes 64g + 16c .. +15: low nibbles (c < 2), then high
+              uint32_t L[4], H[4];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t w = nw[4 * (c & 1) + k];
+                expand4(c < 2 ? (w & 0x0F0F0F0Fu) : ((w >> 4) & 0x0F0F0F0Fu), c < 2 ? sc_lo : sc_hi, L[k], H[k]);
+              }
+              *reinterpret_cast<uint4*>(al + sw128_chunk(r, 4 * g + c)) = make_uint4(L[0], L[1], L[2], L[3]);
+              *reinterpret_cast<uint4*>(ah + sw128_chunk(r, 4 * g + c)) = make_uint4(H[0], H[1], H[2], H[3]);
+            }
+          }
+          fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&a_full[i]);
-          ++uses;
+          if (lane == 0) mbar_arrive(&a_full[s]);
+          if (++s == N_STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&r_empty[rs]);
@@ -450,102 +523,110 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     if (!ok && lane == 0) raise_abort(abort_flag, a.status, ST_TIMEOUT_FULL);
   } else {
-    // Epilogue: quadrant q (rows 32q + lane), token half j (tokens 32j..32j+31 of the tile).
+    // Epilogue: quadrant q (rows 32q + lane), token half j (tokens 64j..64j+63 of the tile).
     const int q = warp & 3, j = (warp - WARP_EPI0) >> 2;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * j);
-    {
-      uint32_t bias8[8];
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(EPI_TOK * j);
+    uint32_t bias8[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) bias8[k] = ACC_BIAS;
+    for (int k = 0; k < 8; ++k) bias8[k] = ACC_BIAS;
 #pragma unroll
-      for (int b = 0; b < 2; ++b)
+    for (int b = 0; b < 2; ++b)
 #pragma unroll
-        for (int p = 0; p < 3; ++p)
+      for (int p = 0; p < 2; ++p)
 #pragma unroll
-          for (int h = 0; h < 4; ++h) tmem_st8(lane_base + b * ACC_COLS + p * TC_BN + 8 * h, bias8);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&acc_empty[0]);
-        mbar_arrive(&acc_empty[1]);
-      }
+        for (int h = 0; h < EPI_TOK / 8; ++h) tmem_st8(lane_base + b * ACC_COLS + p * TC_BN + 8 * h, bias8);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&acc_empty[0]);
+      mbar_arrive(&acc_empty[1]);
     }
-    uint32_t accb = 0;
+    uint32_t accb = 0, xs = 0, xph = 0;
     bool ok = true;
     for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
       const int rt = (int)(tile / n_tt), tt = (int)(tile % n_tt);
       const int n = rt * TC_BM + 32 * q + lane;
       const bool valid = n < a.n_rows;
       const uint8_t* rowp = a.w + (size_t)(valid ? n : 0) * a.row_bytes;
-      const int t0 = tt * TC_BN + 32 * j;
-      float acc[32];
+      const int t0 = tt * TC_BN + EPI_TOK * j;
+      float acc[EPI_TOK];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) acc[e] = 0.0f;
-      uint32_t ddm = __ldg(reinterpret_cast<const uint32_t*>(rowp));
+      for (int e = 0; e < EPI_TOK; ++e) acc[e] = 0.0f;
+      uint4 hdr = __ldg(reinterpret_cast<const uint4*>(rowp));
       for (int sb = 0; sb < nb; ++sb) {
-        const float dw = fp16_bits_to_float(ddm), dmw = fp16_bits_to_float(ddm >> 16);
-        if (sb + 1 < nb) ddm = __ldg(reinterpret_cast<const uint32_t*>(rowp + (sb + 1) * Q4_K_BYTES));
-        const float* dxp = a.dx + ((size_t)tt * nb + sb) * TC_BN + 32 * j;
+        const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
+        uint32_t sc4, m03, m47;
+        q4k_scales_half(hdr.y, hdr.z, hdr.w, 0, sc4, m03);
+        q4k_scales_half(hdr.y, hdr.z, hdr.w, 1, sc4, m47);
+        if (sb + 1 < nb) hdr = __ldg(reinterpret_cast<const uint4*>(rowp + (sb + 1) * Q4_K_BYTES));
         const uint32_t ab = accb & 1u;
-        if (!warp_wait(&acc_full[ab], (accb >> 1) & 1u, abort_flag)) {
+        if (!warp_wait(&x_full[xs], xph, abort_flag) || !warp_wait(&acc_full[ab], (accb >> 1) & 1u, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const float* dxs = reinterpret_cast<const float*>(xst + xs * AUX_BYTES) + EPI_TOK * j;
+        const uint4* dgs = reinterpret_cast<const uint4*>(xst + xs * AUX_BYTES + AUX_DX) + EPI_TOK * j;
         const uint32_t col = lane_base + ab * ACC_COLS;
+        // One group = EG tokens.  The loads of group h + 1 are issued right after the wait for
+        // group h, so their latency overlaps the arithmetic of group h.
+        uint32_t Lb[2][EG], Hb[2][EG];
+        tmem_ld8(col, Lb[0]);
+        tmem_ld8(col + TC_BN, Hb[0]);
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          uint32_t L[8], H[8], M[8];
-          tmem_ld8(col + 8 * h, L);
-          tmem_ld8(col + TC_BN + 8 * h, H);
-          tmem_ld8(col + 2 * TC_BN + 8 * h, M);
-          const float4 x0 = __ldg(reinterpret_cast<const float4*>(dxp + 8 * h));
-          const float4 x1 = __ldg(reinterpret_cast<const float4*>(dxp + 8 * h + 4));
-          const float dxv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        for (int h = 0; h < EPI_TOK / EG; ++h) {
+          const int c = h & 1;
+          __syncwarp();  // tcgen05.ld/st are warp-collective; the partials stores below diverge
           tmem_wait_ld();
-          {
-            uint32_t bias8[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) bias8[k] = ACC_BIAS;
-            tmem_st8(col + 8 * h, bias8);
-            tmem_st8(col + TC_BN + 8 * h, bias8);
-            tmem_st8(col + 2 * TC_BN + 8 * h, bias8);
+          tmem_st8(col + EG * h, bias8);
+          tmem_st8(col + TC_BN + EG * h, bias8);
+          if (h + 1 < EPI_TOK / EG) {
+            tmem_ld8(col + EG * (h + 1), Lb[c ^ 1]);
+            tmem_ld8(col + TC_BN + EG * (h + 1), Hb[c ^ 1]);
           }
-          if (a.partials != nullptr) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int t = t0 + 8 * h + e;
+          for (int e = 0; e < EG; ++e) {
+            const uint32_t Le = Lb[c][e], He = Hb[c][e];
+            const uint4 dg = dgs[EG * h + e];  // Sl0..3, Sl4..7, Sh0..3, Sh4..7
+            // summ = sum_j m_j * (128*Sh_j + Sl_j), carried with the float bias
+            int sm = dp4a_us(m47, dg.w, dp4a_us(m03, dg.z, 0));
+            sm = dp4a_us(m47, dg.y, dp4a_us(m03, dg.x, sm * 128 + (int)ACC_BIAS));
+            if constexpr (PARTIALS) {
+              const int t = t0 + EG * h + e;
               if (valid && t < a.m) {
-                const int sumi = (int)(L[e] - ACC_BIAS) + (int)((H[e] - ACC_BIAS) << 8);
-                const int summ = (int)(M[e] - ACC_BIAS);
+                const int sumi = (int)(Le - ACC_BIAS) + (int)((He - ACC_BIAS) << 8);
                 *reinterpret_cast<int2*>(a.partials + (((size_t)t * a.n_rows + n) * nb + sb) * 2) =
-                    make_int2(sumi, summ);
+                    make_int2(sumi, sm - (int)ACC_BIAS);
               }
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float fl = __uint_as_float(L[e]) - ACC_BIAS_F;
-              const float fh = __uint_as_float(H[e]) - ACC_BIAS_F;
-              const float fm = __uint_as_float(M[e]) - ACC_BIAS_F;
+            } else {
+              const float fl = __uint_as_float(Le) - ACC_BIAS_F;
+              const float fh = __uint_as_float(He) - ACC_BIAS_F;
+              const float fm = __int_as_float(sm) - ACC_BIAS_F;
               const float fs = fmaf(256.0f, fh, fl);
               const float tv = fmaf(-dmw, fm, dw * fs);
-              acc[8 * h + e] = fmaf(dxv[e], tv, acc[8 * h + e]);
+              acc[EG * h + e] = fmaf(dxs[EG * h + e], tv, acc[EG * h + e]);
             }
           }
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        if (lane == 0) {
+          mbar_arrive(&acc_empty[ab]);
+          mbar_arrive(&x_empty[xs]);
+        }
         ++accb;
+        if (++xs == NX_STAGES) {
+          xs = 0;
+          xph ^= 1u;
+        }
       }
       if (!ok) break;
-      if (a.partials == nullptr && valid) {
+      if (!PARTIALS && valid) {
         const float bv = a.bias != nullptr ? a.bias[n] : 0.0f;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
+        for (int e = 0; e < EPI_TOK; ++e) {
           const int t = t0 + e;
           if (t < a.m) a.out[(size_t)t * a.out_stride + n] = acc[e] + bv;
         }
@@ -585,7 +666,7 @@ EncodeTiledFn encode_tiled() {
 
 size_t tc_act_bytes(int m, int K) {
   const size_t n_tt = (size_t)(m + TC_BN - 1) / TC_BN, nb = (size_t)K / QK_K;
-  return n_tt * nb * (2 * B_TILE_BYTES + TC_BN * sizeof(float));
+  return n_tt * nb * (2 * B_TILE + AUX_BYTES);
 }
 
 static cudaError_t launch_pack(bool from_f32, const float* x, const uint8_t* xq, int m, int K, uint8_t* act,
@@ -593,13 +674,13 @@ static cudaError_t launch_pack(bool from_f32, const float* x, const uint8_t* xq,
   if (m <= 0 || K <= 0 || K % QK_K != 0) return cudaErrorInvalidValue;
   const int n_tt = (m + TC_BN - 1) / TC_BN, nb = K / QK_K;
   uint8_t* bt = act;
-  float* dx = reinterpret_cast<float*>(act + (size_t)n_tt * nb * 2 * B_TILE_BYTES);
+  uint8_t* aux = act + (size_t)n_tt * nb * 2 * B_TILE;
   const long long warps = (long long)n_tt * TC_BN * nb;
   const unsigned grid = (unsigned)((warps + 7) / 8);
   if (from_f32)
-    tc_pack_kernel<true><<<grid, 256, 0, st>>>(x, nullptr, m, K, bt, dx);
+    tc_pack_kernel<true><<<grid, 256, 0, st>>>(x, nullptr, m, K, bt, aux);
   else
-    tc_pack_kernel<false><<<grid, 256, 0, st>>>(nullptr, xq, m, K, bt, dx);
+    tc_pack_kernel<false><<<grid, 256, 0, st>>>(nullptr, xq, m, K, bt, aux);
   return cudaGetLastError();
 }
 
@@ -638,7 +719,7 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& g, const DeviceInfo& dev, cudaStrea
   k.n_rt = (g.n_rows + TC_BM - 1) / TC_BM;
   k.w = g.w;
   k.bt = g.act;
-  k.dx = reinterpret_cast<const float*>(g.act + (size_t)k.n_tt * nb * 2 * B_TILE_BYTES);
+  k.aux = g.act + (size_t)k.n_tt * nb * 2 * B_TILE;
   k.bias = g.bias;
   k.out = g.out;
   k.out_stride = g.out_stride;
@@ -647,14 +728,20 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& g, const DeviceInfo& dev, cudaStrea
 
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          SmemLayout::ALLOC);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_q4k_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               SmemLayout::ALLOC);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
   const long long tiles = (long long)k.n_tt * k.n_rt;
   const int grid = (int)(tiles < dev.sm_count ? tiles : dev.sm_count);
-  gemm_q4k_tc_kernel<<<grid, TC_THREADS, SmemLayout::ALLOC, st>>>(map, k);
+  if (k.partials != nullptr)
+    gemm_q4k_tc_kernel<true><<<grid, TC_THREADS, SmemLayout::ALLOC, st>>>(map, k);
+  else
+    gemm_q4k_tc_kernel<false><<<grid, TC_THREADS, SmemLayout::ALLOC, st>>>(map, k);
   return cudaGetLastError();
 }
 
