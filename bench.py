@@ -18,6 +18,11 @@ Workloads (``--workload``):
   max-reduction of packed (score, id) keys.  Total work is fixed, so scaling is "strong".
 * ``smollm2_q8_0_decode``: configuration 1's weight stream (30 layers of SmolLM2-135M-shaped
   Q8_0 projections + the tied 49152x576 Q8_0 logits), replicas only at N > 1.
+* ``llama3_8b_q4k_prefill``: configuration 3 -- one step = every quantized projection of the
+  32 Llama-3-8B-shaped layers (``--layers`` fewer for small profiling cases) for a prompt of
+  ``--batch`` tokens (default 2048), run by the tensor-core GEMM (tcgen05 kind::i8).  Metric:
+  useful int8 TOPS (2 * M * N * K per projection); the tensor roofline is 2 x the measured bf16
+  peak (B200's dense int8 rate is twice bf16).
 
 Arms: ``--impl ours`` (default) times the CUDA path; ``--impl reference`` times the reference's
 own CPU implementation (oracle/_ref, compiled from the reference sources) on this host's cores.
@@ -729,20 +734,307 @@ def run_gemv(args):
     pkg.shutdown()
 
 
+# ---- configuration 3: prefill GEMM ------------------------------------------------------------
+
+PREFILL = WORKLOADS["llama3_8b_q4k_decode"]
+TENSOR_I8_SPEC_TOPS = 4500.0
+
+
+def prefill_ops(m, layers):
+    return 2.0 * m * layers * sum(n_out * n_in for _, n_out, n_in, _k in PREFILL["proj"])
+
+
+def peak_i8():
+    try:
+        pk = json.loads(PEAKS.read_text())
+        if pk.get("bf16_tflops"):
+            return 2.0 * float(pk["bf16_tflops"]), "2 x measured bf16_tflops (MEASURED_PEAKS.json)"
+    except (OSError, ValueError):
+        pass
+    return 2.0 * 1590.0, "2 x fallback bf16 1590 TFLOP/s"
+
+
+class CpuPrefill:
+    """One layer's seven projections at m tokens through the reference's CPU linear."""
+
+    def __init__(self, m):
+        import numpy as np
+
+        self.ref = RefCPU()
+        rng = np.random.default_rng(0)
+        self.m = m
+        self.ws = [(host_weight(rng, TYPE_Q4_K, n_out, n_in), n_out, n_in) for _, n_out, n_in, _k in PREFILL["proj"]]
+        self.xs = {n_in: rng.standard_normal((m, n_in)).astype(np.float32) for _, _, n_in in self.ws}
+        self.outs = {n_out: np.empty((m, n_out), np.float32) for _, n_out, _ in self.ws}
+        self.ops = prefill_ops(m, 1)
+        self.threads = int(os.environ["OMP_NUM_THREADS"])
+
+    def step(self):
+        for w, n_out, n_in in self.ws:
+            self.ref.linear(self.outs[n_out], self.xs[n_in], w, TYPE_Q4_K, self.m, n_out, n_in)
+
+
+def cpu_prefill(m, min_seconds, min_reps):
+    """Reference CPU TOPS on the one-layer sample, median over reps lasting >= min_seconds."""
+    w = CpuPrefill(m)
+    w.step()  # the first call runs the reference's OpenMP thread probe (cpu_kernel.c:28-177)
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < min_reps or time.perf_counter() - t_start < min_seconds:
+        t0 = time.perf_counter()
+        w.step()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return w.ops / sec / 1e12, sec, w.threads
+
+
+def run_prefill_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    m = min(args.batch, 64)
+    try:
+        w = CpuPrefill(m)
+    except FileNotFoundError as e:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU build missing: {e}"}))
+        return
+    for _ in range(max(1, args.warmup)):
+        w.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        w.step()
+    sec = (time.perf_counter() - t0) / args.steps
+    tops = w.ops / sec / 1e12
+    sample = (f"one layer's seven projections at {m} of {args.batch} prompt tokens per step "
+              f"({w.ops:.3e} useful ops), reference AVX2 build with OpenMP")
+    print(json.dumps({
+        "metric": f"Q4_K prefill GEMM useful int8 TOPS (llama3_8b_q4k_prefill, M {args.batch})",
+        "value": round(tops, 4), "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u4/i8 x i8 -> i32 -> f32", "data": "synthetic (seeded random-init GGUF blocks)",
+        "impl": "reference", "config": {"workload": "llama3_8b_q4k_prefill", "batch": args.batch,
+                                        "parallelism": f"cpu ({w.threads} threads)"},
+        "cpu_baseline": {"value": round(tops, 4), "unit": "TOPS", "cores": w.threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": round(tops, 4), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_prefill(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    pkg = load_pkg()
+    from edgexpu_llm_b200 import synth
+
+    cuda = pkg.load_cuda()
+    host = pkg.load_host()
+    pkg.init(local)
+    dev = torch.device("cuda", local)
+    m = args.batch
+    shapes = PREFILL["proj"]
+    L = args.layers or PREFILL["layers"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3000 + rank)
+    layers = []
+    for _ in range(L):
+        lay = []
+        for label, n_out, n_in, _k in shapes:
+            buf = synth.torch_weight(TYPE_Q4_K, n_out, n_in, gen, dev)
+            lay.append((label, n_out, n_in, buf, pkg.register_weight(buf, TYPE_Q4_K, n_out, n_in)))
+        layers.append(lay)
+    ins = {n_in: torch.randn((m, n_in), generator=gen, device=dev) for _, _, n_in, _k in shapes}
+    outs = {label: torch.empty((m, n_out), device=dev) for label, n_out, _, _k in shapes}
+    groups = [[0, 1, 2], [3], [4, 5], [6]]  # q|k|v and gate|up share their activations
+    P = ctypes.c_void_p * 4
+    I4 = ctypes.c_int * 4
+    calls = []
+    for lay in layers:
+        for grp in groups:
+            calls.append((len(grp), P(*[outs[lay[i][0]].data_ptr() for i in grp]), P(*[lay[i][4] for i in grp]),
+                          I4(*[lay[i][1] for i in grp]), lay[grp[0]][2]))
+    buf = ctypes.create_string_buffer(512)
+    for n_in in ins:
+        assert cuda.edgexpu_cuda_reserve(m, n_in, buf, 512), buf.value
+
+    def enqueue_step():
+        st = torch.cuda.current_stream().cuda_stream
+        for n_t, o_arr, w_arr, n_arr, n_in in calls:
+            if n_t == 1:
+                ok = cuda.edgexpu_cuda_linear_quant_batch_dev(o_arr[0], ins[n_in].data_ptr(), w_arr[0], TYPE_Q4_K, None,
+                                                              m, n_arr[0], n_in, st)
+            else:
+                ok = cuda.edgexpu_cuda_linear_quant_multi_dev(n_t, o_arr, w_arr, n_arr, None, TYPE_Q4_K,
+                                                              ins[n_in].data_ptr(), m, n_in, st)
+            if not ok:
+                raise RuntimeError(cuda.edgexpu_cuda_last_error().decode())
+
+    def check_status():
+        if not cuda.edgexpu_cuda_stream_sync(torch.cuda.current_stream().cuda_stream, buf, 512):
+            raise RuntimeError(buf.value.decode())
+
+    enqueue_step()
+    torch.cuda.synchronize()
+    check_status()
+    graph = torch.cuda.CUDAGraph()
+    cap_stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.graph(graph, stream=cap_stream):
+        enqueue_step()
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_load0 = time.time()
+    ev0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    extended = False
+    while time.time() - t_load0 < 2.0:
+        extended = True
+        graph.replay()
+        torch.cuda.synchronize()
+    t_load1 = time.time()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop(t_load0, t_load1)
+    clocks["window"] = ("timed region extended by identical untimed steps to 2 s of sampling"
+                        if extended else "timed region")
+    check_status()
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    ops = prefill_ops(m, L)
+    tops = ops * world * args.steps / (ms_max / 1e3) / 1e12
+
+    # Per projection: the GEMM (with its activation packing) of one layer's shape, events on the stream.
+    per_proj = {}
+    st = torch.cuda.current_stream().cuda_stream
+    for i, (label, n_out, n_in, _k) in enumerate(shapes):
+        o = outs[label]
+        for _ in range(2):
+            cuda.edgexpu_cuda_linear_quant_batch_dev(o.data_ptr(), ins[n_in].data_ptr(), layers[0][i][4], TYPE_Q4_K,
+                                                     None, m, n_out, n_in, st)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        a0.record()
+        for j in range(reps):
+            cuda.edgexpu_cuda_linear_quant_batch_dev(o.data_ptr(), ins[n_in].data_ptr(), layers[j % L][i][4], TYPE_Q4_K,
+                                                     None, m, n_out, n_in, st)
+        a1.record()
+        torch.cuda.synchronize()
+        us = a0.elapsed_time(a1) / reps * 1e3
+        per_proj[label] = {"us": round(us, 1), "tops": round(2.0 * m * n_out * n_in / (us * 1e-6) / 1e12, 1)}
+    check_status()
+    peak, peak_src = peak_i8()
+
+    # End to end through the reference-named host shim (host buffers, copies inside the timed region).
+    hx = {n_in: ins[n_in].cpu().numpy() for n_in in ins}
+    hout = {label: np.empty((m, n_out), np.float32) for label, n_out, _, _k in shapes}
+    h2d = sum(4 * m * n_in for _, _, n_in, _k in shapes) * L
+    d2h = sum(4 * m * n_out for _, n_out, _, _k in shapes) * L
+
+    def e2e_step():
+        for lay in layers:
+            for label, n_out, n_in, _b, h in lay:
+                host.edgexpu_cpu_linear_quant_batch(hout[label].ctypes.data, hx[n_in].ctypes.data, h, TYPE_Q4_K, None,
+                                                    m, n_out, n_in)
+        err = host.edgexpu_b200_last_error()
+        if err:
+            raise RuntimeError(err.decode())
+
+    host.edgexpu_b200_clear_error()
+    e2e_step()
+    if world > 1:
+        dist.barrier()
+    e_steps = max(1, min(args.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(e_steps):
+        e2e_step()
+    e2e_s = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    e2e_tops = ops * world * e_steps / float(e2e_s.item()) / 1e12
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            ct, csec, threads = cpu_prefill(64, 10.0, 3)
+            cpu_baseline = {"value": round(ct, 4), "unit": "TOPS", "cores": threads, "kind": "reference",
+                            "sample": f"one layer's seven projections at 64 of {m} tokens per rep ({csec:.3f} s), "
+                                      f"median over >= 10 s, reference AVX2 build (oracle/_ref) with OpenMP"}
+        except FileNotFoundError as e:
+            cpu_baseline = {"value": None, "unit": "TOPS", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+
+    line = {
+        "metric": f"Q4_K prefill GEMM useful int8 TOPS (llama3_8b_q4k_prefill, M {m})",
+        "value": round(tops, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u4/i8 x i8 -> i32 -> f32",
+        "data": "synthetic (seeded random-init GGUF blocks generated in HBM)",
+        "config": {"workload": "llama3_8b_q4k_prefill", "batch": m, "layers": L,
+                   "parallelism": f"replicas{world}" if world > 1 else "single", "ops_per_step": ops,
+                   "prompt_tokens_per_s": round(m * world * args.steps / (ms_max / 1e3) * L / PREFILL["layers"], 1),
+                   "graph": True, "l2": "weights larger than L2, streamed once per step", "per_projection": per_proj,
+                   "spec_frac": round(tops / world / TENSOR_I8_SPEC_TOPS, 4)},
+        "roofline": {"bound": "tensor", "achieved": round(tops / world, 1), "peak": round(peak, 1), "unit": "TOP/s",
+                     "frac": round(tops / world / peak, 4), "traffic": None,
+                     "kernel": "gemm_q4k_tc (tcgen05 kind::i8) incl. its activation packing",
+                     "peak_source": peak_src,
+                     "note": "exact integer path runs 2 int8 MMA passes per useful MAC (sc*q4 needs 10 bits)"},
+        "cpu_baseline": cpu_baseline,
+        "e2e": {"value": round(e2e_tops, 2), "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "edgexpu_cpu_linear_quant_batch (host buffers), one call per projection"},
+        "gpu_launches": L * (len(groups) + len(shapes)) * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    torch.cuda.synchronize()
+    pkg.shutdown()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gemv"], default="llama3_8b_q4k_decode")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gemv", "llama3_8b_q4k_prefill"],
+                    default="llama3_8b_q4k_decode")
     ap.add_argument("--wtype", choices=["q4_k", "q8_0"], default="q4_k", help="gemv workload: weight type")
     ap.add_argument("--shape", default="14336,4096", help="gemv workload: n_out,n_in")
     ap.add_argument("--rotate-bytes", type=float, default=512e6, help="gemv workload: total bytes of weight copies")
-    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--batch", type=int, default=0, help="tokens per step (default 1 for decode, 2048 for prefill)")
+    ap.add_argument("--layers", type=int, default=0, help="prefill workload: layers per step (0 = all 32)")
     ap.add_argument("--ref-layers", type=int, default=0, help="reference arm: layers per step (0 = all)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.batch <= 0:
+        args.batch = 2048 if args.workload == "llama3_8b_q4k_prefill" else 1
+    if args.workload == "llama3_8b_q4k_prefill":
+        (run_prefill_reference if args.impl == "reference" else run_prefill)(args)
+        return
     if args.workload == "gemv":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the gemv workload has no reference arm; "

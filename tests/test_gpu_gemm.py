@@ -1,9 +1,10 @@
 """GPU parity of the tensor-core prefill GEMM (Q4_K weights x Q8_K activations, m >= 64 rows).
 
 The GEMM splits the folded weight sc*q4 into an int8 low part and a high part and sums
-L = sum l*q8, H = sum h*q8, M = sum m*q8 on the tensor cores; (sumi, summ) = (L + 256 H, M) must
-equal the reference's int32 values bit for bit (dot_q4_k_q8_k, gguf_dot_q8.c:711-759), and the
-fp32 outputs must stay within 1e-5 * sum_k |w_k x_k| of the oracle.
+L = sum l*q8 and H = sum h*q8 on the tensor cores, and the mins term summ = sum_j m_j * S_j with
+dp4a on the CUDA cores; (sumi, summ) = (L + 256 H, summ) must equal the reference's int32 values
+bit for bit (dot_q4_k_q8_k, gguf_dot_q8.c:711-759), and the fp32 outputs must stay within
+1e-5 * sum_k |w_k x_k| of the oracle.
 """
 
 import ctypes
