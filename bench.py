@@ -171,6 +171,16 @@ class ClockSampler:
 # ---- distributed plumbing -----------------------------------------------------------------------
 
 
+def traffic_per_launch(alg_bytes):
+    """DRAM bytes per row-stream launch: the DRAM/algorithmic byte ratio that ncu measured on a
+    capturable case (profiles/traffic.json) applied to this launch's algorithmic bytes."""
+    try:
+        rs = json.loads(TRAFFIC.read_text())["rowstream"]
+        return int(round(alg_bytes * rs["dram_bytes_per_launch"] / rs["alg_bytes_per_launch"]))
+    except (OSError, ValueError, KeyError):
+        return None
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -496,12 +506,7 @@ def run_ours(args, wl):
     achieved = kern_bytes / kern_s / 1e9
     del g_k
     peak, peak_kind = peak_hbm()
-    traffic = None
-    try:
-        tr = json.loads(TRAFFIC.read_text())
-        traffic = tr.get(args.workload, {}).get(str(world))
-    except (OSError, ValueError):
-        pass
+    traffic = traffic_per_launch(kern_bytes / kern_launches)
 
     # End to end through the reference-named host shim: host buffers, H2D/D2H inside the timed region.
     hx = {n_in: ins[n_in].cpu().numpy() for n_in in ins}
@@ -719,7 +724,7 @@ def run_gemv(args):
                    "weight_copies": copies, "l2": f"rotating {copies} weight copies ({copies * wb} bytes) > L2",
                    "parallelism": "single"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "kernel_us": round(kern_ms * 1e3, 3),
+                     "frac": round(achieved / peak, 4), "traffic": traffic_per_launch(nbytes), "kernel_us": round(kern_ms * 1e3, 3),
                      "peak_source": f"{peak_kind} hbm_gbs"},
         "cpu_baseline": None,
         "e2e": {"value": round(nbytes * args.steps / e2e_s / 1e9, 2), "unit": "GB/s",
