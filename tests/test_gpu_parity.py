@@ -171,6 +171,42 @@ def test_linear_logits_shape_q4_k(gpu, port):
     assert_close(got, port.linear(x, w, TYPE_Q4_K, 128256), port.linear_bound(x, w, TYPE_Q4_K, 128256))
 
 
+@pytest.mark.parametrize("wtype,n_out,n_in", [(TYPE_Q4_K, 4096, 14336), (TYPE_Q4_K, 1024, 4096),
+                                               (TYPE_Q8_0, 1536, 576)])
+@pytest.mark.parametrize("m", [1, 2])
+def test_fused_quantization_prologue_is_bit_exact(gpu, port, wtype, n_out, n_in, m):
+    """At m <= 2 the GEMV quantizes the fp32 activations in its own prologue.  Fed the oracle's
+    quantized bytes instead (the pre-quantized path of the same kernel), it must give the same
+    output bits -- so the fused quantization is bit-exact, incl. zero blocks, sign ties and
+    constant blocks."""
+    torch = _torch()
+    s = _synth()
+    rng = np.random.default_rng(n_in + m)
+    w = s.weight(rng, wtype, n_out, n_in)
+    x = s.activations(rng, m, n_in)
+    b = 256 if wtype == TYPE_Q4_K else 32     # quantization block
+    x[0, :b] = 0.0                            # all-zero block
+    x[0, b:2 * b] = 1.0                       # constant block
+    x[0, 2 * b + 7] = 9.0
+    x[0, 2 * b + b // 2] = -9.0               # equal |max|: the first one sets the sign
+    x[m - 1, -b // 4:] = -1e-30               # tiny values in the last block
+    h = gpu.upload_weight(w, wtype, n_out, n_in)
+    try:
+        xd = torch.from_numpy(x).cuda()
+        xq = torch.from_numpy(port.quantize(x, wtype)).cuda()
+        fused = torch.full((m, n_out), float("nan"), device="cuda")
+        pre = torch.full((m, n_out), float("nan"), device="cuda")
+        cuda = gpu.load_cuda()
+        assert cuda.edgexpu_cuda_linear_quant_batch_dev(fused.data_ptr(), xd.data_ptr(), h, wtype, None, m, n_out,
+                                                        n_in, _stream())
+        assert cuda.edgexpu_cuda_dot_quant_q8_dev(pre.data_ptr(), xq.data_ptr(), h, wtype, None, m, n_out, n_in,
+                                                  _stream())
+        _sync(gpu)
+        np.testing.assert_array_equal(fused.cpu().numpy(), pre.cpu().numpy())
+    finally:
+        gpu.free_weight(h)
+
+
 def test_linear_row_subrange_and_dev_path(gpu, port):
     """A handle may point at any row of a registered tensor; the device-buffer entry point gives
     the same bits as the host-buffer one."""
