@@ -289,12 +289,19 @@ def cpu_run(wl, m, layers, vocab_rows, min_seconds, min_reps):
     return w.nbytes / sec / 1e9, sec, w.nbytes, w.threads
 
 
+def ref_sample_layers(wl, m, budget_bytes=0.6e9):
+    """Whole layers (with their share of the logits rows) per reference step, at most ~0.6 GB of
+    algorithmic bytes, so that a --steps K run of the CPU reference ends within minutes."""
+    per_layer = step_bytes(wl, m) / wl["layers"]
+    return max(1, min(wl["layers"], int(budget_bytes // per_layer)))
+
+
 def run_reference(args, wl):
     world, rank, _ = dist_env()
     if rank != 0:
         return
     m = args.batch
-    layers = args.ref_layers or wl["layers"]
+    layers = args.ref_layers or ref_sample_layers(wl, m)
     vocab_rows = wl["vocab"] * layers // wl["layers"]
     try:
         w = CpuWorkload(wl, m, layers, vocab_rows)
@@ -1032,7 +1039,8 @@ def main():
     ap.add_argument("--rotate-bytes", type=float, default=512e6, help="gemv workload: total bytes of weight copies")
     ap.add_argument("--batch", type=int, default=0, help="tokens per step (default 1 for decode, 2048 for prefill)")
     ap.add_argument("--layers", type=int, default=0, help="prefill workload: layers per step (0 = all 32)")
-    ap.add_argument("--ref-layers", type=int, default=0, help="reference arm: layers per step (0 = all)")
+    ap.add_argument("--ref-layers", type=int, default=0,
+                    help="reference arm: layers per step (0 = a sample of about 0.6 GB per step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.batch <= 0:
