@@ -402,12 +402,20 @@ def run_ours(args, wl):
     buf = ctypes.create_string_buffer(512)
     for n_in in ins:
         assert cuda.edgexpu_cuda_reserve(m, n_in, buf, 512), buf.value
+    p2p = tp and args.collective == "p2p"
+    if p2p:
+        from edgexpu_llm_b200 import tp as tpmod
+
+        tpmod.connect_p2p(cuda, world, rank)
 
     def enqueue_gemvs(st, collectives):
         for lay, ga in zip(layers, group_args):
             for n_t, out_arr, w_arr, n_arr, grp in ga:
                 label, n_out, n_in, kind = shapes[grp[0]]
-                if n_t == 1:
+                if n_t == 1 and p2p and kind == "col":  # GEMV with its all-reduce over NVLink, one launch
+                    ok = cuda.edgexpu_cuda_linear_quant_batch_tp_dev(out_arr[0], ins[n_in].data_ptr(), w_arr[0], t, None,
+                                                                     m, n_out, n_in, st)
+                elif n_t == 1:
                     ok = cuda.edgexpu_cuda_linear_quant_batch_dev(out_arr[0], ins[n_in].data_ptr(), w_arr[0], t, None, m,
                                                                   n_out, n_in, st)
                 else:
@@ -415,7 +423,7 @@ def run_ours(args, wl):
                                                                   ins[n_in].data_ptr(), m, n_in, st)
                 if not ok:
                     raise RuntimeError(cuda.edgexpu_cuda_last_error().decode())
-                if collectives and tp and kind == "col":
+                if collectives and tp and kind == "col" and not p2p:
                     dist.all_reduce(outs[label])
 
     def enqueue_step():
@@ -587,7 +595,9 @@ def run_ours(args, wl):
         "config": {"workload": args.workload, "batch": m,
                    "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
                    "bytes_per_step": total_bytes, "l2": "inputs larger than L2 (weights streamed once per step)",
-                   "graph": graph is not None, "tokens_per_s_gemv_only": round(args.steps / (ms_max / 1e3) * m, 2)},
+                   "graph": graph is not None, "tokens_per_s_gemv_only": round(args.steps / (ms_max / 1e3) * m, 2),
+                   "collective": ("o/down all-reduce inside the GEMV over NVLink (P2P stores), argmax via NCCL"
+                                  if p2p else ("NCCL all-reduce after o/down, NCCL argmax" if tp else "none"))},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "rowstream GEMV (Q4_K x Q8_K)" if t == TYPE_Q4_K else "rowstream GEMV (Q8_0 x Q8_0)",
@@ -603,6 +613,8 @@ def run_ours(args, wl):
         print(json.dumps(line), flush=True)
     graph = None
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # no rank unmaps its exchange region while a peer may still write to it
     pkg.shutdown()
     if world > 1:
         dist.barrier()
@@ -1042,6 +1054,8 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=0,
                     help="reference arm: layers per step (0 = a sample of about 0.6 GB per step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--collective", choices=["p2p", "nccl"], default="p2p",
+                    help="tensor parallel: all-reduce of o/down inside the GEMV over NVLink (p2p) or NCCL after it")
     args = ap.parse_args()
     if args.batch <= 0:
         args.batch = 2048 if args.workload == "llama3_8b_q4k_prefill" else 1

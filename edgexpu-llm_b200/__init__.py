@@ -61,6 +61,11 @@ _CUDA_SIGS = {
     "edgexpu_cuda_block_partials_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_int, _c_int, _c_int, _c_vp]),
     "edgexpu_cuda_reserve": (_c_int, [_c_int, _c_int, _c_str, _c_sz]),
     "edgexpu_cuda_stream_sync": (_c_int, [_c_vp, _c_str, _c_sz]),
+    "edgexpu_cuda_tp_init": (_c_int, [_c_int, _c_int, _c_vp, _c_str, _c_sz]),
+    "edgexpu_cuda_tp_connect": (_c_int, [_c_vp, _c_str, _c_sz]),
+    "edgexpu_cuda_tp_shutdown": (_c_int, []),
+    "edgexpu_cuda_linear_quant_batch_tp_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int,
+                                                        _c_vp]),
 }
 
 _HOST_SIGS = {

@@ -323,6 +323,7 @@ int edgexpu_cuda_shutdown(void) {
   if (!g.ready) return 1;
   cudaSetDevice(g.device);
   cudaDeviceSynchronize();
+  ex::tp_release();
   for (auto& kv : g.weights)
     if (kv.second.owned) cudaFree(reinterpret_cast<void*>(kv.first));
   g.weights.clear();
@@ -640,5 +641,8 @@ int api_device() { return g.device; }
 uint32_t* api_status_word() { return g.d_status; }
 size_t api_row_bytes(uint32_t type, int n) { return row_bytes_of(type, n); }
 size_t api_act_row_bytes(uint32_t type, int n) { return act_row_bytes_of(type, n); }
+void* api_act_scratch(size_t bytes, cudaStream_t st, char* error, size_t error_size) {
+  return grow_dev(g.xq, bytes, st, error, error_size) ? g.xq.p : nullptr;
+}
 
 }  // namespace ex

@@ -6,6 +6,8 @@
 #include <cstdint>
 #include <mutex>
 
+#include <cuda_runtime.h>
+
 #include "launch.h"
 
 namespace ex {
@@ -23,5 +25,9 @@ int api_device();
 uint32_t* api_status_word();
 size_t api_row_bytes(uint32_t type, int n);
 size_t api_act_row_bytes(uint32_t type, int n);
+// Device scratch of at least `bytes` (the library's activation buffer, grown outside stream capture).
+void* api_act_scratch(size_t bytes, cudaStream_t st, char* error, size_t error_size);
+// Close the tensor-parallel peer mappings and free the local region (tp_p2p.cu); no-op if unused.
+void tp_release();
 
 }  // namespace ex

@@ -25,6 +25,7 @@ constexpr uint32_t TYPE_Q4_K = 12;  // EDGEXPU_GGUF_TYPE_Q4_K, include/edgexpu/g
 constexpr uint32_t ST_TIMEOUT_FULL = 1u;   // a consumer gave up waiting for a tile copy
 constexpr uint32_t ST_TIMEOUT_EMPTY = 2u;  // the producer gave up waiting for a free stage
 constexpr uint32_t ST_TIMEOUT_DRAIN = 4u;  // copies still in flight at exit after the limit
+constexpr uint32_t ST_TIMEOUT_PEER = 8u;   // a tensor-parallel peer did not deliver its partial in time
 
 // Every mbarrier wait gives up after this long and reports through the status word.
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // 2 s

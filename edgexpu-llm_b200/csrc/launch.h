@@ -36,6 +36,20 @@ struct RowSeg {
 };
 constexpr int MAX_SEGS = 4;
 
+// Tensor-parallel all-reduce over peer memory (tp_p2p.cu).  Every rank holds one region of the
+// same layout; peer[r] is rank r's region mapped into this process (peer[rank] = the local one).
+constexpr int TP_MAX_WORLD = 8;
+constexpr size_t TP_SLOT_BYTES = 512 * 1024;                             // one rank's partials: 65536 u64 entries
+constexpr size_t TP_DATA_BYTES = 2 * TP_MAX_WORLD * TP_SLOT_BYTES;       // [parity][rank] (value, tag) words
+constexpr size_t TP_CTRL_OFF = TP_DATA_BYTES;                            // u32 CTA counter, u32 epoch
+constexpr size_t TP_REGION_BYTES = TP_CTRL_OFF + 256;
+
+struct TpArgs {
+  int world;                       // 0 or 1: no all-reduce
+  int rank;
+  uint8_t* peer[TP_MAX_WORLD];
+};
+
 struct RowStreamArgs {
   Fmt fmt;
   RowOut mode;
@@ -56,6 +70,7 @@ struct RowStreamArgs {
   uint32_t* status;       // device-visible status word
   int n_seg;              // 0: one tensor (w, n_rows, bias, out, out_stride); 1..MAX_SEGS: seg[] (Store only)
   RowSeg seg[MAX_SEGS];
+  TpArgs tp;              // Store, one tensor: sum the outputs of all ranks into out (column-sharded weights)
 };
 
 struct DeviceInfo {

@@ -462,6 +462,65 @@ __device__ __forceinline__ TileRef tile_ref(const RowStreamArgs& a, const Layout
   return t;
 }
 
+// ---- tensor-parallel all-reduce over peer memory -------------------------------------------------
+// Each partial output travels with its own flag: the consumer lane that computes output (t, row)
+// stores the 64-bit word (float bits, tag = epoch + 1) into entry [parity][rank][t*n + row] of every
+// rank's exchange region (CUDA IPC mappings over NVLink).  An aligned 64-bit store is single-copy
+// atomic, so a reader that sees the current tag also sees that store's value -- no fences, no
+// separate flag.  After its own rows, each CTA polls (bounded) the entries of those rows in the
+// local region until every rank's tag is current and sums them in rank order, so every rank gets
+// the same bits.  The row-to-CTA map is the same on every rank.  Parity: a rank writes parity p
+// again only in launch e + 2, which starts after its launch e + 1 read every peer's entries of
+// e + 1, which the peers wrote only after finishing their launch e (and its reads).
+__device__ __forceinline__ void st_relaxed_sys_u64(void* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const void* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ void tp_finalize(const RowStreamArgs& a, const Layout& L, uint32_t e, int ct) {
+  const uint8_t* local = a.tp.peer[a.tp.rank];
+  uint32_t* counter = reinterpret_cast<uint32_t*>(a.tp.peer[a.tp.rank] + TP_CTRL_OFF);
+  const uint32_t f = e + 1u;
+  const int n = static_cast<int>(a.seg[0].n_rows);
+  const unsigned long long* slots =
+      reinterpret_cast<const unsigned long long*>(local + static_cast<size_t>(e & 1u) * TP_MAX_WORLD * TP_SLOT_BYTES);
+  const size_t per_rank = TP_SLOT_BYTES / 8;
+  const unsigned long long t0 = global_ns();
+  bool ok = true;
+  for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
+    const TileRef tr = tile_ref(a, L, tile);
+    const int cnt = tr.nr * a.m;
+    for (int i = ct; i < cnt; i += CONSUMERS) {
+      const int t = i / tr.nr, row = static_cast<int>(tr.r0) + (i - t * tr.nr);
+      const size_t idx = static_cast<size_t>(t) * n + row;
+      float sum = 0.0f;
+      for (int r = 0; r < a.tp.world; ++r) {  // rank order: the same additions on every rank
+        unsigned long long v = ld_relaxed_sys_u64(slots + r * per_rank + idx);
+        for (uint32_t k = 0; ok && static_cast<uint32_t>(v >> 32) != f; ++k) {
+          if ((k & 63u) == 63u && global_ns() - t0 > WAIT_LIMIT_NS) ok = false;
+          v = ld_relaxed_sys_u64(slots + r * per_rank + idx);
+        }
+        sum += __uint_as_float(static_cast<uint32_t>(v));
+      }
+      a.seg[0].out[static_cast<size_t>(t) * a.out_stride + row] = sum;
+    }
+  }
+  if (!ok) atomicOr(a.status, ST_TIMEOUT_PEER);
+  // Advance the epoch once every CTA of this launch is done with it (it read it at its start).
+  named_bar_sync(2, CONSUMERS);
+  if (ct == 0) {
+    __threadfence();
+    if (atomicAdd(counter, 1u) == gridDim.x - 1) {
+      counter[0] = 0u;
+      counter[1] = e + 1u;  // the next launch reads it after its griddepcontrol.wait
+    }
+  }
+}
+
 template <Fmt F, RowOut MODE, int MTOK, bool XREG>
 __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamArgs a, const Layout L) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -524,6 +583,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   const int cw = warp - 1;
   uint8_t* act = smem + L.act_off;
   griddep_wait();  // the activations may be the previous grid's output
+  const bool tp_on = MODE == RowOut::Store && a.tp.world > 1;
+  const uint32_t tp_e = tp_on ? *reinterpret_cast<volatile const uint32_t*>(a.tp.peer[a.tp.rank] + TP_CTRL_OFF + 4) : 0u;
+  const size_t tp_slot =
+      tp_on ? (static_cast<size_t>(tp_e & 1u) * TP_MAX_WORLD + a.tp.rank) * TP_SLOT_BYTES : 0;  // [parity][rank]
   load_act(a, act, threadIdx.x - 32);
   named_bar_sync(1, CONSUMERS);
 
@@ -573,7 +636,13 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
             if (lane < a.m) {
               const float y = (tr.bias != nullptr ? tr.bias[row] : 0.0f) + mine;  // cpu_kernel.c:596-597
               if constexpr (MODE == RowOut::Store) {
-                tr.out[static_cast<size_t>(lane) * tr.stride + row] = y;
+                if (tp_on) {  // (partial, tag) into entry [parity][rank][t*n + row] of every rank
+                  const size_t off = tp_slot + (static_cast<size_t>(lane) * a.seg[0].n_rows + row) * 8;
+                  const unsigned long long v = (static_cast<unsigned long long>(tp_e + 1u) << 32) | __float_as_uint(y);
+                  for (int r = 0; r < a.tp.world; ++r) st_relaxed_sys_u64(a.tp.peer[r] + off, v);
+                } else {
+                  tr.out[static_cast<size_t>(lane) * tr.stride + row] = y;
+                }
               } else {
                 const unsigned long long k = argmax_key(y, static_cast<uint32_t>(a.row0 + row));
                 best = k > best ? k : best;
@@ -592,6 +661,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
       fphase ^= 1u;
     }
   }
+  if (tp_on) tp_finalize(a, L, tp_e, threadIdx.x - 32);
   if constexpr (MODE == RowOut::Argmax) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {

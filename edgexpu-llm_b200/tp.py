@@ -103,3 +103,24 @@ def make_key(score: float, token: int) -> int:
 def key_as_int64(key: int) -> int:
     """Unsigned 64-bit key -> the int64 with the same bits (for int64 tensor storage)."""
     return key - (1 << 64) if key >= (1 << 63) else key
+
+
+def connect_p2p(cuda_lib, world: int, rank: int, group=None) -> None:
+    """Set up the in-GEMV all-reduce of column-sharded projections: allocate this rank's exchange
+    region, exchange the CUDA IPC handles over torch.distributed and open the peers' regions.
+    After this, ``edgexpu_cuda_linear_quant_batch_tp_dev`` returns the summed output on every
+    rank (no separate collective)."""
+    import ctypes
+
+    import torch.distributed as dist
+
+    err = ctypes.create_string_buffer(512)
+    handle = (ctypes.c_uint8 * 64)()
+    if not cuda_lib.edgexpu_cuda_tp_init(world, rank, handle, err, 512):
+        raise RuntimeError(err.value.decode())
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(handle), group=group)
+    blob = b"".join(handles)
+    if not cuda_lib.edgexpu_cuda_tp_connect(blob, err, 512):
+        raise RuntimeError(err.value.decode())
+    dist.barrier(group=group)

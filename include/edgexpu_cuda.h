@@ -141,6 +141,29 @@ int edgexpu_cuda_reserve(int m, int n_in, char *error, size_t error_size);
 /* Wait for `stream`, then report any device-side timeout recorded by the kernels. */
 int edgexpu_cuda_stream_sync(void *stream, char *error, size_t error_size);
 
+/* ---- tensor parallelism: column-sharded linear with the all-reduce inside the GEMV ----------
+ * No counterpart in the reference (it is single-process).  One process per GPU.  The o and down
+ * projections of a tensor-parallel layer shard their weights by input columns (at 256-element
+ * block boundaries, so the Q8_K quantization of each shard is that of the full row), so every rank
+ * holds a partial of the whole output.  edgexpu_cuda_linear_quant_batch_tp_dev computes this
+ * rank's partial and sums the partials of all ranks in the same launch: every partial output is
+ * stored, tagged with the launch's epoch in the same 64-bit word, into every rank's exchange
+ * region (CUDA IPC mappings over NVLink), and each CTA waits for the tagged partials of its own
+ * rows (bounded; a peer that does not deliver within 2 s sets a status error) and adds them in
+ * rank order.  Every rank gets the same bits.  Set-up: tp_init on every rank, exchange the handles (EDGEXPU_CUDA_TP_HANDLE_BYTES
+ * each) with any host channel, tp_connect with all `world` handles in rank order, then a barrier.
+ * All ranks must make the same sequence of _tp_dev calls, one at a time per process. */
+#define EDGEXPU_CUDA_TP_HANDLE_BYTES 64
+int edgexpu_cuda_tp_init(int world, int rank, uint8_t *handle_out, char *error, size_t error_size);
+int edgexpu_cuda_tp_connect(const uint8_t *handles, char *error, size_t error_size);
+int edgexpu_cuda_tp_shutdown(void);
+/* out[t*n_out + o] = bias[o] + sum over ranks of dot(W_rank,o, quantize(x_rank,t)); `weight` is this
+ * rank's column shard (n_out rows of n_in = its share of the input), x this rank's slice of the
+ * activations; bias (full, may be NULL) is applied once.  Rows are processed in launches of up to
+ * min(the GEMV's row limit, 65536 / n_out); n_out may be at most 65536. */
+int edgexpu_cuda_linear_quant_batch_tp_dev(float *out, const float *x, const uint8_t *weight, uint32_t type,
+                                           const float *bias, int m, int n_out, int n_in, void *stream);
+
 /* Token id encoded in an argmax key (0 when no row had a finite score). */
 static inline uint32_t edgexpu_cuda_argmax_key_id(uint64_t key) {
     return key == 0 ? 0u : 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);

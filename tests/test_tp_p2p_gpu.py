@@ -1,0 +1,97 @@
+"""Tensor-parallel linear with the all-reduce inside the GEMV (edgexpu_cuda_linear_quant_batch_tp_dev),
+on two GPUs: two processes, CUDA IPC exchange regions, partials written over NVLink.
+
+Checks: the summed output matches the oracle's unsharded linear within the usual bound; both ranks
+hold the same bits; repeated calls (both parities of the exchange slots) give the same bits.
+Skipped on boxes with fewer than two GPUs."""
+
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CASES = [(12, 4096, 4096, 1), (12, 4096, 14336, 2), (12, 1024, 2048, 5), (8, 576, 1536, 3),
+         (12, 14336, 4096, 6)]  # the last: 4 rows per exchange slot, two launches
+
+
+def _rank_main(rank, world, port, result_dir):
+    import sys
+
+    import torch
+    import torch.distributed as dist
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    from _oracle import load_pkg
+
+    pkg = load_pkg()
+    from edgexpu_llm_b200 import synth, tp
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.cuda.set_device(rank)
+    pkg.init(rank)
+    cuda = pkg.load_cuda()
+    tp.connect_p2p(cuda, world, rank)
+    out = {}
+    for wtype, n_out, n_in, m in CASES:
+        rng = np.random.default_rng(n_out + n_in + m)
+        w = synth.weight(rng, wtype, n_out, n_in)
+        x = synth.activations(rng, m, n_in)
+        bias = rng.standard_normal(n_out).astype(np.float32)
+        c0, per = tp.col_range(n_in, wtype, world, rank)
+        ws = tp.shard_cols(w, n_in, wtype, world, rank)
+        h = pkg.upload_weight(ws, wtype, n_out, per)
+        xd = torch.from_numpy(np.ascontiguousarray(x[:, c0:c0 + per])).cuda()
+        bd = torch.from_numpy(bias).cuda()
+        st = torch.cuda.current_stream().cuda_stream
+        runs = []
+        for _ in range(3):
+            o = torch.full((m, n_out), float("nan"), device="cuda")
+            ok = cuda.edgexpu_cuda_linear_quant_batch_tp_dev(o.data_ptr(), xd.data_ptr(), h, wtype, bd.data_ptr(), m,
+                                                             n_out, per, st)
+            assert ok, cuda.edgexpu_cuda_last_error()
+            runs.append(o)
+        buf = __import__("ctypes").create_string_buffer(512)
+        assert cuda.edgexpu_cuda_stream_sync(st, buf, 512), buf.value
+        res = [r.cpu().numpy() for r in runs]
+        out[(wtype, n_out, n_in, m)] = res
+        pkg.free_weight(h)
+    dist.barrier()
+    cuda.edgexpu_cuda_tp_shutdown()
+    pkg.shutdown()
+    np.savez(os.path.join(result_dir, f"rank{rank}.npz"),
+             **{f"{k[0]}_{k[1]}_{k[2]}_{k[3]}_{i}": v for k, vs in out.items() for i, v in enumerate(vs)})
+    dist.destroy_process_group()
+
+
+def test_tp_linear_allreduce_in_gemv_two_gpus(tmp_path, port):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import random
+
+    import torch.multiprocessing as mp
+
+    mp.spawn(_rank_main, args=(2, random.randint(20000, 40000), str(tmp_path)), nprocs=2, join=True)
+    from test_oracle import _synth
+    from test_gpu_parity import assert_close
+
+    s = _synth()
+    r0 = np.load(tmp_path / "rank0.npz")
+    r1 = np.load(tmp_path / "rank1.npz")
+    for wtype, n_out, n_in, m in CASES:
+        rng = np.random.default_rng(n_out + n_in + m)
+        w = s.weight(rng, wtype, n_out, n_in)
+        x = s.activations(rng, m, n_in)
+        bias = rng.standard_normal(n_out).astype(np.float32)
+        key = f"{wtype}_{n_out}_{n_in}_{m}"
+        got = r0[key + "_0"]
+        for i in range(3):  # every call, both ranks: the same bits
+            np.testing.assert_array_equal(r0[key + f"_{i}"], got)
+            np.testing.assert_array_equal(r1[key + f"_{i}"], got)
+        assert_close(got, port.linear(x, w, wtype, n_out, bias), port.linear_bound(x, w, wtype, n_out),
+                     1e-7 * np.abs(bias)[None, :] + 1e-6)
