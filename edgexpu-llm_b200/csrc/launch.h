@@ -17,6 +17,7 @@ enum class RowOut : int {
   Store = 0,     // out[t*out_stride + r] = bias[r] + dot
   Argmax = 1,    // atomicMax of argmax_key(bias[r] + dot, row0 + r) into *key (m == 1)
   Partials = 2,  // per-block int32 partials instead of the float dot (test hook)
+  StoreTp = 3,   // Store of the sum over the tensor-parallel group (RowStreamArgs::tp), one tensor
 };
 
 enum class Fmt : int {
@@ -42,6 +43,7 @@ constexpr int TP_MAX_WORLD = 8;
 constexpr size_t TP_SLOT_BYTES = 512 * 1024;                             // one rank's partials: 65536 u64 entries
 constexpr size_t TP_DATA_BYTES = 2 * TP_MAX_WORLD * TP_SLOT_BYTES;       // [parity][rank] (value, tag) words
 constexpr size_t TP_CTRL_OFF = TP_DATA_BYTES;                            // u32 CTA counter, u32 epoch
+constexpr int TP_DIRECT_WORLD = 4;  // up to this many ranks each output goes to the peers as it is computed
 constexpr size_t TP_REGION_BYTES = TP_CTRL_OFF + 256;
 
 struct TpArgs {

@@ -464,14 +464,18 @@ __device__ __forceinline__ TileRef tile_ref(const RowStreamArgs& a, const Layout
 
 // ---- tensor-parallel all-reduce over peer memory -------------------------------------------------
 // Each partial output travels with its own flag: the consumer lane that computes output (t, row)
-// stores the 64-bit word (float bits, tag = epoch + 1) into entry [parity][rank][t*n + row] of every
-// rank's exchange region (CUDA IPC mappings over NVLink).  An aligned 64-bit store is single-copy
-// atomic, so a reader that sees the current tag also sees that store's value -- no fences, no
-// separate flag.  After its own rows, each CTA polls (bounded) the entries of those rows in the
-// local region until every rank's tag is current and sums them in rank order, so every rank gets
-// the same bits.  The row-to-CTA map is the same on every rank.  Parity: a rank writes parity p
-// again only in launch e + 2, which starts after its launch e + 1 read every peer's entries of
-// e + 1, which the peers wrote only after finishing their launch e (and its reads).
+// writes the 64-bit word (float bits, tag = epoch + 1) to entry [parity][rank][t*n + row] of every
+// rank's exchange region (CUDA IPC mappings over NVLink). Up to TP_DIRECT_WORLD ranks the lane
+// stores to every peer as soon as it has the value (the stores overlap the remaining tiles); with
+// more ranks the one-word-per-output NVLink writes cost more than they overlap (measured: 4096
+// outputs x 7 peers added ~4 us per launch), so the lane writes only the local entry and after its
+// last tile the CTA copies its entries to every peer with coalesced stores. An aligned 64-bit store
+// is single-copy atomic, so a reader that sees the current tag also sees that store's value -- no
+// fences, no separate flag. Each CTA then polls (bounded) the entries of its own rows in the local
+// region until every rank's tag is current and sums them in rank order, so every rank gets the same
+// bits. The row-to-CTA map is the same on every rank. Parity: a rank writes parity p again only in
+// launch e + 2, which starts after its launch e + 1 read every peer's entries of e + 1, which the
+// peers wrote only after finishing their launch e (and its reads).
 __device__ __forceinline__ void st_relaxed_sys_u64(void* p, unsigned long long v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -489,6 +493,23 @@ __device__ void tp_finalize(const RowStreamArgs& a, const Layout& L, uint32_t e,
   const unsigned long long* slots =
       reinterpret_cast<const unsigned long long*>(local + static_cast<size_t>(e & 1u) * TP_MAX_WORLD * TP_SLOT_BYTES);
   const size_t per_rank = TP_SLOT_BYTES / 8;
+  // Push (more than TP_DIRECT_WORLD ranks): this CTA's own entries, written by its consumer warps
+  // before the barrier, go to every peer as warp-wide stores of consecutive rows -- a few large
+  // NVLink writes instead of one 8-byte write per output and peer.
+  const size_t own = static_cast<size_t>(a.tp.rank) * per_rank;
+  if (a.tp.world > TP_DIRECT_WORLD) named_bar_sync(2, CONSUMERS);
+  for (long long tile = a.tp.world > TP_DIRECT_WORLD ? blockIdx.x : L.n_tiles; tile < L.n_tiles; tile += gridDim.x) {
+    const TileRef tr = tile_ref(a, L, tile);
+    const int cnt = tr.nr * a.m;
+    for (int i = ct; i < cnt; i += CONSUMERS) {
+      const int t = i / tr.nr, row = static_cast<int>(tr.r0) + (i - t * tr.nr);
+      const size_t idx = static_cast<size_t>(t) * n + row;
+      const unsigned long long v = slots[own + idx];  // written by this CTA before the barrier
+      const size_t off = reinterpret_cast<const uint8_t*>(slots + own + idx) - local;
+      for (int r = 0; r < a.tp.world; ++r)
+        if (r != a.tp.rank) st_relaxed_sys_u64(a.tp.peer[r] + off, v);
+    }
+  }
   const unsigned long long t0 = global_ns();
   bool ok = true;
   for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
@@ -497,14 +518,21 @@ __device__ void tp_finalize(const RowStreamArgs& a, const Layout& L, uint32_t e,
     for (int i = ct; i < cnt; i += CONSUMERS) {
       const int t = i / tr.nr, row = static_cast<int>(tr.r0) + (i - t * tr.nr);
       const size_t idx = static_cast<size_t>(t) * n + row;
+      // All ranks' entries in flight at once (one L2 round trip when they have arrived), then
+      // re-poll only the stale ones.
+      unsigned long long v[TP_MAX_WORLD];
+#pragma unroll
+      for (int r = 0; r < TP_MAX_WORLD; ++r)
+        if (r < a.tp.world) v[r] = ld_relaxed_sys_u64(slots + r * per_rank + idx);
       float sum = 0.0f;
-      for (int r = 0; r < a.tp.world; ++r) {  // rank order: the same additions on every rank
-        unsigned long long v = ld_relaxed_sys_u64(slots + r * per_rank + idx);
-        for (uint32_t k = 0; ok && static_cast<uint32_t>(v >> 32) != f; ++k) {
+#pragma unroll
+      for (int r = 0; r < TP_MAX_WORLD; ++r) {  // rank order: the same additions on every rank
+        if (r >= a.tp.world) break;
+        for (uint32_t k = 0; ok && static_cast<uint32_t>(v[r] >> 32) != f; ++k) {
           if ((k & 63u) == 63u && global_ns() - t0 > WAIT_LIMIT_NS) ok = false;
-          v = ld_relaxed_sys_u64(slots + r * per_rank + idx);
+          v[r] = ld_relaxed_sys_u64(slots + r * per_rank + idx);
         }
-        sum += __uint_as_float(static_cast<uint32_t>(v));
+        sum += __uint_as_float(static_cast<uint32_t>(v[r]));
       }
       a.seg[0].out[static_cast<size_t>(t) * a.out_stride + row] = sum;
     }
@@ -583,10 +611,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   const int cw = warp - 1;
   uint8_t* act = smem + L.act_off;
   griddep_wait();  // the activations may be the previous grid's output
-  const bool tp_on = MODE == RowOut::Store && a.tp.world > 1;
-  const uint32_t tp_e = tp_on ? *reinterpret_cast<volatile const uint32_t*>(a.tp.peer[a.tp.rank] + TP_CTRL_OFF + 4) : 0u;
+  constexpr bool TP = MODE == RowOut::StoreTp;
+  const uint32_t tp_e = TP ? *reinterpret_cast<volatile const uint32_t*>(a.tp.peer[a.tp.rank] + TP_CTRL_OFF + 4) : 0u;
   const size_t tp_slot =
-      tp_on ? (static_cast<size_t>(tp_e & 1u) * TP_MAX_WORLD + a.tp.rank) * TP_SLOT_BYTES : 0;  // [parity][rank]
+      TP ? (static_cast<size_t>(tp_e & 1u) * TP_MAX_WORLD + a.tp.rank) * TP_SLOT_BYTES : 0;  // [parity][rank]
   load_act(a, act, threadIdx.x - 32);
   named_bar_sync(1, CONSUMERS);
 
@@ -635,14 +663,16 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
             }
             if (lane < a.m) {
               const float y = (tr.bias != nullptr ? tr.bias[row] : 0.0f) + mine;  // cpu_kernel.c:596-597
-              if constexpr (MODE == RowOut::Store) {
-                if (tp_on) {  // (partial, tag) into entry [parity][rank][t*n + row] of every rank
-                  const size_t off = tp_slot + (static_cast<size_t>(lane) * a.seg[0].n_rows + row) * 8;
-                  const unsigned long long v = (static_cast<unsigned long long>(tp_e + 1u) << 32) | __float_as_uint(y);
+              if constexpr (TP) {  // (partial, tag) into entry [parity][rank][t*n + row]: every rank's, or ours
+                const size_t off = tp_slot + (static_cast<size_t>(lane) * a.seg[0].n_rows + row) * 8;
+                const unsigned long long v = (static_cast<unsigned long long>(tp_e + 1u) << 32) | __float_as_uint(y);
+                if (a.tp.world <= TP_DIRECT_WORLD) {
                   for (int r = 0; r < a.tp.world; ++r) st_relaxed_sys_u64(a.tp.peer[r] + off, v);
-                } else {
-                  tr.out[static_cast<size_t>(lane) * tr.stride + row] = y;
+                } else {  // tp_finalize pushes it
+                  *reinterpret_cast<unsigned long long*>(a.tp.peer[a.tp.rank] + off) = v;
                 }
+              } else if constexpr (MODE == RowOut::Store) {
+                tr.out[static_cast<size_t>(lane) * tr.stride + row] = y;
               } else {
                 const unsigned long long k = argmax_key(y, static_cast<uint32_t>(a.row0 + row));
                 best = k > best ? k : best;
@@ -661,7 +691,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
       fphase ^= 1u;
     }
   }
-  if (tp_on) tp_finalize(a, L, tp_e, threadIdx.x - 32);
+  if constexpr (TP) tp_finalize(a, L, tp_e, threadIdx.x - 32);
   if constexpr (MODE == RowOut::Argmax) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -726,6 +756,8 @@ cudaError_t launch_rowstream(const RowStreamArgs& in, const DeviceInfo& dev, cud
     a.n_rows = 0;
     for (int i = 0; i < a.n_seg; ++i) a.n_rows += a.seg[i].n_rows;
   }
+  if (a.mode == RowOut::StoreTp && (a.tp.world < 2 || a.tp.world > TP_MAX_WORLD || a.fmt == Fmt::Q4_KxF32))
+    return cudaErrorInvalidValue;
   if (a.n_rows <= 0 || a.m <= 0) return cudaSuccess;
   if (a.m > MAX_M || a.K % (a.fmt == Fmt::Q8_0xQ8_0 ? QK8_0 : QK_K) != 0) return cudaErrorInvalidValue;
   Layout L{};
@@ -753,10 +785,12 @@ cudaError_t launch_rowstream(const RowStreamArgs& in, const DeviceInfo& dev, cud
   switch (a.fmt) {
     case Fmt::Q8_0xQ8_0:
       if (a.mode == RowOut::Store) return launch_mtok<Fmt::Q8_0xQ8_0, RowOut::Store>(a, L, grid, st);
+      if (a.mode == RowOut::StoreTp) return launch_mtok<Fmt::Q8_0xQ8_0, RowOut::StoreTp>(a, L, grid, st);
       if (a.mode == RowOut::Argmax) return launch_mtok<Fmt::Q8_0xQ8_0, RowOut::Argmax>(a, L, grid, st);
       return launch_mtok<Fmt::Q8_0xQ8_0, RowOut::Partials>(a, L, grid, st);
     case Fmt::Q4_KxQ8_K:
       if (a.mode == RowOut::Store) return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::Store>(a, L, grid, st);
+      if (a.mode == RowOut::StoreTp) return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::StoreTp>(a, L, grid, st);
       if (a.mode == RowOut::Argmax) return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::Argmax>(a, L, grid, st);
       return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::Partials>(a, L, grid, st);
     default:

@@ -4,10 +4,11 @@
 // every rank computes a partial of the whole output and the partials must be summed.  Instead of
 // a GEMV launch followed by a collective, the row-stream GEMV stores every partial output, tagged
 // with the launch's epoch in the same 64-bit word, into every rank's exchange region (NVLink
-// stores through CUDA IPC mappings); each CTA then waits for the tagged partials of its own rows
-// in local memory and sums them in rank order (rowstream.cu, tp_finalize).  One launch per
-// projection, no separate collective kernel, no fences, and the same additions in the same order
-// on every rank.
+// stores through CUDA IPC mappings: as each output is computed with up to 4 ranks, as coalesced
+// per-CTA copies after the last tile with more); each CTA then waits for the tagged partials of
+// its own rows in local memory and sums them in rank order (rowstream.cu, tp_finalize).  One
+// launch per projection, no separate collective kernel, no fences, and the same additions in the
+// same order on every rank.
 //
 // Set-up, once per process (one process per GPU): edgexpu_cuda_tp_init allocates the local region
 // and exports its IPC handle; the caller exchanges the handles (e.g. torch.distributed
@@ -138,7 +139,7 @@ int edgexpu_cuda_linear_quant_batch_tp_dev(float* out, const float* x, const uin
   for (int t0 = 0; t0 < m; t0 += chunk) {
     ex::RowStreamArgs a{};
     a.fmt = fmt;
-    a.mode = ex::RowOut::Store;
+    a.mode = ex::RowOut::StoreTp;
     a.w = weight;
     a.n_rows = n_out;
     a.row0 = 0;

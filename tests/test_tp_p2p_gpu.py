@@ -1,9 +1,9 @@
 """Tensor-parallel linear with the all-reduce inside the GEMV (edgexpu_cuda_linear_quant_batch_tp_dev),
-on two GPUs: two processes, CUDA IPC exchange regions, partials written over NVLink.
+on 2, 4 and 8 GPUs: one process per GPU, CUDA IPC exchange regions, partials written over NVLink.
 
 Checks: the summed output matches the oracle's unsharded linear within the usual bound; both ranks
 hold the same bits; repeated calls (both parities of the exchange slots) give the same bits.
-Skipped on boxes with fewer than two GPUs."""
+Each world size is skipped on boxes with fewer GPUs."""
 
 import os
 
@@ -67,31 +67,31 @@ def _rank_main(rank, world, port, result_dir):
     dist.destroy_process_group()
 
 
-def test_tp_linear_allreduce_in_gemv_two_gpus(tmp_path, port):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_linear_allreduce_in_gemv(tmp_path, port, world):
     import torch
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import random
 
     import torch.multiprocessing as mp
 
-    mp.spawn(_rank_main, args=(2, random.randint(20000, 40000), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_rank_main, args=(world, random.randint(20000, 40000), str(tmp_path)), nprocs=world, join=True)
     from test_oracle import _synth
     from test_gpu_parity import assert_close
 
     s = _synth()
-    r0 = np.load(tmp_path / "rank0.npz")
-    r1 = np.load(tmp_path / "rank1.npz")
+    ranks = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     for wtype, n_out, n_in, m in CASES:
         rng = np.random.default_rng(n_out + n_in + m)
         w = s.weight(rng, wtype, n_out, n_in)
         x = s.activations(rng, m, n_in)
         bias = rng.standard_normal(n_out).astype(np.float32)
         key = f"{wtype}_{n_out}_{n_in}_{m}"
-        got = r0[key + "_0"]
-        for i in range(3):  # every call, both ranks: the same bits
-            np.testing.assert_array_equal(r0[key + f"_{i}"], got)
-            np.testing.assert_array_equal(r1[key + f"_{i}"], got)
+        got = ranks[0][key + "_0"]
+        for r in ranks:  # every call, every rank: the same bits
+            for i in range(3):
+                np.testing.assert_array_equal(r[key + f"_{i}"], got)
         assert_close(got, port.linear(x, w, wtype, n_out, bias), port.linear_bound(x, w, wtype, n_out),
                      1e-7 * np.abs(bias)[None, :] + 1e-6)
