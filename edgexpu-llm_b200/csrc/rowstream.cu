@@ -37,9 +37,12 @@ namespace {
 constexpr int CONSUMER_WARPS = 15;  // + 1 producer warp = 16 warps, 4 per SM sub-partition (128 registers each)
 constexpr int CONSUMERS = CONSUMER_WARPS * 32;
 constexpr int THREADS = CONSUMERS + 32;
-constexpr int STAGE_TARGET = 32768;
+#ifndef EX_RS_STAGE
+#define EX_RS_STAGE 32768
+#endif
+constexpr int STAGE_TARGET = EX_RS_STAGE;
 constexpr int MAX_STAGES = 8;
-constexpr int BAR_BYTES = 256;        // full[8], empty[8], abort flag
+constexpr int BAR_BYTES = 512;        // full[8], empty[8], abort flag, tile descriptors[8] at 256
 constexpr int ACT_BUDGET = 96 * 1024;
 constexpr int STAGE_SLACK = 48;       // alignment round-down (<16) + over-read of the last block
 constexpr int MAX_M = 8;              // activation rows (tokens) per launch; the host splits more
@@ -229,14 +232,14 @@ __device__ __forceinline__ float warp_sum(float v) {
 // single token is streamed and a row fits in one warp pass (U <= 32: Q8_0 K <= 1024, Q4_K K <= 4096):
 // the lane then owns the same unit in every row, so its activation chunks never change.
 struct XRegs {
-  int4 q[8];  // Q8_K: the unit's 8 chunks; Q8_0: q[0..1]
-  int4 b;     // Q8_K: bsums of the unit's 4 sub-blocks
-  float d;    // activation scale of the unit's block
+  int4 q[8];        // Q8_K: the unit's 8 chunks; Q8_0: q[0..1]
+  uint32_t sl, sh;  // Q8_K: 32-element sums S_j of the unit's 4 sub-blocks as 7-bit digits, S = 128*sh + sl
+  float d;          // activation scale of the unit's block
 };
 
 __device__ __forceinline__ void load_xregs(Fmt f, const RowStreamArgs& a, const uint8_t* act, int lane, XRegs& xr) {
   const int U = units_per_row(f, a.K);
-  xr.b = make_int4(0, 0, 0, 0);
+  xr.sl = xr.sh = 0u;
   xr.d = 0.0f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) xr.q[j] = make_int4(0, 0, 0, 0);
@@ -249,7 +252,9 @@ __device__ __forceinline__ void load_xregs(Fmt f, const RowStreamArgs& a, const 
   } else {
 #pragma unroll
     for (int j = 0; j < 8; ++j) xr.q[j] = xq[j * U + lane];
-    xr.b = reinterpret_cast<const int4*>(act + U * 128)[lane];
+    const int4 b = reinterpret_cast<const int4*>(act + U * 128)[lane];  // |S_j| <= 32 * 127
+    xr.sl = pack4_i8(b.x & 127, b.y & 127, b.z & 127, b.w & 127);
+    xr.sh = pack4_i8(b.x >> 7, b.y >> 7, b.z >> 7, b.w >> 7);
     xr.d = reinterpret_cast<const float*>(act + U * 128 + U * 16)[lane >> 1];
   }
 }
@@ -316,22 +321,28 @@ __device__ __forceinline__ void q4k_load_half(const uint8_t* rowp, int sb, int h
 // combined in int32 before the float step, so every per-block (sumi, summ) equals the
 // reference's int32 values.  High nibbles are used in place (byte & 0xF0 = 16*q) with an
 // unsigned-by-signed dp4a and the exact sum is shifted down by 4 afterwards.
-template <RowOut MODE, int MTOK, bool XREG>
+template <RowOut MODE, int MTOK, bool XREG, bool FULL = false>
 __device__ __forceinline__ void row_q4k_q8k(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
                                             long long row, float (&acc)[MTOK], int lane, const XRegs& xr) {
+  static_assert(!FULL || XREG, "FULL: one unit per lane, activations in registers");
   const int U = a.K / 128, nb = U / 2;
   const int4* xq = reinterpret_cast<const int4*>(act);
   const int4* xb = reinterpret_cast<const int4*>(act + a.m * U * 128);
   const float* xd = reinterpret_cast<const float*>(act + a.m * U * 128 + a.m * U * 16);
   for (int u0 = 0; u0 < U; u0 += 32) {
     const int u = u0 + lane;
-    const bool live = u < U;
+    const bool live = FULL || u < U;
     const int sb = u >> 1, h = u & 1;
-    uint4 hdr = make_uint4(0, 0, 0, 0);
+    uint4 hdr;
     uint32_t qw[16];
+    if (FULL) {
+      q4k_load_half(rowp, sb, h, hdr, qw);
+    } else {
+      hdr = make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) qw[i] = 0;
-    if (live) q4k_load_half(rowp, sb, h, hdr, qw);
+      for (int i = 0; i < 16; ++i) qw[i] = 0;
+      if (live) q4k_load_half(rowp, sb, h, hdr, qw);
+    }
     uint32_t sc4, mn4;
     q4k_scales_half(hdr.y, hdr.z, hdr.w, h, sc4, mn4);
     const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
@@ -360,11 +371,15 @@ __device__ __forceinline__ void row_q4k_q8k(const RowStreamArgs& a, const uint8_
           }
           ip[1] >>= 4;  // exact: the sums of 16*q*x are multiples of 16
           ip[3] >>= 4;
-          const int4 bs = XREG ? xr.b : xb[t * U + u];
           sumi = static_cast<int>(sc4 & 0xFFu) * ip[0] + static_cast<int>((sc4 >> 8) & 0xFFu) * ip[1] +
                  static_cast<int>((sc4 >> 16) & 0xFFu) * ip[2] + static_cast<int>(sc4 >> 24) * ip[3];
-          summ = static_cast<int>(mn4 & 0xFFu) * bs.x + static_cast<int>((mn4 >> 8) & 0xFFu) * bs.y +
-                 static_cast<int>((mn4 >> 16) & 0xFFu) * bs.z + static_cast<int>(mn4 >> 24) * bs.w;
+          if constexpr (XREG) {  // sum_j m_j * (128*Sh_j + Sl_j), exact (m_j <= 63, Sl_j <= 127)
+            summ = dp4a_us(mn4, xr.sl, dp4a_us(mn4, xr.sh, 0) * 128);
+          } else {
+            const int4 bs = xb[t * U + u];
+            summ = static_cast<int>(mn4 & 0xFFu) * bs.x + static_cast<int>((mn4 >> 8) & 0xFFu) * bs.y +
+                   static_cast<int>((mn4 >> 16) & 0xFFu) * bs.z + static_cast<int>(mn4 >> 24) * bs.w;
+          }
         }
         sumi += __shfl_xor_sync(0xFFFFFFFFu, sumi, 1);
         summ += __shfl_xor_sync(0xFFFFFFFFu, summ, 1);
@@ -445,6 +460,18 @@ struct TileRef {
   long long r0;
   int nr;
 };
+
+// What consumers need of a stage's tile, written by the producer before it arms the stage's
+// barrier (the barrier's release/acquire orders it), so consumer warps need not re-derive it.
+struct __align__(16) TileDesc {
+  float* out;
+  const float* bias;
+  int r0;        // first row of the tile within its tensor
+  int nr;        // rows in the tile
+  int stride;    // output row stride (elements)
+  int misalign;  // start of the tile's first row inside the stage (the copy starts 16-byte aligned)
+};
+static_assert(sizeof(TileDesc) == 32, "two 16-byte words");
 
 __device__ __forceinline__ TileRef tile_ref(const RowStreamArgs& a, const Layout& L, long long tile) {
   int s = 0;
@@ -555,6 +582,8 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAX_STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 2 * MAX_STAGES * 8);
+  TileDesc* descs = reinterpret_cast<TileDesc*>(smem + 256);
+  static_assert(256 + MAX_STAGES * sizeof(TileDesc) <= BAR_BYTES, "tile descriptors fit the header");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = L.n_stages;
 
@@ -593,6 +622,13 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
       const uintptr_t start = reinterpret_cast<uintptr_t>(tr.w) + static_cast<uintptr_t>(tr.r0) * a.row_bytes;
       const uintptr_t al = start & ~static_cast<uintptr_t>(15);
       const uint32_t bytes = static_cast<uint32_t>((start - al + static_cast<long long>(tr.nr) * a.row_bytes + 15) & ~15ull);
+      TileDesc& td = descs[s];
+      td.out = tr.out;
+      td.bias = tr.bias;
+      td.r0 = static_cast<int>(tr.r0);
+      td.nr = tr.nr;
+      td.stride = static_cast<int>(tr.stride);
+      td.misalign = static_cast<int>(start - al);
       mbar_arrive_expect_tx(&full[s], bytes);
       bulk_g2s(smem + L.stage_off + s * L.stage_bytes, reinterpret_cast<const void*>(al), bytes, &full[s], pol);
       if (++s == S) {
@@ -620,6 +656,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
 
   XRegs xr;
   if constexpr (XREG) load_xregs(F, a, act, lane, xr);
+  const bool full_warp = units_per_row(F, a.K) == 32;  // every lane has a unit (XREG rows)
 
   unsigned long long best = 0ull;
   bool dead = false;
@@ -635,10 +672,9 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
         dead = true;
       }
       if (!dead) {
-        const TileRef tr = tile_ref(a, L, tile);
+        const TileDesc tr = descs[s];
         const long long r0 = tr.r0;
-        const uintptr_t start = reinterpret_cast<uintptr_t>(tr.w) + static_cast<uintptr_t>(r0) * a.row_bytes;
-        const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + (start & 15u);
+        const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + tr.misalign;
         for (int r = first; r < tr.nr; r += CONSUMER_WARPS) {
           float acc[MTOK];
 #pragma unroll
@@ -647,7 +683,11 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
           if constexpr (F == Fmt::Q8_0xQ8_0) {
             row_q8_0<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
           } else if constexpr (F == Fmt::Q4_KxQ8_K) {
-            row_q4k_q8k<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
+            if (XREG && full_warp) {
+              row_q4k_q8k<MODE, MTOK, XREG, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
+            } else {
+              row_q4k_q8k<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
+            }
           } else {
             row_q4k_f32<MODE, MTOK>(a, act, rowp, acc, lane);
           }
@@ -672,7 +712,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
                   *reinterpret_cast<unsigned long long*>(a.tp.peer[a.tp.rank] + off) = v;
                 }
               } else if constexpr (MODE == RowOut::Store) {
-                tr.out[static_cast<size_t>(lane) * tr.stride + row] = y;
+                tr.out[static_cast<size_t>(lane) * tr.stride + row] = y;  // stride: int, outputs < 2^31
               } else {
                 const unsigned long long k = argmax_key(y, static_cast<uint32_t>(a.row0 + row));
                 best = k > best ? k : best;
