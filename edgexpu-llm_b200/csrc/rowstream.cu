@@ -321,6 +321,63 @@ __device__ __forceinline__ void q4k_load_half(const uint8_t* rowp, int sb, int h
 // combined in int32 before the float step, so every per-block (sumi, summ) equals the
 // reference's int32 values.  High nibbles are used in place (byte & 0xF0 = 16*q) with an
 // unsigned-by-signed dp4a and the exact sum is shifted down by 4 afterwards.
+// Per-lane constants of the one-unit-per-lane Q4_K row (U == 32, activations in registers):
+// where the lane's half super-block sits in a row, and masks that select the 6-bit scale/min
+// layout of its half (get_scale_min_k4, gguf_quant.c:212-220) without a branch.
+struct Q4kLane {
+  int hdr_off, q_off;         // byte offsets of the super-block header and of the half's 64 quant bytes
+  uint32_t m_lo, m_s2, m_hi;  // h = 0: (0x3F.., 0, 0); h = 1: (0, 0x0F.., 0x30..)
+};
+
+__device__ __forceinline__ Q4kLane q4k_lane(int lane) {
+  const int sb = lane >> 1, h = lane & 1;
+  Q4kLane c;
+  c.hdr_off = sb * Q4_K_BYTES;
+  c.q_off = sb * Q4_K_BYTES + 16 + 64 * h;
+  c.m_lo = h ? 0u : 0x3F3F3F3Fu;
+  c.m_s2 = h ? 0x0F0F0F0Fu : 0u;
+  c.m_hi = h ? 0x30303030u : 0u;
+  return c;
+}
+
+// One Q4_K row of K = 4096 (32 half super-blocks) against one token whose Q8_K activations are
+// held in registers.  Each lane adds its own half super-block to acc:
+//   acc += (d_x d_w) * sumi_half - (d_x dmin_w) * summ_half
+// with sumi_half (|.| <= 945*127*128 < 2^24) and summ_half exact in int32 and in fp32; the
+// reference adds the two halves in int32 first (gguf_dot_q8.c:711-759), which differs only in
+// the fp32 rounding of the final sum.
+__device__ __forceinline__ void row_q4k_full(const uint8_t* rowp, float& acc, const XRegs& xr, const Q4kLane& c) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(rowp + c.hdr_off);
+  const uint4* qp = reinterpret_cast<const uint4*>(rowp + c.q_off);
+  const uint4 w0 = qp[0], w1 = qp[1], w2 = qp[2], w3 = qp[3];
+  const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
+  const uint32_t sc4 = (s0 & c.m_lo) | (s2 & c.m_s2) | ((s0 >> 2) & c.m_hi);
+  const uint32_t mn4 = (s1 & c.m_lo) | ((s2 >> 4) & c.m_s2) | ((s1 >> 2) & c.m_hi);
+  // Sub-block 2g: low nibbles of group g's 32 bytes against chunks 4g, 4g+1; sub-block 2g+1: high
+  // nibbles (16*q in place, unsigned x signed dp4a) against chunks 4g+2, 4g+3.
+  const uint32_t g0[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  const uint32_t g1[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
+  const int xw[8][4] = {{xr.q[0].x, xr.q[0].y, xr.q[0].z, xr.q[0].w}, {xr.q[1].x, xr.q[1].y, xr.q[1].z, xr.q[1].w},
+                        {xr.q[2].x, xr.q[2].y, xr.q[2].z, xr.q[2].w}, {xr.q[3].x, xr.q[3].y, xr.q[3].z, xr.q[3].w},
+                        {xr.q[4].x, xr.q[4].y, xr.q[4].z, xr.q[4].w}, {xr.q[5].x, xr.q[5].y, xr.q[5].z, xr.q[5].w},
+                        {xr.q[6].x, xr.q[6].y, xr.q[6].z, xr.q[6].w}, {xr.q[7].x, xr.q[7].y, xr.q[7].z, xr.q[7].w}};
+  int ip0 = 0, ip1 = 0, ip2 = 0, ip3 = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int c4 = k >> 2, wi = k & 3;
+    ip0 = dp4a(static_cast<int>(g0[k] & 0x0F0F0F0Fu), xw[c4][wi], ip0);
+    ip1 = dp4a_us(g0[k] & 0xF0F0F0F0u, xw[2 + c4][wi], ip1);
+    ip2 = dp4a(static_cast<int>(g1[k] & 0x0F0F0F0Fu), xw[4 + c4][wi], ip2);
+    ip3 = dp4a_us(g1[k] & 0xF0F0F0F0u, xw[6 + c4][wi], ip3);
+  }
+  // ip1, ip3 are 16x their sub-block sums; their scaled sum stays exact below 2^31 before the shift.
+  const int sumi = static_cast<int>(sc4 & 0xFFu) * ip0 + static_cast<int>((sc4 >> 16) & 0xFFu) * ip2 +
+                   ((static_cast<int>((sc4 >> 8) & 0xFFu) * ip1 + static_cast<int>(sc4 >> 24) * ip3) >> 4);
+  const int summ = dp4a_us(mn4, xr.sl, dp4a_us(mn4, xr.sh, 0) * 128);
+  const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
+  acc += (xr.d * dw) * static_cast<float>(sumi) - (xr.d * dmw) * static_cast<float>(summ);
+}
+
 template <RowOut MODE, int MTOK, bool XREG, bool FULL = false>
 __device__ __forceinline__ void row_q4k_q8k(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
                                             long long row, float (&acc)[MTOK], int lane, const XRegs& xr) {
@@ -657,6 +714,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   XRegs xr;
   if constexpr (XREG) load_xregs(F, a, act, lane, xr);
   const bool full_warp = units_per_row(F, a.K) == 32;  // every lane has a unit (XREG rows)
+  const Q4kLane q4l = q4k_lane(lane);
 
   unsigned long long best = 0ull;
   bool dead = false;
@@ -683,7 +741,13 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
           if constexpr (F == Fmt::Q8_0xQ8_0) {
             row_q8_0<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
           } else if constexpr (F == Fmt::Q4_KxQ8_K) {
-            if (XREG && full_warp) {
+            if constexpr (XREG && MTOK == 1 && MODE != RowOut::Partials) {
+              if (full_warp) {
+                row_q4k_full(rowp, acc[0], xr, q4l);
+              } else {
+                row_q4k_q8k<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
+              }
+            } else if (XREG && full_warp) {
               row_q4k_q8k<MODE, MTOK, XREG, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
             } else {
               row_q4k_q8k<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
