@@ -48,6 +48,11 @@ constexpr int STAGE_SLACK = 48;       // alignment round-down (<16) + over-read 
 constexpr int MAX_M = 8;              // activation rows (tokens) per launch; the host splits more
 constexpr int PROLOGUE_QUANT_MAX_M = 2;
 constexpr int PRO_BATCH = 4;          // activation blocks a consumer warp loads before quantizing them
+#ifndef EX_RS_PRE
+#define EX_RS_PRE 2
+#endif
+constexpr int PRE_STAGES = EX_RS_PRE;  // weight copies the producer issues before the activations land
+constexpr unsigned long long HOLD_LIMIT_NS = 20000;  // the hold is a scheduling aid: give up after 20 us
 
 struct Layout {
   int tile_rows;
@@ -84,9 +89,23 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Wait (at most HOLD_LIMIT_NS; nothing depends on it for correctness) until every consumer warp
+// reported its activation loads landed.
+__device__ __forceinline__ void hold_for_activations(uint64_t* xin) {
+  if (mbar_try_wait(xin, 0)) return;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait_sleep(xin, 0, 1000u))
+    if (global_ns() - t0 > HOLD_LIMIT_NS) return;
+}
+
 // ---- activation prologue ---------------------------------------------------------------------------
 
-__device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct) {
+// Lane 0 of every consumer warp arrives once on `xin` when the warp's first activation loads
+// have landed (or, on paths without a separate load phase, when it is done): the producer holds
+// back all but its first PRE_STAGES weight copies until then, so the activations -- on the
+// critical path of every launch -- do not queue behind a full ring of weights into the SM.
+__device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct, uint64_t* xin) {
+  bool arrived = false;
   const int K = a.K, m = a.m, lane = ct & 31, cw = ct >> 5;
   const int U = units_per_row(a.fmt, K);
   if (a.fmt == Fmt::Q8_0xQ8_0) {
@@ -156,6 +175,13 @@ __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct) {
             ld[k][1] = src[1];
           }
         }
+        if (!arrived) {  // the vote issues once every lane's first load has landed; the arrive after it
+          const int seen = __any_sync(0xFFFFFFFFu, ld[0][0].x != ld[0][0].x);
+          uint64_t* bar = xin;
+          asm volatile("" : "+l"(bar) : "r"(seen));  // keeps the arrive after the vote
+          if (lane == 0) mbar_arrive(bar);
+          arrived = true;
+        }
 #pragma unroll
         for (int k = 0; k < PRO_BATCH; ++k) {
           const int blk = base + k * CONSUMER_WARPS;
@@ -217,6 +243,10 @@ __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct) {
       const int t = i / (U * 4), rem = i - t * U * 4;
       xs[(t * U + (rem >> 2)) * 4 + (rem & 3)] = s;
     }
+  }
+  if (!arrived) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(xin);
   }
 }
 
@@ -639,6 +669,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAX_STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 2 * MAX_STAGES * 8);
+  uint64_t* xin = reinterpret_cast<uint64_t*>(smem + 2 * MAX_STAGES * 8 + 8);
   TileDesc* descs = reinterpret_cast<TileDesc*>(smem + 256);
   static_assert(256 + MAX_STAGES * sizeof(TileDesc) <= BAR_BYTES, "tile descriptors fit the header");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -652,6 +683,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], R < CONSUMER_WARPS ? R : CONSUMER_WARPS);
     }
+    mbar_init(xin, CONSUMER_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -668,6 +700,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
     int s = 0;
     uint32_t ephase = 1;  // iteration it >= S waits for completion (it/S - 1) of empty[s]: parity (it/S - 1) & 1
     for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x, ++it) {
+      if (it == PRE_STAGES) hold_for_activations(xin);
       if (it >= S) {
         if (!wait_or_abort(&empty[s], ephase, abort_flag)) {
           atomicOr(a.status, ST_TIMEOUT_EMPTY);
@@ -708,7 +741,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   const uint32_t tp_e = TP ? *reinterpret_cast<volatile const uint32_t*>(a.tp.peer[a.tp.rank] + TP_CTRL_OFF + 4) : 0u;
   const size_t tp_slot =
       TP ? (static_cast<size_t>(tp_e & 1u) * TP_MAX_WORLD + a.tp.rank) * TP_SLOT_BYTES : 0;  // [parity][rank]
-  load_act(a, act, threadIdx.x - 32);
+  load_act(a, act, threadIdx.x - 32, xin);
   named_bar_sync(1, CONSUMERS);
 
   XRegs xr;
