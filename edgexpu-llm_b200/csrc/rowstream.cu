@@ -675,13 +675,14 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = L.n_stages;
 
-  // Tile slot r belongs to consumer warp (it*R + r) % CONSUMER_WARPS, so min(R, CONSUMER_WARPS)
-  // warps release each stage.
+  // Tile slot r belongs to consumer warp (it*R + r) % CONSUMER_WARPS.  Every consumer warp waits
+  // for every tile and releases it, owner or not: a warp that skipped tiles could otherwise reach
+  // a stage's fill k before fill k - 1 completed, when the parity wait for k returns at once.
   const int R = L.tile_rows;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], R < CONSUMER_WARPS ? R : CONSUMER_WARPS);
+      mbar_init(&empty[s], CONSUMER_WARPS);
     }
     mbar_init(xin, CONSUMER_WARPS);
     *abort_flag = 0;
@@ -756,13 +757,13 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   const int step = R % CONSUMER_WARPS;
   int first = cw;  // first slot of this warp in the current tile: (cw - it*R) mod CONSUMER_WARPS
   for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
-    if (first < R) {  // this warp owns at least one slot of the tile
+    {
       if (!dead && !wait_or_abort(&full[s], fphase, abort_flag)) {
         atomicOr(a.status, ST_TIMEOUT_FULL);
         *abort_flag = 1;
         dead = true;
       }
-      if (!dead) {
+      if (!dead && first < R) {  // this warp owns at least one slot of the tile
         const TileDesc tr = descs[s];
         const long long r0 = tr.r0;
         const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + tr.misalign;

@@ -137,6 +137,9 @@ LINEAR_CASES = [
     (TYPE_Q4_K, 1, 256, 1, False),
     (TYPE_Q4_K, 13, 768, 40, True),
     (TYPE_Q4_K, 999, 2048, 2, False),
+    # rows longer than a 32 KB stage -> one-row tiles: each warp owns every 15th tile and skips the
+    # rest, so it can reach a stage's next fill before the previous one landed (~28 tiles per CTA)
+    (TYPE_Q8_0, 4096, 16384, 1, False),
 ]
 
 
