@@ -91,7 +91,8 @@ def act_bytes(t, n):
 
 
 def linear_alg_bytes(t, n_out, n_in, m):
-    """W + b * (4K in + quantized activation + 4N out)."""
+    """Algorithmic bytes of one linear: the weight once, plus per activation row its fp32 input
+    (4K), its quantized form and its fp32 output (4N)."""
     return n_out * row_bytes(t, n_in) + m * (4 * n_in + act_bytes(t, n_in) + 4 * n_out)
 
 
