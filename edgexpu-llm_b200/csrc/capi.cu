@@ -271,7 +271,11 @@ int check_status(char* error, size_t error_size) {
     const uint32_t s = *g.h_status;
     *g.h_status = 0;
     cudaMemset(g.d_status, 0, sizeof(uint32_t));
-    return fail(error, error_size, "device wait timed out (status 0x%x): a tile copy never completed", s);
+    return fail(error, error_size, "device wait timed out (status 0x%x):%s%s%s%s", s,
+                (s & ex::ST_TIMEOUT_FULL) ? " a consumer gave up waiting for a tile copy;" : "",
+                (s & ex::ST_TIMEOUT_EMPTY) ? " the producer gave up waiting for a free stage;" : "",
+                (s & ex::ST_TIMEOUT_DRAIN) ? " copies were still in flight at exit;" : "",
+                (s & ex::ST_TIMEOUT_PEER) ? " a tensor-parallel peer did not deliver its partial in time;" : "");
   }
   return 1;
 }
