@@ -5,6 +5,11 @@
   (scale, min) pairs are ~ U{0..63}; 128 bytes of nibbles ~ U{0..15}.  The 6-bit fields of the
   packing (get_scale_min_k4, gguf_quant.c:212-220) are a bijection of the 96 scale bits, so
   uniform random scale bytes give uniform independent (scale, min) pairs.
+* Q4_0 (18 B) / Q5_0 (22 B): fp16 d ~ U(1e-4, 2e-3) as for Q8_0; high bits and nibbles uniform.
+* Q5_K (176 B): the Q4_K recipe, plus 32 bytes of uniform high bits.
+* Q6_K (210 B): 128 + 64 bytes of uniform low/high quant bits, int8 scales ~ U{-128..127}, fp16
+  d ~ U(1e-4, 1e-3).
+  (The benchmark configurations name only Q8_0 and Q4_K; these recipes follow their value ranges.)
 * Activations: fp32 ~ N(0, 1).
 
 The numpy versions are used for parity tests; the torch versions generate the multi-GB
@@ -16,6 +21,9 @@ from __future__ import annotations
 import numpy as np
 
 Q8_0_BYTES, Q4_K_BYTES = 34, 144
+TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 2, 6, 8, 12, 13, 14
+BLOCK = {TYPE_Q4_0: (32, 18), TYPE_Q5_0: (32, 22), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144),
+         TYPE_Q5_K: (256, 176), TYPE_Q6_K: (256, 210)}
 
 
 def _fp16_bits(v: np.ndarray) -> np.ndarray:
@@ -38,8 +46,45 @@ def q4_k_weight(rng: np.random.Generator, n_out: int, n_in: int) -> np.ndarray:
     return blk.reshape(n_out, nb * Q4_K_BYTES)
 
 
+def _blocks(rng: np.random.Generator, wtype: int, n_out: int, n_in: int) -> np.ndarray:
+    qk, bb = BLOCK[wtype]
+    return rng.integers(0, 256, (n_out, n_in // qk, bb), dtype=np.uint8)
+
+
+def q4_0_weight(rng: np.random.Generator, n_out: int, n_in: int) -> np.ndarray:
+    blk = _blocks(rng, TYPE_Q4_0, n_out, n_in)
+    blk[..., 0:2] = _fp16_bits(rng.uniform(1e-4, 2e-3, blk.shape[:2]))
+    return blk.reshape(n_out, -1)
+
+
+def q5_0_weight(rng: np.random.Generator, n_out: int, n_in: int) -> np.ndarray:
+    blk = _blocks(rng, TYPE_Q5_0, n_out, n_in)
+    blk[..., 0:2] = _fp16_bits(rng.uniform(1e-4, 2e-3, blk.shape[:2]))
+    return blk.reshape(n_out, -1)
+
+
+def q5_k_weight(rng: np.random.Generator, n_out: int, n_in: int) -> np.ndarray:
+    blk = _blocks(rng, TYPE_Q5_K, n_out, n_in)
+    blk[..., 0:2] = _fp16_bits(rng.uniform(1e-4, 1e-3, blk.shape[:2]))
+    blk[..., 2:4] = _fp16_bits(rng.uniform(1e-4, 1e-3, blk.shape[:2]))
+    return blk.reshape(n_out, -1)
+
+
+def q6_k_weight(rng: np.random.Generator, n_out: int, n_in: int) -> np.ndarray:
+    blk = _blocks(rng, TYPE_Q6_K, n_out, n_in)
+    blk[..., 208:210] = _fp16_bits(rng.uniform(1e-4, 1e-3, blk.shape[:2]))
+    return blk.reshape(n_out, -1)
+
+
+_MAKERS = {TYPE_Q4_0: q4_0_weight, TYPE_Q5_0: q5_0_weight, TYPE_Q5_K: q5_k_weight, TYPE_Q6_K: q6_k_weight}
+
+
 def weight(rng: np.random.Generator, wtype: int, n_out: int, n_in: int) -> np.ndarray:
-    return q8_0_weight(rng, n_out, n_in) if wtype == 8 else q4_k_weight(rng, n_out, n_in)
+    if wtype == TYPE_Q8_0:
+        return q8_0_weight(rng, n_out, n_in)
+    if wtype == TYPE_Q4_K:
+        return q4_k_weight(rng, n_out, n_in)
+    return _MAKERS[wtype](rng, n_out, n_in)
 
 
 def activations(rng: np.random.Generator, m: int, n: int) -> np.ndarray:

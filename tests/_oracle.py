@@ -22,7 +22,16 @@ REF_AVX2 = ORACLE_DIR / "_ref" / "libedgexpu_ref_avx2.so"
 REF_SCALAR = ORACLE_DIR / "_ref" / "libedgexpu_ref_scalar.so"
 REF_SRC = pathlib.Path("/root/reference/src")
 
-TYPE_Q8_0, TYPE_Q4_K = 8, 12
+TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 2, 6, 8, 12, 13, 14
+ALL_TYPES = (TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K)
+B32_TYPES = (TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0)  # Q8_0 activations (can_dot_q8)
+BLOCK = {TYPE_Q4_0: (32, 18), TYPE_Q5_0: (32, 22), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144),
+         TYPE_Q5_K: (256, 176), TYPE_Q6_K: (256, 210)}
+
+
+def act_is_q8_0(wtype: int) -> bool:
+    return wtype in B32_TYPES
+
 
 _vp, _int, _u32, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_size_t
 
@@ -69,6 +78,10 @@ class Port:
             "eo_quantize_q8_k": (_int, [_vp, _int, _vp]),
             "eo_partials_q8_0": (_int, [_vp, _vp, _int, _vp]),
             "eo_partials_q4_k": (_int, [_vp, _vp, _int, _vp, _vp]),
+            "eo_partials_b32": (_int, [_u32, _vp, _vp, _int, _vp]),
+            "eo_partials_k": (_int, [_u32, _vp, _vp, _int, _vp, _vp]),
+            "eo_dot_q8": (ctypes.c_float, [_u32, _vp, _vp, _int]),
+            "eo_dot_f32": (ctypes.c_float, [_u32, _vp, _vp, _int]),
             "eo_dot_q8_0_q8_0": (ctypes.c_float, [_vp, _vp, _int]),
             "eo_dot_q4_k_q8_k": (ctypes.c_float, [_vp, _vp, _int]),
             "eo_dot_q4_k_f32": (ctypes.c_float, [_vp, _vp, _int]),
@@ -92,7 +105,7 @@ class Port:
             x = x[None]
         rows = []
         for r in x:
-            if wtype == TYPE_Q8_0:
+            if act_is_q8_0(wtype):
                 out = np.empty(r.size // 32 * 34, np.uint8)
                 fn = self.lib.eo_quantize_q8_0_scalar if scalar else self.lib.eo_quantize_q8_0
             else:
@@ -103,16 +116,17 @@ class Port:
         return np.stack(rows)
 
     def partials(self, w: np.ndarray, xq: np.ndarray, wtype: int, n_in: int) -> np.ndarray:
-        """[m][n_out][nb] (Q8_0) or [m][n_out][nb][2] (Q4_K) int32 per-block partials."""
+        """[m][n_out][nb] (32-element types) or [m][n_out][nb][2] (K-quants) int32 per-block partials."""
         w = np.ascontiguousarray(w, np.uint8)
         xq = np.ascontiguousarray(xq, np.uint8)
         n_out, m = w.shape[0], xq.shape[0]
-        if wtype == TYPE_Q8_0:
+        if act_is_q8_0(wtype):
             nb = n_in // 32
             out = np.empty((m, n_out, nb), np.int32)
             for t in range(m):
                 for o in range(n_out):
-                    assert self.lib.eo_partials_q8_0(w[o].ctypes.data, xq[t].ctypes.data, n_in, out[t, o].ctypes.data)
+                    assert self.lib.eo_partials_b32(wtype, w[o].ctypes.data, xq[t].ctypes.data, n_in,
+                                                    out[t, o].ctypes.data)
             return out
         nb = n_in // 256
         out = np.empty((m, n_out, nb, 2), np.int32)
@@ -120,7 +134,8 @@ class Port:
         sm = np.empty(nb, np.int32)
         for t in range(m):
             for o in range(n_out):
-                assert self.lib.eo_partials_q4_k(w[o].ctypes.data, xq[t].ctypes.data, n_in, si.ctypes.data, sm.ctypes.data)
+                assert self.lib.eo_partials_k(wtype, w[o].ctypes.data, xq[t].ctypes.data, n_in, si.ctypes.data,
+                                              sm.ctypes.data)
                 out[t, o, :, 0] = si
                 out[t, o, :, 1] = sm
         return out
@@ -161,10 +176,11 @@ class Port:
         return int(tok.value), float(sc.value), scores
 
     def logits_bound(self, w, wtype, hidden, rows):
-        """Per-row tolerance bound of the logits dot (quantized hidden for Q8_0, fp32 for Q4_K)."""
+        """Per-row tolerance bound of the logits dot (quantized hidden for the Q8_0-activation types,
+        fp32 for the K-quants)."""
         w = np.ascontiguousarray(w, np.uint8)
         h = np.ascontiguousarray(hidden, np.float32).ravel()
-        if wtype == TYPE_Q8_0:
+        if act_is_q8_0(wtype):
             hq = self.quantize(h, TYPE_Q8_0)[0]
             return np.array([self.lib.eo_abs_bound_q8(wtype, w[r].ctypes.data, hq.ctypes.data, h.size) for r in rows])
         return np.array([self.lib.eo_abs_bound_f32(wtype, w[r].ctypes.data, h.ctypes.data, h.size) for r in rows])
@@ -196,7 +212,7 @@ class Ref:
             x = x[None]
         rows = []
         for r in x:
-            if wtype == TYPE_Q8_0:
+            if act_is_q8_0(wtype):
                 out = np.empty(r.size // 32 * 34, np.uint8)
                 assert self.lib.edgexpu_gguf_quantize_q8_0(r.ctypes.data, r.size, out.ctypes.data) == 1
             else:
@@ -208,7 +224,7 @@ class Ref:
     def dot_q8(self, wtype, wrow, xq, n):
         wrow = np.ascontiguousarray(wrow, np.uint8)
         xq = np.ascontiguousarray(xq, np.uint8)
-        fn = self.lib.edgexpu_gguf_dot_quant_q8 if wtype == TYPE_Q8_0 else self.lib.edgexpu_gguf_dot_quant_q8k
+        fn = self.lib.edgexpu_gguf_dot_quant_q8 if act_is_q8_0(wtype) else self.lib.edgexpu_gguf_dot_quant_q8k
         return fn(wtype, wrow.ctypes.data, xq.ctypes.data, n)
 
     def dot_f32(self, wtype, wrow, x, n):
@@ -233,7 +249,7 @@ class Ref:
         w = np.ascontiguousarray(w, np.uint8)
         h = np.ascontiguousarray(hidden, np.float32).ravel()
         n = h.size
-        if wtype == TYPE_Q8_0:
+        if act_is_q8_0(wtype):
             hq = self.quantize(h, TYPE_Q8_0)[0]
             scores = np.array([self.dot_q8(wtype, w[i], hq, n) for i in range(vocab)], np.float32)
         else:

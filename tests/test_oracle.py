@@ -15,7 +15,7 @@ and the restatement is then pinned bit-for-bit against the reference on seeded i
 import numpy as np
 import pytest
 
-from _oracle import TYPE_Q4_K, TYPE_Q8_0, load_pkg
+from _oracle import BLOCK, TYPE_Q4_0, TYPE_Q4_K, TYPE_Q5_0, TYPE_Q5_K, TYPE_Q6_K, TYPE_Q8_0, load_pkg
 
 synth = None
 
@@ -305,3 +305,149 @@ def test_logits_tie_prefers_lowest_id(port):
     bias[7] = np.nan
     tok, sc, _ = port.logits(w2, TYPE_Q8_0, h, 51, bias)
     assert tok == 0 and sc == -np.inf  # nothing beats -inf: the reference keeps id 0
+
+
+# ---- the other GGUF weight types behind the same dispatch (Q4_0, Q5_0, Q5_K, Q6_K) --------------
+
+OTHER_TYPES = (TYPE_Q4_0, TYPE_Q5_0, TYPE_Q5_K, TYPE_Q6_K)
+
+
+@pytest.mark.parametrize("wtype", OTHER_TYPES)
+@pytest.mark.parametrize("n", [256, 1536])
+def test_other_types_dot_q8_matches_reference(port, ref, ref_scalar, wtype, n):
+    """edgexpu_gguf_dot_quant_q8 / _q8k: bit-exact against the scalar build, bounded against AVX2."""
+    s = _synth()
+    rng = np.random.default_rng(wtype * 100 + n)
+    w = s.weight(rng, wtype, 12, n)
+    x = s.activations(rng, 2, n)
+    xq = port.quantize(x, wtype)
+    for t in range(2):
+        for o in range(12):
+            got = np.float32(port.lib.eo_dot_q8(wtype, w[o].ctypes.data, xq[t].ctypes.data, n))
+            exact = np.float32(ref_scalar.dot_q8(wtype, w[o], xq[t], n))
+            assert got.view(np.uint32) == exact.view(np.uint32), (t, o)
+            bound = port.lib.eo_abs_bound_q8(wtype, w[o].ctypes.data, xq[t].ctypes.data, n)
+            assert abs(float(got) - ref.dot_q8(wtype, w[o], xq[t], n)) <= 1e-5 * bound
+
+
+@pytest.mark.parametrize("wtype", OTHER_TYPES + (TYPE_Q8_0,))
+@pytest.mark.parametrize("n", [256, 1024])
+def test_other_types_dot_f32_matches_reference(port, ref, ref_scalar, wtype, n):
+    """edgexpu_gguf_dot_quant (fp32 activations, the logits path of the K-quants)."""
+    s = _synth()
+    rng = np.random.default_rng(wtype * 10 + n)
+    w = s.weight(rng, wtype, 10, n)
+    x = s.activations(rng, 1, n)[0]
+    for o in range(10):
+        got = np.float32(port.lib.eo_dot_f32(wtype, w[o].ctypes.data, x.ctypes.data, n))
+        exact = np.float32(ref_scalar.dot_f32(wtype, w[o], x, n))
+        assert got.view(np.uint32) == exact.view(np.uint32), o
+        bound = port.lib.eo_abs_bound_f32(wtype, w[o].ctypes.data, x.ctypes.data, n)
+        assert abs(float(got) - ref.dot_f32(wtype, w[o], x, n)) <= 1e-5 * bound
+
+
+@pytest.mark.parametrize("wtype", OTHER_TYPES + (TYPE_Q8_0, TYPE_Q4_K))
+def test_dequantize_row_matches_reference(port, ref, wtype):
+    """edgexpu_gguf_dequantize (gguf_quant.c:355-411) row by row: bit-exact floats."""
+    import ctypes
+
+    s = _synth()
+    rng = np.random.default_rng(wtype)
+    n = 512
+    w = s.weight(rng, wtype, 4, n)
+    fn = ref.lib.edgexpu_gguf_dequantize
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
+    for o in range(4):
+        got = np.empty(n, np.float32)
+        want = np.empty(n, np.float32)
+        assert port.lib.eo_dequantize_row(wtype, w[o].ctypes.data, n, got.ctypes.data)
+        assert fn(w[o].ctypes.data, wtype, n, want.ctypes.data, None, 0) == 1
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("wtype", (TYPE_Q4_0, TYPE_Q5_0))
+def test_partials_b32_pinned_by_reference(port, ref, wtype):
+    """With d_w = d_x = 1.0 the reference's one-block dot returns exactly (float)ip."""
+    s = _synth()
+    rng = np.random.default_rng(wtype + 40)
+    bb = BLOCK[wtype][1]
+    w = s.weight(rng, wtype, 6, 256)
+    xq = port.quantize(s.activations(rng, 2, 256), wtype)
+    parts = port.partials(w, xq, wtype, 256)
+    one = np.array([0x3C00], np.uint16).view(np.uint8)
+    for t in range(2):
+        for o in range(6):
+            for b in range(8):
+                wb = w[o, bb * b:bb * b + bb].copy()
+                xb = xq[t, 34 * b:34 * b + 34].copy()
+                wb[0:2] = one
+                xb[0:2] = one
+                assert ref.dot_q8(wtype, wb, xb, 32) == float(parts[t, o, b])
+
+
+def test_partials_q5_k_pinned_by_reference(port, ref_scalar):
+    """As for Q4_K: d = 1, dmin = 0 gives sumi; d = 0, dmin = 1 gives -summ."""
+    s = _synth()
+    rng = np.random.default_rng(51)
+    w = s.weight(rng, TYPE_Q5_K, 5, 512)
+    xq = port.quantize(s.activations(rng, 2, 512), TYPE_Q5_K)
+    parts = port.partials(w, xq, TYPE_Q5_K, 512)
+    one16 = np.array([0x3C00], np.uint16).view(np.uint8)
+    zero16 = np.zeros(2, np.uint8)
+    one32 = np.array([1.0], np.float32).view(np.uint8)
+    for t in range(2):
+        for o in range(5):
+            for b in range(2):
+                wb = w[o, 176 * b:176 * b + 176].copy()
+                xb = xq[t, 292 * b:292 * b + 292].copy()
+                xb[0:4] = one32
+                wb[0:2], wb[2:4] = one16, zero16
+                assert ref_scalar.dot_q8(TYPE_Q5_K, wb, xb, 256) == float(parts[t, o, b, 0])
+                wb[0:2], wb[2:4] = zero16, one16
+                assert ref_scalar.dot_q8(TYPE_Q5_K, wb, xb, 256) == -float(parts[t, o, b, 1])
+
+
+def test_partials_q6_k_pinned_by_reference(port, ref):
+    """d = 1 and Q8_K d = 1 with small scales (|sumi| < 2^24, every float step exact): the AVX2
+    reference dot, which forms sumi in int32 (gguf_dot_q8.c:908-963), returns exactly (float)sumi."""
+    s = _synth()
+    rng = np.random.default_rng(61)
+    w = s.weight(rng, TYPE_Q6_K, 5, 512).reshape(5, 2, 210)
+    w[:, :, 192:208] = rng.integers(-4, 5, (5, 2, 16), dtype=np.int8).view(np.uint8)
+    w = w.reshape(5, 420)
+    xq = port.quantize(s.activations(rng, 2, 512), TYPE_Q6_K)
+    parts = port.partials(w, xq, TYPE_Q6_K, 512)
+    one16 = np.array([0x3C00], np.uint16).view(np.uint8)
+    one32 = np.array([1.0], np.float32).view(np.uint8)
+    assert np.all(parts[..., 1] == 0)
+    for t in range(2):
+        for o in range(5):
+            for b in range(2):
+                wb = w[o, 210 * b:210 * b + 210].copy()
+                xb = xq[t, 292 * b:292 * b + 292].copy()
+                xb[0:4] = one32
+                wb[208:210] = one16
+                assert abs(int(parts[t, o, b, 0])) < (1 << 24)
+                assert ref.dot_q8(TYPE_Q6_K, wb, xb, 256) == float(parts[t, o, b, 0])
+
+
+@pytest.mark.parametrize("wtype", OTHER_TYPES)
+def test_other_types_linear_and_logits_match_reference(port, ref, wtype):
+    s = _synth()
+    rng = np.random.default_rng(wtype + 7)
+    n_out, n_in, m = 40, 512, 3
+    w = s.weight(rng, wtype, n_out, n_in)
+    x = s.activations(rng, m, n_in)
+    bias = rng.standard_normal(n_out).astype(np.float32)
+    got = port.linear(x, w, wtype, n_out, bias)
+    want = ref.linear(x, w, wtype, n_out, bias)
+    bound = port.linear_bound(x, w, wtype, n_out)
+    assert np.all(np.abs(got.astype(np.float64) - want) <= 1e-5 * bound + 1e-6 * np.abs(bias))
+    tok, _, scores = port.logits(w, wtype, x[0], n_out)
+    rtok, _, rscores = ref.logits(w, wtype, x[0], n_out)
+    lb = port.logits_bound(w, wtype, x[0], range(n_out))
+    assert np.all(np.abs(scores.astype(np.float64) - rscores) <= 1e-5 * lb)
+    srt = np.sort(rscores)
+    if srt[-1] - srt[-2] > 2e-5 * lb.max():
+        assert tok == rtok
