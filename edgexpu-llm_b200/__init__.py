@@ -23,8 +23,10 @@ LIB_DIR = PKG_DIR / "lib"
 CUDA_LIB = LIB_DIR / "libedgexpu_cuda.so"
 HOST_LIB = LIB_DIR / "libedgexpu_b200_host.so"
 
+TYPE_F32, TYPE_F16, TYPE_Q4_0, TYPE_Q5_0 = 0, 1, 2, 6
 TYPE_Q8_0 = 8
 TYPE_Q4_K = 12
+TYPE_Q5_K, TYPE_Q6_K = 13, 14
 QK8_0, QK_K = 32, 256
 Q8_0_BYTES, Q8_K_BYTES, Q4_K_BYTES = 34, 292, 144
 
@@ -59,6 +61,9 @@ _CUDA_SIGS = {
     "edgexpu_cuda_dot_quant_q8_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int, _c_vp]),
     "edgexpu_cuda_logits_argmax_dev": (_c_int, [_c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp, ctypes.c_int64, _c_vp, _c_vp]),
     "edgexpu_cuda_block_partials_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_int, _c_int, _c_int, _c_vp]),
+    "edgexpu_cuda_dot_quant": (_c_int, [_c_u32, _c_vp, _c_vp, _c_int, _c_int, _c_f32p, _c_str, _c_sz]),
+    "edgexpu_cuda_dequantize_row": (_c_int, [_c_vp, _c_u32, ctypes.c_int64, _c_int, _c_vp, _c_str, _c_sz]),
+    "edgexpu_cuda_dequantize_rows_dev": (_c_int, [_c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp]),
     "edgexpu_cuda_reserve": (_c_int, [_c_int, _c_int, _c_str, _c_sz]),
     "edgexpu_cuda_stream_sync": (_c_int, [_c_vp, _c_str, _c_sz]),
     "edgexpu_cuda_tp_init": (_c_int, [_c_int, _c_int, _c_vp, _c_str, _c_sz]),
@@ -77,6 +82,9 @@ _HOST_SIGS = {
     "edgexpu_gguf_q8_k_nbytes": (_c_sz, [_c_int]),
     "edgexpu_gguf_quantize_q8_k": (_c_int, [_c_vp, _c_int, _c_vp]),
     "edgexpu_gguf_can_dot_q8k": (_c_int, [_c_u32]),
+    "edgexpu_gguf_dot_quant_q8": (ctypes.c_float, [_c_u32, _c_vp, _c_vp, _c_int]),
+    "edgexpu_gguf_dot_quant_q8k": (ctypes.c_float, [_c_u32, _c_vp, _c_vp, _c_int]),
+    "edgexpu_gguf_dot_quant": (ctypes.c_float, [_c_u32, _c_vp, _c_vp, _c_int]),
     "edgexpu_b200_init": (_c_int, [_c_int, _c_str, _c_sz]),
     "edgexpu_b200_shutdown": (None, []),
     "edgexpu_b200_last_error": (_c_str, []),
@@ -127,16 +135,21 @@ def _check(ok: int, buf=None) -> None:
         raise EdgexpuError(msg)
 
 
+# GGUF type id -> (elements per block, bytes per block), gguf_quant.c:69-106.
+BLOCKS = {TYPE_F32: (1, 4), TYPE_F16: (1, 2), TYPE_Q4_0: (32, 18), TYPE_Q5_0: (32, 22), TYPE_Q8_0: (32, 34),
+          TYPE_Q4_K: (256, 144), TYPE_Q5_K: (256, 176), TYPE_Q6_K: (256, 210)}
+Q8_0_ACT_TYPES = (TYPE_Q8_0, TYPE_Q5_0, TYPE_Q4_0)  # edgexpu_gguf_can_dot_q8; the K-quants use Q8_K
+
+
 def row_bytes(wtype: int, n: int) -> int:
-    if wtype == TYPE_Q8_0:
-        return (n // QK8_0) * Q8_0_BYTES
-    if wtype == TYPE_Q4_K:
-        return (n // QK_K) * Q4_K_BYTES
-    raise ValueError(f"unsupported type {wtype}")
+    if wtype not in BLOCKS:
+        raise ValueError(f"unsupported type {wtype}")
+    qk, bb = BLOCKS[wtype]
+    return (n // qk) * bb
 
 
 def act_row_bytes(wtype: int, n: int) -> int:
-    return (n // QK8_0) * Q8_0_BYTES if wtype == TYPE_Q8_0 else (n // QK_K) * Q8_K_BYTES
+    return (n // QK8_0) * Q8_0_BYTES if wtype in Q8_0_ACT_TYPES else (n // QK_K) * Q8_K_BYTES
 
 
 def init(device: int = 0) -> None:
@@ -186,7 +199,7 @@ def quantize(x, wtype: int):
     x = np.ascontiguousarray(x, dtype=np.float32).ravel()
     out = np.empty(act_row_bytes(wtype, x.size), np.uint8)
     buf = _err_buf()
-    fn = load_cuda().edgexpu_cuda_quantize_q8_0 if wtype == TYPE_Q8_0 else load_cuda().edgexpu_cuda_quantize_q8_k
+    fn = load_cuda().edgexpu_cuda_quantize_q8_0 if wtype in Q8_0_ACT_TYPES else load_cuda().edgexpu_cuda_quantize_q8_k
     _check(fn(x.ctypes.data, x.size, out.ctypes.data, buf, 512), buf)
     return out
 

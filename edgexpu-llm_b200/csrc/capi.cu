@@ -44,7 +44,7 @@ struct Ctx {
   cudaStream_t stream = nullptr;
   ex::DeviceInfo info{};
   std::map<uintptr_t, WeightRec> weights;
-  DevBuf x, xq, out, bias;
+  DevBuf x, xq, out, bias, wrow;
   HostBuf hx, hout, hbias;
   unsigned long long* d_key = nullptr;
   uint32_t* d_status = nullptr;
@@ -71,15 +71,30 @@ int fail(char* error, size_t error_size, const char* fmt, ...) {
     if (e_ != cudaSuccess) return fail(error, error_size, "%s: %s", #call, cudaGetErrorString(e_));       \
   } while (0)
 
+// edgexpu_gguf_row_bytes (gguf_quant.c:468-480) for the quantized types of the path; 0 otherwise.
 size_t row_bytes_of(uint32_t type, int n) {
   if (n <= 0) return 0;
-  if (type == ex::TYPE_Q8_0) return (n % ex::QK8_0) ? 0 : static_cast<size_t>(n / ex::QK8_0) * ex::Q8_0_BYTES;
-  if (type == ex::TYPE_Q4_K) return (n % ex::QK_K) ? 0 : static_cast<size_t>(n / ex::QK_K) * ex::Q4_K_BYTES;
-  return 0;
+  int qk = ex::QK_K, bb = 0;
+  switch (type) {
+    case ex::TYPE_Q8_0: qk = ex::QK8_0; bb = ex::Q8_0_BYTES; break;
+    case ex::TYPE_Q4_0: qk = ex::QK8_0; bb = ex::Q4_0_BYTES; break;
+    case ex::TYPE_Q5_0: qk = ex::QK8_0; bb = ex::Q5_0_BYTES; break;
+    case ex::TYPE_Q4_K: bb = ex::Q4_K_BYTES; break;
+    case ex::TYPE_Q5_K: bb = ex::Q5_K_BYTES; break;
+    case ex::TYPE_Q6_K: bb = ex::Q6_K_BYTES; break;
+    case ex::TYPE_F16: return static_cast<size_t>(n) * 2;
+    case ex::TYPE_F32: return static_cast<size_t>(n) * 4;
+    default: return 0;
+  }
+  return (n % qk) ? 0 : static_cast<size_t>(n / qk) * bb;
 }
 
+// F16/F32 weights: the reference's linear dots them against the fp32 activations directly
+// (cpu_kernel.c:565-568, :633-643).
+bool is_float_type(uint32_t type) { return type == ex::TYPE_F16 || type == ex::TYPE_F32; }
+
 size_t act_row_bytes_of(uint32_t type, int n) {
-  if (type == ex::TYPE_Q8_0) return static_cast<size_t>(n / ex::QK8_0) * ex::Q8_0_BYTES;
+  if (ex::acts_are_q8_0(type)) return static_cast<size_t>(n / ex::QK8_0) * ex::Q8_0_BYTES;
   return static_cast<size_t>(n / ex::QK_K) * ex::Q8_K_BYTES;
 }
 
@@ -132,7 +147,10 @@ int grow_host(HostBuf& b, size_t need, char* error, size_t error_size) {
 // Find the registered tensor holding rows [weight, weight + n_out rows) of width n_in.
 int lookup(const uint8_t* weight, uint32_t type, int n_out, int n_in, char* error, size_t error_size) {
   const size_t rb = row_bytes_of(type, n_in);
-  if (rb == 0) return fail(error, error_size, "unsupported weight type %u or n_in %d (Q8_0: n_in %% 32, Q4_K: n_in %% 256)", type, n_in);
+  if (rb == 0)
+    return fail(error, error_size,
+                "unsupported weight type %u or n_in %d (Q8_0/Q5_0/Q4_0: n_in %% 32, Q4_K/Q5_K/Q6_K: n_in %% 256)", type,
+                n_in);
   const uintptr_t w = reinterpret_cast<uintptr_t>(weight);
   auto it = g.weights.upper_bound(w);
   if (it == g.weights.begin()) return fail(error, error_size, "weight %p is not a registered device tensor", weight);
@@ -155,7 +173,7 @@ int run_rows_dev(float* out, const void* act, bool act_f32, const uint8_t* weigh
                  int m, int n_out, int n_in, cudaStream_t st, char* error, size_t error_size) {
   const size_t qb = act_row_bytes_of(type, n_in);
   const size_t stride = act_f32 ? static_cast<size_t>(n_in) * 4 : qb;
-  const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  const ex::Fmt fmt = ex::fmt_q8(type);
   const int max_m = ex::rowstream_max_m(fmt, n_in, g.info);
   if (max_m <= 0) return fail(error, error_size, "n_in %d too large for the shared-memory activation tile", n_in);
   for (int t0 = 0; t0 < m; t0 += max_m) {
@@ -214,10 +232,15 @@ int run_linear_dev(float* out, const float* x, const uint8_t* weight, uint32_t t
   if (out == nullptr || x == nullptr || weight == nullptr || m <= 0 || n_out <= 0 || n_in <= 0)
     return fail(error, error_size, "invalid arguments");
   if (!lookup(weight, type, n_out, n_in, error, error_size)) return 0;
+  if (is_float_type(type)) {
+    EX_CUDA(ex::launch_dot_f32(type, weight, row_bytes_of(type, n_in), n_out, n_in, x, m, bias, out, st), error,
+            error_size);
+    return 1;
+  }
   if (use_tc(type, m, n_in))
     return tc_pack(x, nullptr, m, n_in, st, error, error_size) &&
            tc_gemm(out, nullptr, weight, bias, m, n_out, n_in, st, error, error_size);
-  const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  const ex::Fmt fmt = ex::fmt_q8(type);
   // cpu_kernel.c:577-631: every activation row is quantized once, then each weight row is dotted
   // against every quantized row.  Small batches quantize inside the GEMV launch itself.
   if (ex::rowstream_quantizes_itself(fmt, m))
@@ -225,8 +248,7 @@ int run_linear_dev(float* out, const float* x, const uint8_t* weight, uint32_t t
   const size_t qb = act_row_bytes_of(type, n_in);
   if (!grow_dev(g.xq, static_cast<size_t>(m) * qb + 64, st, error, error_size)) return 0;
   uint8_t* xq = static_cast<uint8_t*>(g.xq.p);
-  EX_CUDA(type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n_in, xq, st) : ex::launch_quantize_q8_k(x, m, n_in, xq, st),
-          error, error_size);
+  EX_CUDA(ex::launch_quantize_for(type, x, m, n_in, xq, st), error, error_size);
   return run_rows_dev(out, xq, false, weight, type, bias, m, n_out, n_in, st, error, error_size);
 }
 
@@ -237,6 +259,14 @@ int run_logits_dev(const uint8_t* weight, uint32_t type, const float* hidden, in
   if (row0 < 0 || row0 + vocab > 0xFFFFFFFFll) return fail(error, error_size, "row0 %lld out of range", (long long)row0);
   if (!lookup(weight, type, vocab, n_embd, error, error_size)) return 0;
   EX_CUDA(cudaMemsetAsync(key, 0, sizeof(unsigned long long), st), error, error_size);
+  if (is_float_type(type)) {  // F16/F32 output weights: fp32 scores (dot_f16 / dot_f32_row), then the key
+    if (!grow_dev(g.out, static_cast<size_t>(vocab) * 4, st, error, error_size)) return 0;
+    float* scores = static_cast<float*>(g.out.p);
+    EX_CUDA(ex::launch_dot_f32(type, weight, row_bytes_of(type, n_embd), vocab, n_embd, hidden, 1, bias, scores, st),
+            error, error_size);
+    EX_CUDA(ex::launch_argmax_key(scores, vocab, row0, key, st), error, error_size);
+    return 1;
+  }
   ex::RowStreamArgs a{};
   a.mode = ex::RowOut::Argmax;
   a.w = weight;
@@ -250,14 +280,14 @@ int run_logits_dev(const uint8_t* weight, uint32_t type, const float* hidden, in
   a.status = g.d_status;
   a.act = hidden;
   a.act_f32 = true;
-  if (type == ex::TYPE_Q8_0) {
-    // native.c:2317-2319: Q8_0-class logits weights see a Q8_0-quantized hidden state (the
-    // kernel quantizes it in its prologue).
-    a.fmt = ex::Fmt::Q8_0xQ8_0;
+  a.fmt = ex::logits_fmt(type);
+  if (ex::acts_are_q8_0(type)) {
+    // native.c:2317-2319: Q8_0-class logits weights (can_dot_q8) see a Q8_0-quantized hidden
+    // state (the kernel quantizes it in its prologue).
     a.act_row_bytes = static_cast<int>(act_row_bytes_of(type, n_embd));
   } else {
-    // logit_dot_row native.c:445-462 -> dot_q4_k gguf_quant.c:704-752: fp32 hidden state.
-    a.fmt = ex::Fmt::Q4_KxF32;
+    // logit_dot_row native.c:445-462 -> edgexpu_gguf_dot_quant gguf_quant.c:894-918: the K-quants
+    // see the fp32 hidden state.
     a.act_row_bytes = n_embd * 4;
   }
   if (ex::rowstream_max_m(a.fmt, n_embd, g.info) < 1) return fail(error, error_size, "n_embd %d too large", n_embd);
@@ -271,11 +301,12 @@ int check_status(char* error, size_t error_size) {
     const uint32_t s = *g.h_status;
     *g.h_status = 0;
     cudaMemset(g.d_status, 0, sizeof(uint32_t));
-    return fail(error, error_size, "device wait timed out (status 0x%x):%s%s%s%s", s,
+    return fail(error, error_size, "device status 0x%x:%s%s%s%s%s", s,
                 (s & ex::ST_TIMEOUT_FULL) ? " a consumer gave up waiting for a tile copy;" : "",
                 (s & ex::ST_TIMEOUT_EMPTY) ? " the producer gave up waiting for a free stage;" : "",
                 (s & ex::ST_TIMEOUT_DRAIN) ? " copies were still in flight at exit;" : "",
-                (s & ex::ST_TIMEOUT_PEER) ? " a tensor-parallel peer did not deliver its partial in time;" : "");
+                (s & ex::ST_TIMEOUT_PEER) ? " a tensor-parallel peer did not deliver its partial in time;" : "",
+                (s & ex::ST_BAD_INDEX) ? " a row id was outside the tensor;" : "");
   }
   return 1;
 }
@@ -331,7 +362,7 @@ int edgexpu_cuda_shutdown(void) {
   for (auto& kv : g.weights)
     if (kv.second.owned) cudaFree(reinterpret_cast<void*>(kv.first));
   g.weights.clear();
-  for (DevBuf* b : {&g.x, &g.xq, &g.out, &g.bias})
+  for (DevBuf* b : {&g.x, &g.xq, &g.out, &g.bias, &g.wrow})
     if (b->p) cudaFree(b->p);
   for (HostBuf* b : {&g.hx, &g.hout, &g.hbias})
     if (b->p) cudaFreeHost(b->p);
@@ -488,14 +519,101 @@ int edgexpu_cuda_logits_argmax(const uint8_t* weight, uint32_t type, const float
   return 1;
 }
 
+// Where the registered tensor holding `weight` starts, and its row count (0 if not registered).
+static const uint8_t* tensor_of(const uint8_t* weight, long long* n_rows) {
+  auto it = g.weights.upper_bound(reinterpret_cast<uintptr_t>(weight));
+  if (it == g.weights.begin()) return nullptr;
+  --it;
+  if (reinterpret_cast<uintptr_t>(weight) >= it->first + it->second.capacity) return nullptr;
+  *n_rows = it->second.n_out;
+  return reinterpret_cast<const uint8_t*>(it->first);
+}
+
+int edgexpu_cuda_dequantize_rows_dev(float* out, const uint8_t* weight, uint32_t type, const int32_t* ids, int n_ids,
+                                     int n_in, void* stream) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(nullptr, 0)) return 0;
+  if (out == nullptr || weight == nullptr || n_ids <= 0 || n_in <= 0) return fail(nullptr, 0, "dequantize_rows: invalid arguments");
+  long long n_rows = 0;
+  if (tensor_of(weight, &n_rows) != weight) return fail(nullptr, 0, "dequantize_rows: %p is not a registered tensor handle", weight);
+  if (!lookup(weight, type, static_cast<int>(n_rows), n_in, nullptr, 0)) return 0;
+  if (ids == nullptr && n_ids > n_rows) return fail(nullptr, 0, "dequantize_rows: %d rows exceed the tensor's %lld", n_ids, n_rows);
+  EX_CUDA(ex::launch_dequant_rows(type, weight, row_bytes_of(type, n_in), n_rows, ids, n_ids, n_in, out, g.d_status,
+                                  pick(stream)),
+          nullptr, 0);
+  return 1;
+}
+
+int edgexpu_cuda_dequantize_row(const uint8_t* weight, uint32_t type, int64_t row, int n_in, float* dst, char* error,
+                                size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  if (weight == nullptr || dst == nullptr || n_in <= 0) return fail(error, error_size, "dequantize_row: invalid arguments");
+  long long n_rows = 0;
+  if (tensor_of(weight, &n_rows) != weight) return fail(error, error_size, "dequantize_row: %p is not a registered tensor handle", weight);
+  if (!lookup(weight, type, static_cast<int>(n_rows), n_in, error, error_size)) return 0;
+  if (row < 0 || row >= n_rows) return fail(error, error_size, "dequantize_row: row %lld outside the tensor's %lld rows", (long long)row, n_rows);
+  cudaStream_t st = g.stream;
+  const size_t ob = static_cast<size_t>(n_in) * 4;
+  if (!grow_dev(g.out, ob, st, error, error_size) || !grow_host(g.hout, ob, error, error_size)) return 0;
+  const size_t rb = row_bytes_of(type, n_in);
+  EX_CUDA(ex::launch_dequant_rows(type, weight + static_cast<size_t>(row) * rb, rb, 1, nullptr, 1, n_in,
+                                  static_cast<float*>(g.out.p), g.d_status, st),
+          error, error_size);
+  EX_CUDA(cudaMemcpyAsync(g.hout.p, g.out.p, ob, cudaMemcpyDeviceToHost, st), error, error_size);
+  if (!sync_and_check(st, error, error_size)) return 0;
+  std::memcpy(dst, g.hout.p, ob);
+  return 1;
+}
+
+int edgexpu_cuda_dot_quant(uint32_t type, const uint8_t* wrow, const void* x, int x_quantized, int n, float* result,
+                           char* error, size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  const size_t rb = row_bytes_of(type, n);
+  ex::Fmt fmt;
+  if (wrow == nullptr || x == nullptr || result == nullptr || rb == 0) return fail(error, error_size, "dot_quant: invalid arguments or type %u", type);
+  if (x_quantized && !ex::fmt_of_type(type, &fmt)) return fail(error, error_size, "dot_quant: type %u has no quantized-activation dot", type);
+  cudaStream_t st = g.stream;
+  // The row: a row of a registered tensor is used in place; anything else is host memory (the
+  // reference's mmap'd row) and is copied first.
+  long long n_rows = 0;
+  const uint8_t* w = wrow;
+  if (tensor_of(wrow, &n_rows) == nullptr) {
+    if (!grow_dev(g.wrow, rb + 256, st, error, error_size)) return 0;
+    EX_CUDA(cudaMemcpyAsync(g.wrow.p, wrow, rb, cudaMemcpyHostToDevice, st), error, error_size);
+    EX_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(g.wrow.p) + rb, 0, 256, st), error, error_size);
+    w = static_cast<const uint8_t*>(g.wrow.p);
+  } else if (!lookup(wrow, type, 1, n, error, error_size)) {
+    return 0;
+  }
+  const size_t xb = x_quantized ? act_row_bytes_of(type, n) : static_cast<size_t>(n) * 4;
+  if (!grow_host(g.hx, xb, error, error_size) || !grow_dev(g.x, xb + 64, st, error, error_size) ||
+      !grow_dev(g.out, 64, st, error, error_size) || !grow_host(g.hout, 64, error, error_size))
+    return 0;
+  std::memcpy(g.hx.p, x, xb);
+  EX_CUDA(cudaMemcpyAsync(g.x.p, g.hx.p, xb, cudaMemcpyHostToDevice, st), error, error_size);
+  float* d_out = static_cast<float*>(g.out.p);
+  if (x_quantized) {
+    if (!run_rows_dev(d_out, g.x.p, false, w, type, nullptr, 1, 1, n, st, error, error_size)) return 0;
+  } else {
+    EX_CUDA(ex::launch_dot_f32(type, w, rb, 1, n, static_cast<const float*>(g.x.p), 1, nullptr, d_out, st), error,
+            error_size);
+  }
+  EX_CUDA(cudaMemcpyAsync(g.hout.p, d_out, 4, cudaMemcpyDeviceToHost, st), error, error_size);
+  if (!sync_and_check(st, error, error_size)) return 0;
+  std::memcpy(result, g.hout.p, 4);
+  return 1;
+}
+
 int edgexpu_cuda_quantize_dev(uint32_t weight_type, const float* x, int m, int n, uint8_t* dst, void* stream) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   if (!need_ready(nullptr, 0)) return 0;
-  const int blk = weight_type == ex::TYPE_Q8_0 ? ex::QK8_0 : (weight_type == ex::TYPE_Q4_K ? ex::QK_K : 0);
+  ex::Fmt f;
+  const int blk = !ex::fmt_of_type(weight_type, &f) ? 0 : (ex::acts_are_q8_0(weight_type) ? ex::QK8_0 : ex::QK_K);
   if (blk == 0 || x == nullptr || dst == nullptr || m <= 0 || n <= 0 || n % blk != 0) return fail(nullptr, 0, "invalid arguments");
   cudaStream_t st = pick(stream);
-  EX_CUDA(weight_type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n, dst, st) : ex::launch_quantize_q8_k(x, m, n, dst, st),
-          nullptr, 0);
+  EX_CUDA(ex::launch_quantize_for(weight_type, x, m, n, dst, st), nullptr, 0);
   return 1;
 }
 
@@ -527,15 +645,13 @@ int edgexpu_cuda_linear_quant_multi_dev(int n, float* const* outs, const uint8_t
         return 0;
     return 1;
   }
-  const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  const ex::Fmt fmt = ex::fmt_q8(type);
   const size_t qb = act_row_bytes_of(type, n_in);
   const bool fused = ex::rowstream_quantizes_itself(fmt, m);
   const uint8_t* act = reinterpret_cast<const uint8_t*>(x);
   if (!fused) {
     if (!grow_dev(g.xq, static_cast<size_t>(m) * qb + 64, st, nullptr, 0)) return 0;
-    EX_CUDA(type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n_in, static_cast<uint8_t*>(g.xq.p), st)
-                                  : ex::launch_quantize_q8_k(x, m, n_in, static_cast<uint8_t*>(g.xq.p), st),
-            nullptr, 0);
+    EX_CUDA(ex::launch_quantize_for(type, x, m, n_in, static_cast<uint8_t*>(g.xq.p), st), nullptr, 0);
     act = static_cast<const uint8_t*>(g.xq.p);
   }
   const size_t stride = fused ? static_cast<size_t>(n_in) * 4 : qb;
@@ -592,7 +708,7 @@ int edgexpu_cuda_block_partials_dev(int32_t* partials, const uint8_t* xq, const 
     return tc_pack(nullptr, xq, m, n_in, pick(stream), nullptr, 0) &&
            tc_gemm(nullptr, partials, weight, nullptr, m, n_out, n_in, pick(stream), nullptr, 0);
   ex::RowStreamArgs a{};
-  a.fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  a.fmt = ex::fmt_q8(type);
   a.mode = ex::RowOut::Partials;
   a.w = weight;
   a.n_rows = n_out;

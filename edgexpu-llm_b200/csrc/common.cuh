@@ -1,9 +1,13 @@
 // common.cuh -- block layouts and sm_100a device helpers shared by the edgexpu CUDA kernels.
 //
-// GGUF block layouts (the reference's src/gguf_dot_q8.c:18-26 and :90-110, src/gguf_quant.c:212-266):
+// GGUF block layouts (the reference's src/gguf_dot_q8.c:18-26 and :90-110, src/gguf_quant.c:139-353):
 //   Q8_0  34 B : fp16 d @0, int8 qs[32] @2
 //   Q8_K  292 B: fp32 d @0, int8 qs[256] @4, int16 bsums[16] @260
 //   Q4_K  144 B: fp16 d @0, fp16 dmin @2, 12 B packed 6-bit scales/mins @4, 128 B nibbles @16
+//   Q4_0  18 B : fp16 d @0, 16 B nibbles @2 (element j low nibble, 16+j high; offset 8)
+//   Q5_0  22 B : fp16 d @0, u32 fifth bits @2, 16 B nibbles @6 (offset 16)
+//   Q5_K  176 B: fp16 d @0, fp16 dmin @2, 12 B scales/mins @4, qh[32] @16, ql[128] @48
+//   Q6_K  210 B: ql[128] @0, qh[64] @128, int8 scales[16] @192, fp16 d @208 (offset 32)
 // Weights stay in exactly this layout in HBM; nothing is repacked at upload.
 #pragma once
 
@@ -17,15 +21,27 @@ constexpr int QK_K = 256;
 constexpr int Q8_0_BYTES = 34;
 constexpr int Q8_K_BYTES = 292;
 constexpr int Q4_K_BYTES = 144;
+constexpr int Q4_0_BYTES = 18;   // fp16 d, 16 nibble bytes                         (gguf_dot_q8.c:23)
+constexpr int Q5_0_BYTES = 22;   // fp16 d, 32 fifth bits, 16 nibble bytes          (gguf_dot_q8.c:22)
+constexpr int Q5_K_BYTES = 176;  // fp16 d, fp16 dmin, 12 scale bytes, qh[32], ql[128] (gguf_dot_q8.c:25)
+constexpr int Q6_K_BYTES = 210;  // ql[128], qh[64], int8 scales[16], fp16 d          (gguf_dot_q8.c:26)
 
-constexpr uint32_t TYPE_Q8_0 = 8;   // EDGEXPU_GGUF_TYPE_Q8_0, include/edgexpu/gguf_quant.h:144
-constexpr uint32_t TYPE_Q4_K = 12;  // EDGEXPU_GGUF_TYPE_Q4_K, include/edgexpu/gguf_quant.h:145
+// GGUF type ids, EDGEXPU_GGUF_TYPE_* in include/edgexpu/gguf_quant.h:17-24.
+constexpr uint32_t TYPE_F32 = 0;
+constexpr uint32_t TYPE_F16 = 1;
+constexpr uint32_t TYPE_Q4_0 = 2;
+constexpr uint32_t TYPE_Q5_0 = 6;
+constexpr uint32_t TYPE_Q8_0 = 8;
+constexpr uint32_t TYPE_Q4_K = 12;
+constexpr uint32_t TYPE_Q5_K = 13;
+constexpr uint32_t TYPE_Q6_K = 14;
 
 // Bits of the device status word (host-mapped; kernels only ever OR into it).
 constexpr uint32_t ST_TIMEOUT_FULL = 1u;   // a consumer gave up waiting for a tile copy
 constexpr uint32_t ST_TIMEOUT_EMPTY = 2u;  // the producer gave up waiting for a free stage
 constexpr uint32_t ST_TIMEOUT_DRAIN = 4u;  // copies still in flight at exit after the limit
 constexpr uint32_t ST_TIMEOUT_PEER = 8u;   // a tensor-parallel peer did not deliver its partial in time
+constexpr uint32_t ST_BAD_INDEX = 16u;     // a row id passed to a gather was outside the tensor
 
 // Every mbarrier wait gives up after this long and reports through the status word.
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // 2 s

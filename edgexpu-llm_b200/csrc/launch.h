@@ -12,6 +12,18 @@ namespace ex {
 cudaError_t launch_quantize_q8_0(const float* x, int m, int n, uint8_t* dst, cudaStream_t st);
 cudaError_t launch_quantize_q8_k(const float* x, int m, int n, uint8_t* dst, cudaStream_t st);
 
+// Element-wise row decoding (dequant.cu) for every GGUF type the path accepts (F32, F16, Q8_0,
+// Q4_0, Q5_0, Q4_K, Q5_K, Q6_K), with the reference's float expressions.
+//   out[i][e] = row ids[i] of w (row i if ids is null) dequantized; ids outside [0, n_rows) give NaN
+//   rows and set ST_BAD_INDEX in *status.
+cudaError_t launch_dequant_rows(uint32_t type, const uint8_t* w, size_t row_bytes, long long n_rows,
+                                const int32_t* ids, int n_ids, int n, float* out, uint32_t* status, cudaStream_t st);
+//   out[t*n_out + o] = bias[o] + dot(dequantized row o, x_t) with fp32 activations x [m][n].
+cudaError_t launch_dot_f32(uint32_t type, const uint8_t* w, size_t row_bytes, int n_out, int n, const float* x, int m,
+                           const float* bias, float* out, cudaStream_t st);
+//   atomicMax of argmax_key(scores[i], row0 + i) over i < n into *key (the caller zeroes *key).
+cudaError_t launch_argmax_key(const float* scores, int n, long long row0, unsigned long long* key, cudaStream_t st);
+
 // What the row-stream kernel does with each finished row.
 enum class RowOut : int {
   Store = 0,     // out[t*out_stride + r] = bias[r] + dot
@@ -24,7 +36,27 @@ enum class Fmt : int {
   Q8_0xQ8_0 = 0,  // Q8_0 weight . Q8_0 activation   (gguf_dot_q8.c:436-480)
   Q4_KxQ8_K = 1,  // Q4_K weight . Q8_K activation   (gguf_dot_q8.c:603-762)
   Q4_KxF32 = 2,   // Q4_K weight . fp32 activation   (gguf_quant.c:704-752, logits path)
+  Q4_0xQ8_0 = 3,  // Q4_0 weight . Q8_0 activation   (gguf_dot_q8.c:552-601)
+  Q5_0xQ8_0 = 4,  // Q5_0 weight . Q8_0 activation   (gguf_dot_q8.c:482-550)
+  Q5_KxQ8_K = 5,  // Q5_K weight . Q8_K activation   (gguf_dot_q8.c:764-895)
+  Q6_KxQ8_K = 6,  // Q6_K weight . Q8_K activation   (gguf_dot_q8.c:897-1002)
+  Q5_KxF32 = 7,   // Q5_K weight . fp32 activation   (gguf_quant.c:837-892, logits path)
+  Q6_KxF32 = 8,   // Q6_K weight . fp32 activation   (gguf_quant.c:754-794, logits path)
 };
+
+// Activations a format reads: GGUF Q8_0 rows, GGUF Q8_K rows, or fp32 rows.
+enum class Act : int { Q8_0 = 0, Q8_K = 1, F32 = 2 };
+
+__host__ __device__ constexpr Act act_of(Fmt f) {
+  return (f == Fmt::Q8_0xQ8_0 || f == Fmt::Q4_0xQ8_0 || f == Fmt::Q5_0xQ8_0) ? Act::Q8_0
+         : (f == Fmt::Q4_KxF32 || f == Fmt::Q5_KxF32 || f == Fmt::Q6_KxF32) ? Act::F32
+                                                                              : Act::Q8_K;
+}
+
+// Formats instantiated in rowstream.cu (the original two types); the rest are in rowstream_more.cu.
+__host__ __device__ constexpr bool fmt_is_core(Fmt f) {
+  return f == Fmt::Q8_0xQ8_0 || f == Fmt::Q4_KxQ8_K || f == Fmt::Q4_KxF32;
+}
 
 // One weight tensor of a grouped launch: the segments share K, the weight type and the
 // activations, and each writes its own output (row stride = its n_rows).

@@ -65,9 +65,9 @@ extern "C" int edgexpu_cuda_linear_quant_batch_noalloc(float* out, const float* 
   }
   uint8_t* xq = g_scratch_addr[dev];
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n_in, xq, st) : ex::launch_quantize_q8_k(x, m, n_in, xq, st);
+  cudaError_t e = ex::launch_quantize_for(type, x, m, n_in, xq, st);
   if (e != cudaSuccess) return ex::api_fail(nullptr, 0, "noalloc linear: quantize launch: %s", cudaGetErrorString(e));
-  const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  const ex::Fmt fmt = ex::fmt_q8(type);
   const int max_m = ex::rowstream_max_m(fmt, n_in, ex::api_device_info());
   if (max_m <= 0) return ex::api_fail(nullptr, 0, "noalloc linear: n_in %d too large for the activation tile", n_in);
   for (int t0 = 0; t0 < m; t0 += max_m) {

@@ -1,879 +1,9 @@
-// rowstream.cu -- persistent weight-streaming GEMV for quantized GGUF rows on sm_100a.
-//
-// One kernel serves the reference's three hot dots (per output row o, per token t):
-//   Q8_0 x Q8_0  out = bias + sum_b d_w*d_x*(sum_{j<32} qw*qx)          gguf_dot_q8.c:436-480
-//   Q4_K x Q8_K  out = bias + sum_b d_x*d_w*sumi_b - d_x*dmin_w*summ_b     gguf_dot_q8.c:603-762
-//   Q4_K x fp32  out = bias + sum_subblocks d*sc*sum(q*x) - dmin*m*sum(x)  gguf_quant.c:704-752
-// and three epilogues: store rows (cpu_kernel.c:545-644), greedy argmax over rows
-// (native.c:2355-2397), or per-block int32 partials (test hook for bit-exactness).
-//
-// Design (HBM-bound streaming, batch 1-8):
-//   * grid = one CTA per SM (persistent); CTA c takes tiles c, c+grid, ...; a tile is R whole
-//     rows, i.e. one contiguous byte range (up to 32 KB) of the row-major GGUF tensor.
-//   * warp 0, lane 0 is the producer: it moves each tile into a ring of shared-memory stages
-//     with a 1-D TMA bulk copy (cp.async.bulk, L2 evict-first hint) that completes on the
-//     stage's "full" mbarrier.  Misaligned starts are rounded down to 16 bytes and the
-//     in-stage offset is applied by the consumers.  The producer starts streaming weights at
-//     once; only the consumers depend on the activations.
-//   * warps 1..15 are consumers.  They first bring the activations into shared memory: for
-//     small batches they quantize the fp32 rows themselves (Q8_0 / Q8_K, same arithmetic as the
-//     standalone quantizer), otherwise they copy pre-quantized GGUF blocks.  The layout is
-//     "unit-interleaved": 16-byte chunk j of work unit u of token t sits at (t*J + j)*U + u, so
-//     the lanes of a warp, which hold consecutive units, read consecutive chunks.
-//   * rows are dealt round-robin over the consumer warps along the CTA's tile sequence; a warp
-//     computes a whole row (lane = work unit: a Q8_0 block or half a Q4_K super-block; integer
-//     dots use dp4a), sums its lanes with a fixed shuffle tree (deterministic results), stores
-//     the row or folds it into the argmax key, and releases a stage once done with its rows in
-//     it.  No CTA-wide barrier sits in the loop, so warps overlap each other's latency.
-//   * every mbarrier wait is bounded; a timeout sets a status bit, raises a CTA-wide abort
-//     flag, and the producer still waits (bounded) for its in-flight copies before exiting.
-#include "common.cuh"
-#include "launch.h"
-#include "quant.cuh"
+// rowstream.cu -- host side of the row-stream GEMV: launch geometry and dispatch over the
+// weight formats.  The kernel template is in rowstream_kernel.cuh; the Q8_0 and Q4_K formats are
+// instantiated here, the other GGUF types in rowstream_more.cu.
+#include "rowstream_kernel.cuh"
 
 namespace ex {
-namespace {
-
-constexpr int CONSUMER_WARPS = 15;  // + 1 producer warp = 16 warps, 4 per SM sub-partition (128 registers each)
-constexpr int CONSUMERS = CONSUMER_WARPS * 32;
-constexpr int THREADS = CONSUMERS + 32;
-#ifndef EX_RS_STAGE
-#define EX_RS_STAGE 32768
-#endif
-constexpr int STAGE_TARGET = EX_RS_STAGE;
-constexpr int MAX_STAGES = 8;
-constexpr int BAR_BYTES = 512;        // full[8], empty[8], abort flag, tile descriptors[8] at 256
-constexpr int ACT_BUDGET = 96 * 1024;
-constexpr int STAGE_SLACK = 48;       // alignment round-down (<16) + over-read of the last block
-constexpr int MAX_M = 8;              // activation rows (tokens) per launch; the host splits more
-constexpr int PROLOGUE_QUANT_MAX_M = 2;
-constexpr int PRO_BATCH = 4;          // activation blocks a consumer warp loads before quantizing them
-#ifndef EX_RS_PRE
-#define EX_RS_PRE 2
-#endif
-constexpr int PRE_STAGES = EX_RS_PRE;  // weight copies the producer issues before the activations land
-constexpr unsigned long long HOLD_LIMIT_NS = 20000;  // the hold is a scheduling aid: give up after 20 us
-
-struct Layout {
-  int tile_rows;
-  long long n_tiles;
-  int stage_bytes;
-  int n_stages;
-  int act_off;
-  int stage_off;
-  int smem_total;
-};
-
-// ---- activation layout in shared memory ----------------------------------------------------------
-//   Q8_0 x Q8_0 : unit = block (U = K/32): q chunks (t*2 + j)*U + u, then d[t*U + u]
-//   Q4_K x Q8_K : unit = half super-block (U = K/128): q chunks (t*8 + j)*U + u, then bsum chunks
-//                 [t*U + u] (4 ints: sub-blocks 4h..4h+3), then d[t*(U/2) + sb]
-//   Q4_K x fp32 : unit = half super-block: x chunks (t*32 + j)*U + u, then sum chunks [t*U + u]
-//                 (4 floats: sub-block sums)
-__host__ __device__ __forceinline__ int units_per_row(Fmt f, int K) { return f == Fmt::Q8_0xQ8_0 ? K / QK8_0 : K / 128; }
-
-__host__ __device__ __forceinline__ int act_bytes_total(Fmt f, int K, int m) {
-  const int U = units_per_row(f, K);
-  if (f == Fmt::Q8_0xQ8_0) return m * U * 32 + m * U * 4;
-  if (f == Fmt::Q4_KxQ8_K) return m * U * 128 + m * U * 16 + m * (U / 2) * 4;
-  return m * U * 512 + m * U * 16;
-}
-
-__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
-  // unsigned bytes of a times signed bytes of b, accumulated into c
-  int d;
-  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
-// Wait (at most HOLD_LIMIT_NS; nothing depends on it for correctness) until every consumer warp
-// reported its activation loads landed.
-__device__ __forceinline__ void hold_for_activations(uint64_t* xin) {
-  if (mbar_try_wait(xin, 0)) return;
-  const unsigned long long t0 = global_ns();
-  while (!mbar_try_wait_sleep(xin, 0, 1000u))
-    if (global_ns() - t0 > HOLD_LIMIT_NS) return;
-}
-
-// ---- activation prologue ---------------------------------------------------------------------------
-
-// Lane 0 of every consumer warp arrives once on `xin` when the warp's first activation loads
-// have landed (or, on paths without a separate load phase, when it is done): the producer holds
-// back all but its first PRE_STAGES weight copies until then, so the activations -- on the
-// critical path of every launch -- do not queue behind a full ring of weights into the SM.
-__device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct, uint64_t* xin) {
-  bool arrived = false;
-  const int K = a.K, m = a.m, lane = ct & 31, cw = ct >> 5;
-  const int U = units_per_row(a.fmt, K);
-  if (a.fmt == Fmt::Q8_0xQ8_0) {
-    int4* xq = reinterpret_cast<int4*>(act);
-    float* xd = reinterpret_cast<float*>(act + m * U * 32);
-    if (a.act_f32) {  // quantize in place: one warp per block (quant.cuh), loads of a batch issued first
-      const float* x = static_cast<const float*>(a.act);
-      const int nblk = m * U;
-      for (int base = cw; base < nblk; base += PRO_BATCH * CONSUMER_WARPS) {
-        float v[PRO_BATCH];
-#pragma unroll
-        for (int k = 0; k < PRO_BATCH; ++k) {
-          const int blk = base + k * CONSUMER_WARPS;
-          if (blk < nblk) {
-            const int t = blk / U, b = blk - t * U;
-            v[k] = x[static_cast<size_t>(t) * K + b * QK8_0 + lane];
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < PRO_BATCH; ++k) {
-          const int blk = base + k * CONSUMER_WARPS;
-          if (blk < nblk) {  // warp-uniform
-            const int t = blk / U, b = blk - t * U;
-            uint32_t dbits;
-            const int q = warp_q8_0(v[k], &dbits);
-            // lane i holds element i: gather 4 consecutive lanes into one word
-            const int q1 = __shfl_down_sync(0xFFFFFFFFu, q, 1), q2 = __shfl_down_sync(0xFFFFFFFFu, q, 2),
-                      q3 = __shfl_down_sync(0xFFFFFFFFu, q, 3);
-            if ((lane & 3) == 0) {
-              reinterpret_cast<uint32_t*>(xq + (t * 2 + (lane >> 4)) * U + b)[(lane >> 2) & 3] = pack4_i8(q, q1, q2, q3);
-            }
-            if (lane == 0) xd[t * U + b] = fp16_bits_to_float(dbits);
-          }
-        }
-      }
-    } else {  // pre-quantized GGUF Q8_0 rows: 17 half-words per 34-byte block
-      const uint8_t* src = static_cast<const uint8_t*>(a.act);
-      for (int i = ct; i < m * U * 17; i += CONSUMERS) {
-        const int t = i / (U * 17), rem = i - t * U * 17, b = rem / 17, hw = rem - b * 17;
-        const uint16_t v = *reinterpret_cast<const uint16_t*>(src + static_cast<size_t>(t) * a.act_row_bytes +
-                                                              b * Q8_0_BYTES + hw * 2);
-        if (hw == 0) {
-          xd[t * U + b] = fp16_bits_to_float(v);
-        } else {
-          const int e = (hw - 1) * 2;  // element offset inside the block
-          reinterpret_cast<uint16_t*>(xq + (t * 2 + (e >> 4)) * U + b)[(e & 15) >> 1] = v;
-        }
-      }
-    }
-  } else if (a.fmt == Fmt::Q4_KxQ8_K) {
-    const int nb = U / 2;
-    int4* xq = reinterpret_cast<int4*>(act);
-    int* xb = reinterpret_cast<int*>(act + m * U * 128);
-    float* xd = reinterpret_cast<float*>(act + m * U * 128 + m * U * 16);
-    if (a.act_f32) {  // quantize in place: one warp per 256-block (quant.cuh), loads of a batch issued first
-      const float* x = static_cast<const float*>(a.act);
-      const int nblk = m * nb;
-      for (int base = cw; base < nblk; base += PRO_BATCH * CONSUMER_WARPS) {
-        float4 ld[PRO_BATCH][2];
-#pragma unroll
-        for (int k = 0; k < PRO_BATCH; ++k) {
-          const int blk = base + k * CONSUMER_WARPS;
-          if (blk < nblk) {
-            const int t = blk / nb, sb = blk - t * nb;
-            const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * K + sb * QK_K + lane * 8);
-            ld[k][0] = src[0];
-            ld[k][1] = src[1];
-          }
-        }
-        if (!arrived) {  // the vote issues once every lane's first load has landed; the arrive after it
-          const int seen = __any_sync(0xFFFFFFFFu, ld[0][0].x != ld[0][0].x);
-          uint64_t* bar = xin;
-          asm volatile("" : "+l"(bar) : "r"(seen));  // keeps the arrive after the vote
-          if (lane == 0) mbar_arrive(bar);
-          arrived = true;
-        }
-#pragma unroll
-        for (int k = 0; k < PRO_BATCH; ++k) {
-          const int blk = base + k * CONSUMER_WARPS;
-          if (blk < nblk) {  // warp-uniform
-            const int t = blk / nb, sb = blk - t * nb;
-            const float v[8] = {ld[k][0].x, ld[k][0].y, ld[k][0].z, ld[k][0].w,
-                                ld[k][1].x, ld[k][1].y, ld[k][1].z, ld[k][1].w};
-            int q[8], gsum;
-            const float d = warp_q8_k(v, q, &gsum);
-            // lane l holds elements 8l..8l+7: unit h = l/16, chunk j = (l%16)/2, half (l&1)
-            const int u = 2 * sb + (lane >> 4), j = (lane & 15) >> 1;
-            uint2* dst = reinterpret_cast<uint2*>(xq + (t * 8 + j) * U + u) + (lane & 1);
-            *dst = make_uint2(pack4_i8(q[0], q[1], q[2], q[3]), pack4_i8(q[4], q[5], q[6], q[7]));
-            // sub-block (32 elements) sums: lanes 4s .. 4s+3 (gsum already covers lane pairs)
-            const int s32 = gsum + __shfl_down_sync(0xFFFFFFFFu, gsum, 2);
-            if ((lane & 3) == 0) xb[(t * U + u) * 4 + ((lane >> 2) & 3)] = s32;
-            if (lane == 0) xd[t * nb + sb] = d;
-          }
-        }
-      }
-    } else {  // pre-quantized GGUF Q8_K rows: 73 words per 292-byte block
-      const uint8_t* src = static_cast<const uint8_t*>(a.act);
-      for (int i = ct; i < m * nb * 73; i += CONSUMERS) {
-        const int t = i / (nb * 73), rem = i - t * nb * 73, sb = rem / 73, wi = rem - sb * 73;
-        const uint32_t v = *reinterpret_cast<const uint32_t*>(src + static_cast<size_t>(t) * a.act_row_bytes +
-                                                              sb * Q8_K_BYTES + wi * 4);
-        if (wi == 0) {
-          xd[t * nb + sb] = __uint_as_float(v);
-        } else if (wi <= 64) {
-          const int e = (wi - 1) * 4;  // element offset inside the super-block
-          const int u = 2 * sb + (e >> 7), j = (e & 127) >> 4;
-          reinterpret_cast<uint32_t*>(xq + (t * 8 + j) * U + u)[(e & 15) >> 2] = v;
-        } else {
-          const int s = wi - 65;  // sub-block s: bsum groups 2s, 2s+1
-          const int lo = static_cast<int16_t>(v & 0xFFFFu), hi = static_cast<int16_t>(v >> 16);
-          xb[(t * U + 2 * sb + (s >> 2)) * 4 + (s & 3)] = lo + hi;
-        }
-      }
-    }
-  } else {  // fp32 activations for the Q4_K logits path
-    const float* x = static_cast<const float*>(a.act);
-    float4* xf = reinterpret_cast<float4*>(act);
-    float* xs = reinterpret_cast<float*>(act + m * U * 512);
-    for (int i = ct; i < m * U * 32; i += CONSUMERS) {  // i = source float4 index
-      const int t = i / (U * 32), rem = i - t * U * 32, u = rem >> 5, j = rem & 31;
-      xf[(t * 32 + j) * U + u] = reinterpret_cast<const float4*>(x)[i];
-    }
-    for (int i = ct; i < m * U * 4; i += CONSUMERS) {  // sub-block sums, sequential order
-      const float4* p = reinterpret_cast<const float4*>(x + static_cast<size_t>(i) * 32);
-      float s = 0.0f;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float4 v = p[k];
-        s += v.x;
-        s += v.y;
-        s += v.z;
-        s += v.w;
-      }
-      const int t = i / (U * 4), rem = i - t * U * 4;
-      xs[(t * U + (rem >> 2)) * 4 + (rem & 3)] = s;
-    }
-  }
-  if (!arrived) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(xin);
-  }
-}
-
-// ---- per-row compute: one warp per row, lane = work unit ------------------------------------------
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-  return v;
-}
-
-// Activations of one lane's work unit held in registers for the whole kernel.  Used when a
-// single token is streamed and a row fits in one warp pass (U <= 32: Q8_0 K <= 1024, Q4_K K <= 4096):
-// the lane then owns the same unit in every row, so its activation chunks never change.
-struct XRegs {
-  int4 q[8];        // Q8_K: the unit's 8 chunks; Q8_0: q[0..1]
-  uint32_t sl, sh;  // Q8_K: 32-element sums S_j of the unit's 4 sub-blocks as 7-bit digits, S = 128*sh + sl
-  float d;          // activation scale of the unit's block
-};
-
-__device__ __forceinline__ void load_xregs(Fmt f, const RowStreamArgs& a, const uint8_t* act, int lane, XRegs& xr) {
-  const int U = units_per_row(f, a.K);
-  xr.sl = xr.sh = 0u;
-  xr.d = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) xr.q[j] = make_int4(0, 0, 0, 0);
-  if (lane >= U) return;
-  const int4* xq = reinterpret_cast<const int4*>(act);
-  if (f == Fmt::Q8_0xQ8_0) {
-    xr.q[0] = xq[lane];
-    xr.q[1] = xq[U + lane];
-    xr.d = reinterpret_cast<const float*>(act + U * 32)[lane];
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) xr.q[j] = xq[j * U + lane];
-    const int4 b = reinterpret_cast<const int4*>(act + U * 128)[lane];  // |S_j| <= 32 * 127
-    xr.sl = pack4_i8(b.x & 127, b.y & 127, b.z & 127, b.w & 127);
-    xr.sh = pack4_i8(b.x >> 7, b.y >> 7, b.z >> 7, b.w >> 7);
-    xr.d = reinterpret_cast<const float*>(act + U * 128 + U * 16)[lane >> 1];
-  }
-}
-
-// Q8_0 weight row x Q8_0 activations.  Blocks are 34 B, so inside the stage they are only
-// 2-byte aligned: read the 9 covering words and realign.
-template <RowOut MODE, int MTOK, bool XREG>
-__device__ __forceinline__ void row_q8_0(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
-                                         long long row, float (&acc)[MTOK], int lane, const XRegs& xr) {
-  const int U = a.K / QK8_0;
-  const int4* xq = reinterpret_cast<const int4*>(act);
-  const float* xd = reinterpret_cast<const float*>(act + a.m * U * 32);
-  for (int b = lane; b < U; b += 32) {
-    const uint8_t* p = rowp + b * Q8_0_BYTES;
-    const bool odd = (reinterpret_cast<uintptr_t>(p) & 2u) != 0;  // rows and blocks have even sizes
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(p - (odd ? 2 : 0));
-    uint32_t wv[9];
-#pragma unroll
-    for (int i = 0; i < 9; ++i) wv[i] = w[i];
-    const uint32_t dbits = odd ? (wv[0] >> 16) : (wv[0] & 0xFFFFu);
-    int q[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) q[i] = static_cast<int>(odd ? wv[i + 1] : __funnelshift_r(wv[i], wv[i + 1], 16));
-    const float dw = fp16_bits_to_float(dbits);
-#pragma unroll
-    for (int t = 0; t < MTOK; ++t) {
-      if (MTOK == 1 || t < a.m) {
-        const int4 x0 = XREG ? xr.q[0] : xq[(t * 2) * U + b], x1 = XREG ? xr.q[1] : xq[(t * 2 + 1) * U + b];
-        int ip = dp4a(q[0], x0.x, 0);
-        ip = dp4a(q[1], x0.y, ip);
-        ip = dp4a(q[2], x0.z, ip);
-        ip = dp4a(q[3], x0.w, ip);
-        ip = dp4a(q[4], x1.x, ip);
-        ip = dp4a(q[5], x1.y, ip);
-        ip = dp4a(q[6], x1.z, ip);
-        ip = dp4a(q[7], x1.w, ip);
-        if constexpr (MODE == RowOut::Partials) {
-          a.partials[(static_cast<size_t>(t) * a.n_rows + row) * U + b] = ip;
-        } else {
-          acc[t] += (dw * (XREG ? xr.d : xd[t * U + b])) * static_cast<float>(ip);  // gguf_dot_q8.c:475-476
-        }
-      }
-    }
-  }
-}
-
-// Load half h of super-block sb of a Q4_K row: header (d, dmin, scales) and 64 quant bytes.
-__device__ __forceinline__ void q4k_load_half(const uint8_t* rowp, int sb, int h, uint4& hdr, uint32_t (&qw)[16]) {
-  const uint8_t* blk = rowp + sb * Q4_K_BYTES;
-  hdr = *reinterpret_cast<const uint4*>(blk);
-  const uint4* qp = reinterpret_cast<const uint4*>(blk + 16 + 64 * h);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint4 v = qp[i];
-    qw[4 * i + 0] = v.x;
-    qw[4 * i + 1] = v.y;
-    qw[4 * i + 2] = v.z;
-    qw[4 * i + 3] = v.w;
-  }
-}
-
-// Q4_K weight row x Q8_K activations.  A lane takes half a super-block u = 2*sb + h (4
-// sub-blocks, 64 quant bytes); the halves of one super-block sit in adjacent lanes and are
-// combined in int32 before the float step, so every per-block (sumi, summ) equals the
-// reference's int32 values.  High nibbles are used in place (byte & 0xF0 = 16*q) with an
-// unsigned-by-signed dp4a and the exact sum is shifted down by 4 afterwards.
-// Per-lane constants of the one-unit-per-lane Q4_K row (U == 32, activations in registers):
-// where the lane's half super-block sits in a row, and masks that select the 6-bit scale/min
-// layout of its half (get_scale_min_k4, gguf_quant.c:212-220) without a branch.
-struct Q4kLane {
-  int hdr_off, q_off;         // byte offsets of the super-block header and of the half's 64 quant bytes
-  uint32_t m_lo, m_s2, m_hi;  // h = 0: (0x3F.., 0, 0); h = 1: (0, 0x0F.., 0x30..)
-};
-
-__device__ __forceinline__ Q4kLane q4k_lane(int lane) {
-  const int sb = lane >> 1, h = lane & 1;
-  Q4kLane c;
-  c.hdr_off = sb * Q4_K_BYTES;
-  c.q_off = sb * Q4_K_BYTES + 16 + 64 * h;
-  c.m_lo = h ? 0u : 0x3F3F3F3Fu;
-  c.m_s2 = h ? 0x0F0F0F0Fu : 0u;
-  c.m_hi = h ? 0x30303030u : 0u;
-  return c;
-}
-
-// One Q4_K row of K = 4096 (32 half super-blocks) against one token whose Q8_K activations are
-// held in registers.  Each lane adds its own half super-block to acc:
-//   acc += (d_x d_w) * sumi_half - (d_x dmin_w) * summ_half
-// with sumi_half (|.| <= 945*127*128 < 2^24) and summ_half exact in int32 and in fp32; the
-// reference adds the two halves in int32 first (gguf_dot_q8.c:711-759), which differs only in
-// the fp32 rounding of the final sum.
-__device__ __forceinline__ void row_q4k_full(const uint8_t* rowp, float& acc, const XRegs& xr, const Q4kLane& c) {
-  const uint4 hdr = *reinterpret_cast<const uint4*>(rowp + c.hdr_off);
-  const uint4* qp = reinterpret_cast<const uint4*>(rowp + c.q_off);
-  const uint4 w0 = qp[0], w1 = qp[1], w2 = qp[2], w3 = qp[3];
-  const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
-  const uint32_t sc4 = (s0 & c.m_lo) | (s2 & c.m_s2) | ((s0 >> 2) & c.m_hi);
-  const uint32_t mn4 = (s1 & c.m_lo) | ((s2 >> 4) & c.m_s2) | ((s1 >> 2) & c.m_hi);
-  // Sub-block 2g: low nibbles of group g's 32 bytes against chunks 4g, 4g+1; sub-block 2g+1: high
-  // nibbles (16*q in place, unsigned x signed dp4a) against chunks 4g+2, 4g+3.
-  const uint32_t g0[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-  const uint32_t g1[8] = {w2.x, w2.y, w2.z, w2.w, w3.x, w3.y, w3.z, w3.w};
-  const int xw[8][4] = {{xr.q[0].x, xr.q[0].y, xr.q[0].z, xr.q[0].w}, {xr.q[1].x, xr.q[1].y, xr.q[1].z, xr.q[1].w},
-                        {xr.q[2].x, xr.q[2].y, xr.q[2].z, xr.q[2].w}, {xr.q[3].x, xr.q[3].y, xr.q[3].z, xr.q[3].w},
-                        {xr.q[4].x, xr.q[4].y, xr.q[4].z, xr.q[4].w}, {xr.q[5].x, xr.q[5].y, xr.q[5].z, xr.q[5].w},
-                        {xr.q[6].x, xr.q[6].y, xr.q[6].z, xr.q[6].w}, {xr.q[7].x, xr.q[7].y, xr.q[7].z, xr.q[7].w}};
-  int ip0 = 0, ip1 = 0, ip2 = 0, ip3 = 0;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int c4 = k >> 2, wi = k & 3;
-    ip0 = dp4a(static_cast<int>(g0[k] & 0x0F0F0F0Fu), xw[c4][wi], ip0);
-    ip1 = dp4a_us(g0[k] & 0xF0F0F0F0u, xw[2 + c4][wi], ip1);
-    ip2 = dp4a(static_cast<int>(g1[k] & 0x0F0F0F0Fu), xw[4 + c4][wi], ip2);
-    ip3 = dp4a_us(g1[k] & 0xF0F0F0F0u, xw[6 + c4][wi], ip3);
-  }
-  // ip1, ip3 are 16x their sub-block sums; their scaled sum stays exact below 2^31 before the shift.
-  const int sumi = static_cast<int>(sc4 & 0xFFu) * ip0 + static_cast<int>((sc4 >> 16) & 0xFFu) * ip2 +
-                   ((static_cast<int>((sc4 >> 8) & 0xFFu) * ip1 + static_cast<int>(sc4 >> 24) * ip3) >> 4);
-  const int summ = dp4a_us(mn4, xr.sl, dp4a_us(mn4, xr.sh, 0) * 128);
-  const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
-  acc += (xr.d * dw) * static_cast<float>(sumi) - (xr.d * dmw) * static_cast<float>(summ);
-}
-
-template <RowOut MODE, int MTOK, bool XREG, bool FULL = false>
-__device__ __forceinline__ void row_q4k_q8k(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
-                                            long long row, float (&acc)[MTOK], int lane, const XRegs& xr) {
-  static_assert(!FULL || XREG, "FULL: one unit per lane, activations in registers");
-  const int U = a.K / 128, nb = U / 2;
-  const int4* xq = reinterpret_cast<const int4*>(act);
-  const int4* xb = reinterpret_cast<const int4*>(act + a.m * U * 128);
-  const float* xd = reinterpret_cast<const float*>(act + a.m * U * 128 + a.m * U * 16);
-  for (int u0 = 0; u0 < U; u0 += 32) {
-    const int u = u0 + lane;
-    const bool live = FULL || u < U;
-    const int sb = u >> 1, h = u & 1;
-    uint4 hdr;
-    uint32_t qw[16];
-    if (FULL) {
-      q4k_load_half(rowp, sb, h, hdr, qw);
-    } else {
-      hdr = make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) qw[i] = 0;
-      if (live) q4k_load_half(rowp, sb, h, hdr, qw);
-    }
-    uint32_t sc4, mn4;
-    q4k_scales_half(hdr.y, hdr.z, hdr.w, h, sc4, mn4);
-    const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
-#pragma unroll
-    for (int t = 0; t < MTOK; ++t) {
-      if (MTOK == 1 || t < a.m) {  // warp-uniform
-        int sumi = 0, summ = 0;
-        if (live) {
-          int ip[4] = {0, 0, 0, 0};
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {  // chunk j: group g = j/4; j%4 < 2 low nibbles, else high
-            const int4 x = XREG ? xr.q[j] : xq[(t * 8 + j) * U + u];
-            const int g = j >> 2, c = j & 1;
-            const uint32_t* w = qw + 8 * g + 4 * c;
-            if ((j & 2) == 0) {
-              ip[2 * g] = dp4a(static_cast<int>(w[0] & 0x0F0F0F0Fu), x.x, ip[2 * g]);
-              ip[2 * g] = dp4a(static_cast<int>(w[1] & 0x0F0F0F0Fu), x.y, ip[2 * g]);
-              ip[2 * g] = dp4a(static_cast<int>(w[2] & 0x0F0F0F0Fu), x.z, ip[2 * g]);
-              ip[2 * g] = dp4a(static_cast<int>(w[3] & 0x0F0F0F0Fu), x.w, ip[2 * g]);
-            } else {
-              ip[2 * g + 1] = dp4a_us(w[0] & 0xF0F0F0F0u, x.x, ip[2 * g + 1]);
-              ip[2 * g + 1] = dp4a_us(w[1] & 0xF0F0F0F0u, x.y, ip[2 * g + 1]);
-              ip[2 * g + 1] = dp4a_us(w[2] & 0xF0F0F0F0u, x.z, ip[2 * g + 1]);
-              ip[2 * g + 1] = dp4a_us(w[3] & 0xF0F0F0F0u, x.w, ip[2 * g + 1]);
-            }
-          }
-          ip[1] >>= 4;  // exact: the sums of 16*q*x are multiples of 16
-          ip[3] >>= 4;
-          sumi = static_cast<int>(sc4 & 0xFFu) * ip[0] + static_cast<int>((sc4 >> 8) & 0xFFu) * ip[1] +
-                 static_cast<int>((sc4 >> 16) & 0xFFu) * ip[2] + static_cast<int>(sc4 >> 24) * ip[3];
-          if constexpr (XREG) {  // sum_j m_j * (128*Sh_j + Sl_j), exact (m_j <= 63, Sl_j <= 127)
-            summ = dp4a_us(mn4, xr.sl, dp4a_us(mn4, xr.sh, 0) * 128);
-          } else {
-            const int4 bs = xb[t * U + u];
-            summ = static_cast<int>(mn4 & 0xFFu) * bs.x + static_cast<int>((mn4 >> 8) & 0xFFu) * bs.y +
-                   static_cast<int>((mn4 >> 16) & 0xFFu) * bs.z + static_cast<int>(mn4 >> 24) * bs.w;
-          }
-        }
-        sumi += __shfl_xor_sync(0xFFFFFFFFu, sumi, 1);
-        summ += __shfl_xor_sync(0xFFFFFFFFu, summ, 1);
-        if (live && h == 0) {
-          if constexpr (MODE == RowOut::Partials) {
-            int32_t* pp = a.partials + ((static_cast<size_t>(t) * a.n_rows + row) * nb + sb) * 2;
-            pp[0] = sumi;
-            pp[1] = summ;
-          } else {
-            // gguf_dot_q8.c:619-620, :640, :661: d = d_x*d_w and dmin = -d_x*dmin_w per super-block.
-            const float dx = XREG ? xr.d : xd[t * nb + sb];
-            acc[t] += (dx * dw) * static_cast<float>(sumi) - (dx * dmw) * static_cast<float>(summ);
-          }
-        }
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ float nib_f(uint32_t masked, int k) {
-  // byte k of a word whose bytes are 0..15, as an exact float: (2^23 + v) - 2^23.
-  return __uint_as_float(__byte_perm(masked, 0x4B000000u, 0x7440u | static_cast<uint32_t>(k))) - 8388608.0f;
-}
-
-// Q4_K weight row x fp32 activations (the reference's logits path for non-Q8_0 weights).
-template <RowOut MODE, int MTOK>
-__device__ __forceinline__ void row_q4k_f32(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp,
-                                            float (&acc)[MTOK], int lane) {
-  const int U = a.K / 128;
-  const float4* xf = reinterpret_cast<const float4*>(act);
-  const float4* xs = reinterpret_cast<const float4*>(act + a.m * U * 512);
-  for (int u0 = 0; u0 < U; u0 += 32) {
-    const int u = u0 + lane;
-    if (u >= U) break;
-    const int sb = u >> 1, h = u & 1;
-    uint4 hdr;
-    uint32_t qw[16];
-    q4k_load_half(rowp, sb, h, hdr, qw);
-    uint32_t sc4, mn4;
-    q4k_scales_half(hdr.y, hdr.z, hdr.w, h, sc4, mn4);
-    const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
-#pragma unroll
-    for (int t = 0; t < MTOK; ++t) {
-      if (MTOK == 1 || t < a.m) {
-        const float4 sx = xs[t * U + u];
-        const float sxs[4] = {sx.x, sx.y, sx.z, sx.w};
-        float c = 0.0f;
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {  // sub-block 4h+s: group s>>1, nibble half (s&1)
-          float qx = 0.0f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint32_t mw = (qw[8 * (s >> 1) + i] >> (4 * (s & 1))) & 0x0F0F0F0Fu;
-            const float4 x4 = xf[(t * 32 + 8 * s + i) * U + u];
-            qx = fmaf(nib_f(mw, 0), x4.x, qx);
-            qx = fmaf(nib_f(mw, 1), x4.y, qx);
-            qx = fmaf(nib_f(mw, 2), x4.z, qx);
-            qx = fmaf(nib_f(mw, 3), x4.w, qx);
-          }
-          const float d1 = dw * static_cast<float>((sc4 >> (8 * s)) & 0xFFu);
-          const float m1 = dmw * static_cast<float>((mn4 >> (8 * s)) & 0xFFu);
-          c += d1 * qx - m1 * sxs[s];  // gguf_quant.c:744/746
-        }
-        acc[t] += c;
-      }
-    }
-  }
-}
-
-// ---- the kernel ---------------------------------------------------------------------------------
-
-// Tile -> (segment, first row, rows, weight base, output, bias, output stride).
-struct TileRef {
-  const uint8_t* w;
-  const float* bias;
-  float* out;
-  long long stride;
-  long long r0;
-  int nr;
-};
-
-// What consumers need of a stage's tile, written by the producer before it arms the stage's
-// barrier (the barrier's release/acquire orders it), so consumer warps need not re-derive it.
-struct __align__(16) TileDesc {
-  float* out;
-  const float* bias;
-  int r0;        // first row of the tile within its tensor
-  int nr;        // rows in the tile
-  int stride;    // output row stride (elements)
-  int misalign;  // start of the tile's first row inside the stage (the copy starts 16-byte aligned)
-};
-static_assert(sizeof(TileDesc) == 32, "two 16-byte words");
-
-__device__ __forceinline__ TileRef tile_ref(const RowStreamArgs& a, const Layout& L, long long tile) {
-  int s = 0;
-#pragma unroll
-  for (int i = 1; i < MAX_SEGS; ++i)
-    if (i < a.n_seg && tile >= a.seg[i].tile0) s = i;
-  const RowSeg& g = a.seg[s];
-  TileRef t;
-  t.w = g.w;
-  t.bias = g.bias;
-  t.out = g.out;
-  t.stride = a.n_seg > 1 ? g.n_rows : a.out_stride;
-  t.r0 = (tile - g.tile0) * L.tile_rows;
-  t.nr = static_cast<int>(min(static_cast<long long>(L.tile_rows), g.n_rows - t.r0));
-  return t;
-}
-
-// ---- tensor-parallel all-reduce over peer memory -------------------------------------------------
-// Each partial output travels with its own flag: the consumer lane that computes output (t, row)
-// writes the 64-bit word (float bits, tag = epoch + 1) to entry [parity][rank][t*n + row] of every
-// rank's exchange region (CUDA IPC mappings over NVLink). Up to TP_DIRECT_WORLD ranks the lane
-// stores to every peer as soon as it has the value (the stores overlap the remaining tiles); with
-// more ranks the one-word-per-output NVLink writes cost more than they overlap (measured: 4096
-// outputs x 7 peers added ~4 us per launch), so the lane writes only the local entry and after its
-// last tile the CTA copies its entries to every peer with coalesced stores. An aligned 64-bit store
-// is single-copy atomic, so a reader that sees the current tag also sees that store's value -- no
-// fences, no separate flag. Each CTA then polls (bounded) the entries of its own rows in the local
-// region until every rank's tag is current and sums them in rank order, so every rank gets the same
-// bits. The row-to-CTA map is the same on every rank. Parity: a rank writes parity p again only in
-// launch e + 2, which starts after its launch e + 1 read every peer's entries of e + 1, which the
-// peers wrote only after finishing their launch e (and its reads).
-__device__ __forceinline__ void st_relaxed_sys_u64(void* p, unsigned long long v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const void* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ void tp_finalize(const RowStreamArgs& a, const Layout& L, uint32_t e, int ct) {
-  const uint8_t* local = a.tp.peer[a.tp.rank];
-  uint32_t* counter = reinterpret_cast<uint32_t*>(a.tp.peer[a.tp.rank] + TP_CTRL_OFF);
-  const uint32_t f = e + 1u;
-  const int n = static_cast<int>(a.seg[0].n_rows);
-  const unsigned long long* slots =
-      reinterpret_cast<const unsigned long long*>(local + static_cast<size_t>(e & 1u) * TP_MAX_WORLD * TP_SLOT_BYTES);
-  const size_t per_rank = TP_SLOT_BYTES / 8;
-  // Push (more than TP_DIRECT_WORLD ranks): this CTA's own entries, written by its consumer warps
-  // before the barrier, go to every peer as warp-wide stores of consecutive rows -- a few large
-  // NVLink writes instead of one 8-byte write per output and peer.
-  const size_t own = static_cast<size_t>(a.tp.rank) * per_rank;
-  if (a.tp.world > TP_DIRECT_WORLD) named_bar_sync(2, CONSUMERS);
-  for (long long tile = a.tp.world > TP_DIRECT_WORLD ? blockIdx.x : L.n_tiles; tile < L.n_tiles; tile += gridDim.x) {
-    const TileRef tr = tile_ref(a, L, tile);
-    const int cnt = tr.nr * a.m;
-    for (int i = ct; i < cnt; i += CONSUMERS) {
-      const int t = i / tr.nr, row = static_cast<int>(tr.r0) + (i - t * tr.nr);
-      const size_t idx = static_cast<size_t>(t) * n + row;
-      const unsigned long long v = slots[own + idx];  // written by this CTA before the barrier
-      const size_t off = reinterpret_cast<const uint8_t*>(slots + own + idx) - local;
-      for (int r = 0; r < a.tp.world; ++r)
-        if (r != a.tp.rank) st_relaxed_sys_u64(a.tp.peer[r] + off, v);
-    }
-  }
-  const unsigned long long t0 = global_ns();
-  bool ok = true;
-  for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
-    const TileRef tr = tile_ref(a, L, tile);
-    const int cnt = tr.nr * a.m;
-    for (int i = ct; i < cnt; i += CONSUMERS) {
-      const int t = i / tr.nr, row = static_cast<int>(tr.r0) + (i - t * tr.nr);
-      const size_t idx = static_cast<size_t>(t) * n + row;
-      // All ranks' entries in flight at once (one L2 round trip when they have arrived), then
-      // re-poll only the stale ones.
-      unsigned long long v[TP_MAX_WORLD];
-#pragma unroll
-      for (int r = 0; r < TP_MAX_WORLD; ++r)
-        if (r < a.tp.world) v[r] = ld_relaxed_sys_u64(slots + r * per_rank + idx);
-      float sum = 0.0f;
-#pragma unroll
-      for (int r = 0; r < TP_MAX_WORLD; ++r) {  // rank order: the same additions on every rank
-        if (r >= a.tp.world) break;
-        for (uint32_t k = 0; ok && static_cast<uint32_t>(v[r] >> 32) != f; ++k) {
-          if ((k & 63u) == 63u && global_ns() - t0 > WAIT_LIMIT_NS) ok = false;
-          v[r] = ld_relaxed_sys_u64(slots + r * per_rank + idx);
-        }
-        sum += __uint_as_float(static_cast<uint32_t>(v[r]));
-      }
-      a.seg[0].out[static_cast<size_t>(t) * a.out_stride + row] = sum;
-    }
-  }
-  if (!ok) atomicOr(a.status, ST_TIMEOUT_PEER);
-  // Advance the epoch once every CTA of this launch is done with it (it read it at its start).
-  named_bar_sync(2, CONSUMERS);
-  if (ct == 0) {
-    __threadfence();
-    if (atomicAdd(counter, 1u) == gridDim.x - 1) {
-      counter[0] = 0u;
-      counter[1] = e + 1u;  // the next launch reads it after its griddepcontrol.wait
-    }
-  }
-}
-
-template <Fmt F, RowOut MODE, int MTOK, bool XREG>
-__global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamArgs a, const Layout L) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + MAX_STAGES;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 2 * MAX_STAGES * 8);
-  uint64_t* xin = reinterpret_cast<uint64_t*>(smem + 2 * MAX_STAGES * 8 + 8);
-  TileDesc* descs = reinterpret_cast<TileDesc*>(smem + 256);
-  static_assert(256 + MAX_STAGES * sizeof(TileDesc) <= BAR_BYTES, "tile descriptors fit the header");
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int S = L.n_stages;
-
-  // Tile slot r belongs to consumer warp (it*R + r) % CONSUMER_WARPS.  Every consumer warp waits
-  // for every tile and releases it, owner or not: a warp that skipped tiles could otherwise reach
-  // a stage's fill k before fill k - 1 completed, when the parity wait for k returns at once.
-  const int R = L.tile_rows;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], CONSUMER_WARPS);
-    }
-    mbar_init(xin, CONSUMER_WARPS);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  __syncthreads();
-  // Dependent launches may start their weight prefetch as soon as every CTA of this grid runs;
-  // they wait (griddepcontrol.wait) for this grid to finish before touching its outputs.
-  griddep_launch_dependents();
-
-  if (warp == 0) {
-    if (lane != 0) return;
-    // ---------------- producer (weights only: never waits on the previous grid) ----------------
-    const uint64_t pol = l2_evict_first_policy();
-    long long it = 0;
-    int s = 0;
-    uint32_t ephase = 1;  // iteration it >= S waits for completion (it/S - 1) of empty[s]: parity (it/S - 1) & 1
-    for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x, ++it) {
-      if (it == PRE_STAGES) hold_for_activations(xin);
-      if (it >= S) {
-        if (!wait_or_abort(&empty[s], ephase, abort_flag)) {
-          atomicOr(a.status, ST_TIMEOUT_EMPTY);
-          *abort_flag = 1;
-          break;
-        }
-      }
-      const TileRef tr = tile_ref(a, L, tile);
-      const uintptr_t start = reinterpret_cast<uintptr_t>(tr.w) + static_cast<uintptr_t>(tr.r0) * a.row_bytes;
-      const uintptr_t al = start & ~static_cast<uintptr_t>(15);
-      const uint32_t bytes = static_cast<uint32_t>((start - al + static_cast<long long>(tr.nr) * a.row_bytes + 15) & ~15ull);
-      TileDesc& td = descs[s];
-      td.out = tr.out;
-      td.bias = tr.bias;
-      td.r0 = static_cast<int>(tr.r0);
-      td.nr = tr.nr;
-      td.stride = static_cast<int>(tr.stride);
-      td.misalign = static_cast<int>(start - al);
-      mbar_arrive_expect_tx(&full[s], bytes);
-      bulk_g2s(smem + L.stage_off + s * L.stage_bytes, reinterpret_cast<const void*>(al), bytes, &full[s], pol);
-      if (++s == S) {
-        s = 0;
-        ephase ^= 1u;
-      }
-    }
-    // Drain: the last copies issued into each stage must land before the CTA may exit.
-    for (long long j = (it > S ? it - S : 0); j < it; ++j) {
-      if (!mbar_wait(&full[j % S], static_cast<uint32_t>((j / S) & 1))) atomicOr(a.status, ST_TIMEOUT_DRAIN);
-    }
-    return;
-  }
-
-  // ---------------- consumers ----------------
-  const int cw = warp - 1;
-  uint8_t* act = smem + L.act_off;
-  griddep_wait();  // the activations may be the previous grid's output
-  constexpr bool TP = MODE == RowOut::StoreTp;
-  const uint32_t tp_e = TP ? *reinterpret_cast<volatile const uint32_t*>(a.tp.peer[a.tp.rank] + TP_CTRL_OFF + 4) : 0u;
-  const size_t tp_slot =
-      TP ? (static_cast<size_t>(tp_e & 1u) * TP_MAX_WORLD + a.tp.rank) * TP_SLOT_BYTES : 0;  // [parity][rank]
-  load_act(a, act, threadIdx.x - 32, xin);
-  named_bar_sync(1, CONSUMERS);
-
-  XRegs xr;
-  if constexpr (XREG) load_xregs(F, a, act, lane, xr);
-  const bool full_warp = units_per_row(F, a.K) == 32;  // every lane has a unit (XREG rows)
-  const Q4kLane q4l = q4k_lane(lane);
-
-  unsigned long long best = 0ull;
-  bool dead = false;
-  int s = 0;
-  uint32_t fphase = 0;
-  const int step = R % CONSUMER_WARPS;
-  int first = cw;  // first slot of this warp in the current tile: (cw - it*R) mod CONSUMER_WARPS
-  for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
-    {
-      if (!dead && !wait_or_abort(&full[s], fphase, abort_flag)) {
-        atomicOr(a.status, ST_TIMEOUT_FULL);
-        *abort_flag = 1;
-        dead = true;
-      }
-      if (!dead && first < R) {  // this warp owns at least one slot of the tile
-        const TileDesc tr = descs[s];
-        const long long r0 = tr.r0;
-        const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + tr.misalign;
-        for (int r = first; r < tr.nr; r += CONSUMER_WARPS) {
-          float acc[MTOK];
-#pragma unroll
-          for (int t = 0; t < MTOK; ++t) acc[t] = 0.0f;
-          const uint8_t* rowp = tb + static_cast<size_t>(r) * a.row_bytes;
-          if constexpr (F == Fmt::Q8_0xQ8_0) {
-            row_q8_0<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
-          } else if constexpr (F == Fmt::Q4_KxQ8_K) {
-            if constexpr (XREG && MTOK == 1 && MODE != RowOut::Partials) {
-              if (full_warp) {
-                row_q4k_full(rowp, acc[0], xr, q4l);
-              } else {
-                row_q4k_q8k<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
-              }
-            } else if (XREG && full_warp) {
-              row_q4k_q8k<MODE, MTOK, XREG, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
-            } else {
-              row_q4k_q8k<MODE, MTOK, XREG>(a, act, rowp, r0 + r, acc, lane, xr);
-            }
-          } else {
-            row_q4k_f32<MODE, MTOK>(a, act, rowp, acc, lane);
-          }
-          if constexpr (MODE != RowOut::Partials) {
-            const long long row = r0 + r;
-            float mine = 0.0f;
-#pragma unroll
-            for (int t = 0; t < MTOK; ++t) {
-              if (MTOK == 1 || t < a.m) {
-                const float v = warp_sum(acc[t]);
-                if (lane == t) mine = v;
-              }
-            }
-            if (lane < a.m) {
-              const float y = (tr.bias != nullptr ? tr.bias[row] : 0.0f) + mine;  // cpu_kernel.c:596-597
-              if constexpr (TP) {  // (partial, tag) into entry [parity][rank][t*n + row]: every rank's, or ours
-                const size_t off = tp_slot + (static_cast<size_t>(lane) * a.seg[0].n_rows + row) * 8;
-                const unsigned long long v = (static_cast<unsigned long long>(tp_e + 1u) << 32) | __float_as_uint(y);
-                if (a.tp.world <= TP_DIRECT_WORLD) {
-                  for (int r = 0; r < a.tp.world; ++r) st_relaxed_sys_u64(a.tp.peer[r] + off, v);
-                } else {  // tp_finalize pushes it
-                  *reinterpret_cast<unsigned long long*>(a.tp.peer[a.tp.rank] + off) = v;
-                }
-              } else if constexpr (MODE == RowOut::Store) {
-                tr.out[static_cast<size_t>(lane) * tr.stride + row] = y;  // stride: int, outputs < 2^31
-              } else {
-                const unsigned long long k = argmax_key(y, static_cast<uint32_t>(a.row0 + row));
-                best = k > best ? k : best;
-              }
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    first -= step;
-    if (first < 0) first += CONSUMER_WARPS;
-    if (++s == S) {
-      s = 0;
-      fphase ^= 1u;
-    }
-  }
-  if constexpr (TP) tp_finalize(a, L, tp_e, threadIdx.x - 32);
-  if constexpr (MODE == RowOut::Argmax) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-      best = other > best ? other : best;
-    }
-    if (lane == 0 && best != 0ull) atomicMax(a.key, best);
-  }
-}
-
-template <Fmt F, RowOut MODE, int MTOK, bool XREG = false>
-cudaError_t launch_impl(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
-  static int configured_smem = 0;  // per instantiation; the host API serialises its callers
-  auto kern = rowstream_kernel<F, MODE, MTOK, XREG>;
-  if (L.smem_total > configured_smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_total);
-    if (e != cudaSuccess) return e;
-    configured_smem = L.smem_total;
-  }
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = L.smem_total;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a, L);
-}
-
-template <Fmt F, RowOut MODE>
-cudaError_t launch_mtok(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
-  if constexpr (F != Fmt::Q4_KxF32) {
-    if (a.m == 1 && units_per_row(F, a.K) <= 32) return launch_impl<F, MODE, 1, true>(a, L, grid, st);
-  }
-  if (a.m <= 1) return launch_impl<F, MODE, 1>(a, L, grid, st);
-  if (a.m <= 2) return launch_impl<F, MODE, 2>(a, L, grid, st);
-  if (a.m <= 4) return launch_impl<F, MODE, 4>(a, L, grid, st);
-  return launch_impl<F, MODE, 8>(a, L, grid, st);
-}
-
-}  // namespace
 
 int rowstream_max_m(Fmt fmt, int K, const DeviceInfo& dev) {
   (void)dev;
@@ -882,7 +12,7 @@ int rowstream_max_m(Fmt fmt, int K, const DeviceInfo& dev) {
   return m < MAX_M ? m : MAX_M;
 }
 
-bool rowstream_quantizes_itself(Fmt fmt, int m) { return fmt != Fmt::Q4_KxF32 && m <= PROLOGUE_QUANT_MAX_M; }
+bool rowstream_quantizes_itself(Fmt fmt, int m) { return act_of(fmt) != Act::F32 && m <= PROLOGUE_QUANT_MAX_M; }
 
 cudaError_t launch_rowstream(const RowStreamArgs& in, const DeviceInfo& dev, cudaStream_t st) {
   RowStreamArgs a = in;
@@ -894,10 +24,11 @@ cudaError_t launch_rowstream(const RowStreamArgs& in, const DeviceInfo& dev, cud
     a.n_rows = 0;
     for (int i = 0; i < a.n_seg; ++i) a.n_rows += a.seg[i].n_rows;
   }
-  if (a.mode == RowOut::StoreTp && (a.tp.world < 2 || a.tp.world > TP_MAX_WORLD || a.fmt == Fmt::Q4_KxF32))
+  if (a.mode == RowOut::StoreTp && (a.tp.world < 2 || a.tp.world > TP_MAX_WORLD ||
+                                    (a.fmt != Fmt::Q8_0xQ8_0 && a.fmt != Fmt::Q4_KxQ8_K)))
     return cudaErrorInvalidValue;
   if (a.n_rows <= 0 || a.m <= 0) return cudaSuccess;
-  if (a.m > MAX_M || a.K % (a.fmt == Fmt::Q8_0xQ8_0 ? QK8_0 : QK_K) != 0) return cudaErrorInvalidValue;
+  if (a.m > MAX_M || a.K % (act_of(a.fmt) == Act::Q8_0 ? QK8_0 : QK_K) != 0) return cudaErrorInvalidValue;
   Layout L{};
   L.stage_bytes = STAGE_TARGET;
   if (a.row_bytes + STAGE_SLACK > L.stage_bytes) L.stage_bytes = (a.row_bytes + STAGE_SLACK + 127) & ~127;
@@ -931,10 +62,12 @@ cudaError_t launch_rowstream(const RowStreamArgs& in, const DeviceInfo& dev, cud
       if (a.mode == RowOut::StoreTp) return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::StoreTp>(a, L, grid, st);
       if (a.mode == RowOut::Argmax) return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::Argmax>(a, L, grid, st);
       return launch_mtok<Fmt::Q4_KxQ8_K, RowOut::Partials>(a, L, grid, st);
-    default:
+    case Fmt::Q4_KxF32:
       if (a.mode == RowOut::Store) return launch_mtok<Fmt::Q4_KxF32, RowOut::Store>(a, L, grid, st);
       if (a.mode == RowOut::Argmax) return launch_mtok<Fmt::Q4_KxF32, RowOut::Argmax>(a, L, grid, st);
       return cudaErrorInvalidValue;
+    default:
+      return launch_rowstream_more(a, L, grid, st);
   }
 }
 

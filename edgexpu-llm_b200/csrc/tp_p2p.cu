@@ -114,7 +114,10 @@ int edgexpu_cuda_linear_quant_batch_tp_dev(float* out, const float* x, const uin
   if (out == nullptr || x == nullptr || weight == nullptr || m <= 0 || n_out <= 0 || n_in <= 0)
     return ex::api_fail(nullptr, 0, "linear_tp: invalid arguments");
   if (!ex::api_lookup(weight, type, n_out, n_in, nullptr, 0)) return 0;
-  const ex::Fmt fmt = type == ex::TYPE_Q8_0 ? ex::Fmt::Q8_0xQ8_0 : ex::Fmt::Q4_KxQ8_K;
+  if (type != ex::TYPE_Q8_0 && type != ex::TYPE_Q4_K)
+    return ex::api_fail(nullptr, 0, "linear_tp: the in-kernel all-reduce is built for Q8_0 and Q4_K weights, not type %u",
+                        type);
+  const ex::Fmt fmt = ex::fmt_q8(type);
   const int max_m = ex::rowstream_max_m(fmt, n_in, ex::api_device_info());
   if (max_m <= 0) return ex::api_fail(nullptr, 0, "linear_tp: n_in %d too large for the activation tile", n_in);
   const int slot_m = static_cast<int>(ex::TP_SLOT_BYTES / 8 / static_cast<size_t>(n_out));  // rows one slot holds
@@ -130,8 +133,7 @@ int edgexpu_cuda_linear_quant_batch_tp_dev(float* out, const float* x, const uin
   if (!fused) {  // quantize every row once (cpu_kernel.c:577-631), then stream
     void* xq = ex::api_act_scratch(static_cast<size_t>(m) * qb + 64, st, nullptr, 0);
     if (xq == nullptr) return 0;
-    const cudaError_t e = type == ex::TYPE_Q8_0 ? ex::launch_quantize_q8_0(x, m, n_in, static_cast<uint8_t*>(xq), st)
-                                                 : ex::launch_quantize_q8_k(x, m, n_in, static_cast<uint8_t*>(xq), st);
+    const cudaError_t e = ex::launch_quantize_for(type, x, m, n_in, static_cast<uint8_t*>(xq), st);
     if (e != cudaSuccess) return ex::api_fail(nullptr, 0, "linear_tp: %s", cudaGetErrorString(e));
     act = static_cast<const uint8_t*>(xq);
   }

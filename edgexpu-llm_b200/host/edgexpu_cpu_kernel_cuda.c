@@ -8,6 +8,8 @@
  *   edgexpu_gguf_quantize_q8_0/_k   src/gguf_dot_q8.c:269-412
  *   edgexpu_gguf_q8_0/_k_nbytes     src/gguf_dot_q8.c:255-267
  *   edgexpu_gguf_can_dot_q8(k)      src/gguf_dot_q8.c:414-434
+ *   edgexpu_gguf_dot_quant_q8(k)    src/gguf_dot_q8.c:1004-1044
+ *   edgexpu_gguf_dot_quant          src/gguf_quant.c:894-918
  */
 #include "../../include/edgexpu_b200_host.h"
 
@@ -17,6 +19,8 @@
 
 #include "../../include/edgexpu_cuda.h"
 
+#define GGUF_TYPE_F32 0u
+#define GGUF_TYPE_F16 1u
 #define GGUF_TYPE_Q4_0 2u
 #define GGUF_TYPE_Q5_0 6u
 #define GGUF_TYPE_Q8_0 8u
@@ -86,6 +90,53 @@ int edgexpu_gguf_can_dot_q8(uint32_t type) {
 
 int edgexpu_gguf_can_dot_q8k(uint32_t type) {
     return type == GGUF_TYPE_Q4_K || type == GGUF_TYPE_Q5_K || type == GGUF_TYPE_Q6_K;
+}
+
+/* One row through the GPU; NaN and the sticky message if the device call fails. */
+static float dot_row(const char *what, uint32_t type, const uint8_t *wrow, const void *x, int quantized, int n) {
+    char err[256];
+    float r = 0.0f;
+    if (!edgexpu_cuda_dot_quant(type, wrow, x, quantized, n, &r, err, sizeof err)) {
+        record(what, err);
+        return NAN;
+    }
+    return r;
+}
+
+float edgexpu_gguf_dot_quant_q8(uint32_t type, const uint8_t *wrow, const uint8_t *x_q8, int n) {
+    if (wrow == NULL || x_q8 == NULL || n <= 0 || n % 32 != 0 || !edgexpu_gguf_can_dot_q8(type)) {
+        return 0.0f; /* gguf_dot_q8.c:1010-1022 */
+    }
+    return dot_row("edgexpu_gguf_dot_quant_q8", type, wrow, x_q8, 1, n);
+}
+
+float edgexpu_gguf_dot_quant_q8k(uint32_t type, const uint8_t *wrow, const uint8_t *x_q8k, int n) {
+    if (wrow == NULL || x_q8k == NULL || n <= 0 || n % 256 != 0 || !edgexpu_gguf_can_dot_q8k(type)) {
+        return 0.0f; /* gguf_dot_q8.c:1031-1043 */
+    }
+    return dot_row("edgexpu_gguf_dot_quant_q8k", type, wrow, x_q8k, 1, n);
+}
+
+float edgexpu_gguf_dot_quant(uint32_t type, const uint8_t *row, const float *x, int n) {
+    int block;
+    if (row == NULL || x == NULL || n <= 0) {
+        return 0.0f; /* gguf_quant.c:895-897 */
+    }
+    switch (type) {
+        case GGUF_TYPE_F32:
+        case GGUF_TYPE_F16: block = 1; break;
+        case GGUF_TYPE_Q4_0:
+        case GGUF_TYPE_Q5_0:
+        case GGUF_TYPE_Q8_0: block = 32; break;
+        case GGUF_TYPE_Q4_K:
+        case GGUF_TYPE_Q5_K:
+        case GGUF_TYPE_Q6_K: block = 256; break;
+        default: return 0.0f; /* gguf_quant.c:915-916 */
+    }
+    if (n % block != 0) {
+        return 0.0f; /* the per-type dots reject unaligned widths */
+    }
+    return dot_row("edgexpu_gguf_dot_quant", type, row, x, 0, n);
 }
 
 int edgexpu_gguf_quantize_q8_0(const float *x, int n, uint8_t *dst) {

@@ -15,12 +15,19 @@
  *   edgexpu_gguf_q8_k_nbytes        include/edgexpu/gguf_quant.h:85
  *   edgexpu_gguf_can_dot_q8         include/edgexpu/gguf_quant.h:82
  *   edgexpu_gguf_can_dot_q8k        include/edgexpu/gguf_quant.h:87
+ *   edgexpu_gguf_dot_quant_q8       include/edgexpu/gguf_quant.h:90-95
+ *   edgexpu_gguf_dot_quant_q8k      include/edgexpu/gguf_quant.h:97-102
+ *   edgexpu_gguf_dot_quant          include/edgexpu/gguf_quant.h:72-77
  *
  * Error behaviour follows the reference: the void linear entry points return silently on
  * NULL / non-positive arguments (cpu_kernel.c:562-564).  A GPU-side failure (unregistered
  * weight, unsupported type, CUDA error) fills `out` with NaN -- so the finite-RMS check of
  * native.c:2232-2234 stops generation -- and records a sticky message readable through
- * edgexpu_b200_last_error().  The quantizers return 1/0 like the reference.
+ * edgexpu_b200_last_error().  The quantizers return 1/0 like the reference.  The single-row dots
+ * return 0.0f on bad arguments or an unsupported type, as the reference's dispatch does
+ * (gguf_dot_q8.c:1010-1022, :1031-1043; gguf_quant.c:895-917), and NaN plus the sticky message
+ * on a GPU-side failure.  Their weight row may be a row of an uploaded tensor (device handle) or
+ * host memory such as the reference's mmap'd tensor bytes.
  *
  * The shim adds three calls the reference has no counterpart for: init/shutdown of the device,
  * the sticky error, and the greedy logits call that replaces sample_next_token's chunk loop
@@ -47,6 +54,9 @@ int edgexpu_gguf_can_dot_q8(uint32_t type);
 size_t edgexpu_gguf_q8_k_nbytes(int n);
 int edgexpu_gguf_quantize_q8_k(const float *x, int n, uint8_t *dst);
 int edgexpu_gguf_can_dot_q8k(uint32_t type);
+float edgexpu_gguf_dot_quant_q8(uint32_t type, const uint8_t *wrow, const uint8_t *x_q8, int n);
+float edgexpu_gguf_dot_quant_q8k(uint32_t type, const uint8_t *wrow, const uint8_t *x_q8k, int n);
+float edgexpu_gguf_dot_quant(uint32_t type, const uint8_t *row, const float *x, int n);
 
 /* Binds the shim to a CUDA device; must run before the first linear call (edgexpu_native_load). */
 int edgexpu_b200_init(int device, char *error, size_t error_size);

@@ -19,6 +19,12 @@
  *                                     (chunk loop + logit_score src/native.c:500-514)
  *   edgexpu_cuda_upload_weight        per-token staging of load_qweight src/native.c:593-655,
  *                                     stage_copy_bytes src/native.c:350-380 (uploaded once instead)
+ *   edgexpu_cuda_dot_quant            edgexpu_gguf_dot_quant_q8 / _q8k  include/edgexpu/gguf_quant.h:90-102
+ *                                     and edgexpu_gguf_dot_quant        include/edgexpu/gguf_quant.h:72-77
+ *                                     (one row, host activations)
+ *   edgexpu_cuda_dequantize_row       edgexpu_gguf_dequantize_row       include/edgexpu/gguf_quant.h:50-58
+ *   edgexpu_cuda_dequantize_rows_dev  the token-embedding gather of embedding_row src/native.c:428-443
+ *                                     (a batch of rows, device buffers)
  *
  * Weight handles: edgexpu_cuda_upload_weight returns a device address (typed const uint8_t *)
  * that callers keep in edgexpu_qweight.data (include/edgexpu/native.h:23-28) in place of the
@@ -40,9 +46,18 @@ extern "C" {
 
 #define EDGEXPU_CUDA_ABI_VERSION 1
 
-/* GGUF type ids, as EDGEXPU_GGUF_TYPE_* in include/edgexpu/gguf_quant.h:140-147. */
+/* GGUF type ids, as EDGEXPU_GGUF_TYPE_* in include/edgexpu/gguf_quant.h:17-24.  The quantized
+ * matrix product accepts Q8_0, Q5_0 and Q4_0 weights (Q8_0 activations) and Q4_K, Q5_K and Q6_K
+ * weights (Q8_K activations), the pairs of edgexpu_gguf_can_dot_q8 / _q8k; F16 and F32 weights are
+ * dotted against the fp32 activations, as the reference's linear does for them. */
+#define EDGEXPU_CUDA_TYPE_F32 0u
+#define EDGEXPU_CUDA_TYPE_F16 1u
+#define EDGEXPU_CUDA_TYPE_Q4_0 2u
+#define EDGEXPU_CUDA_TYPE_Q5_0 6u
 #define EDGEXPU_CUDA_TYPE_Q8_0 8u
 #define EDGEXPU_CUDA_TYPE_Q4_K 12u
+#define EDGEXPU_CUDA_TYPE_Q5_K 13u
+#define EDGEXPU_CUDA_TYPE_Q6_K 14u
 
 int edgexpu_cuda_abi_version(void);
 
@@ -72,10 +87,11 @@ int edgexpu_cuda_quantize_q8_0(const float *x, int n, uint8_t *dst, char *error,
 int edgexpu_cuda_quantize_q8_k(const float *x, int n, uint8_t *dst, char *error, size_t error_size);
 
 /* out[t*n_out + o] = bias[o] + dot(W_o, quantize(x_t)) for t < m, o < n_out; x is [m][n_in]
- * row-major, out is [m][n_out]; bias may be NULL.  Q8_0 weights use Q8_0 activations, Q4_K
- * weights use Q8_K activations (cpu_kernel.c:577-631).  Batches of up to 63 rows stream the
- * weight once through the GEMV kernel; Q4_K batches of 64 rows and more (prefill) run as a
- * tensor-core GEMM (tcgen05 kind::i8) with the same integer partials. */
+ * row-major, out is [m][n_out]; bias may be NULL.  Q8_0/Q5_0/Q4_0 weights use Q8_0 activations,
+ * Q4_K/Q5_K/Q6_K weights use Q8_K activations (cpu_kernel.c:577-631), F16/F32 weights the fp32
+ * activations (:633-643).  The GEMV kernel streams the weight once per 8 activation rows; Q4_K
+ * batches of 64 rows and more (prefill) run as a tensor-core GEMM (tcgen05 kind::i8) with the
+ * same integer partials. */
 int edgexpu_cuda_linear_quant_batch(float *out, const float *x, const uint8_t *weight, uint32_t type,
                                     const float *bias, int m, int n_out, int n_in, char *error,
                                     size_t error_size);
@@ -87,7 +103,26 @@ int edgexpu_cuda_logits_argmax(const uint8_t *weight, uint32_t type, const float
                                const float *bias, uint32_t *token_id, float *best_score, char *error,
                                size_t error_size);
 
+/* One weight row against one activation row: *result = dot(wrow, x) over n elements.
+ * x_quantized = 1: x is a quantized activation row (Q8_0 blocks for Q8_0/Q5_0/Q4_0 weights, Q8_K
+ * blocks for Q4_K/Q5_K/Q6_K), as edgexpu_gguf_dot_quant_q8 / _q8k; x_quantized = 0: x is fp32, as
+ * edgexpu_gguf_dot_quant (any type above, F16/F32 included).  wrow is a row of a registered tensor
+ * or host memory (copied for the call). */
+int edgexpu_cuda_dot_quant(uint32_t type, const uint8_t *wrow, const void *x, int x_quantized, int n, float *result,
+                           char *error, size_t error_size);
+
+/* Row `row` of a registered tensor (handle = its first row) dequantized to n_in fp32 values in dst
+ * (host), bit-identical to the reference's dequantizer (gguf_quant.c:139-353). */
+int edgexpu_cuda_dequantize_row(const uint8_t *weight, uint32_t type, int64_t row, int n_in, float *dst, char *error,
+                                size_t error_size);
+
 /* ---- device-buffer entry points (ordered on `stream`, no host synchronisation) ----------- */
+
+/* out[i][0..n_in) = row ids[i] of the registered tensor `weight` (its handle) dequantized, for
+ * i < n_ids (ids: device int32; NULL = rows 0 .. n_ids-1).  An id outside the tensor gives a NaN
+ * row and an error from the next edgexpu_cuda_stream_sync. */
+int edgexpu_cuda_dequantize_rows_dev(float *out, const uint8_t *weight, uint32_t type, const int32_t *ids, int n_ids,
+                                     int n_in, void *stream);
 
 /* Quantize m rows of n fp32 values into the activation format used with `weight_type`. */
 int edgexpu_cuda_quantize_dev(uint32_t weight_type, const float *x, int m, int n, uint8_t *dst, void *stream);

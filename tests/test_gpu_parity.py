@@ -267,7 +267,7 @@ def test_error_paths(gpu):
         with pytest.raises(gpu.EdgexpuError, match="type"):
             gpu.linear_quant_batch(np.ones((1, 256), np.float32), h, TYPE_Q4_K, 4)
         with pytest.raises(gpu.EdgexpuError, match="unsupported"):
-            gpu.linear_quant_batch(np.ones((1, 64), np.float32), h, 6, 4)  # Q5_0: not on this path
+            gpu.linear_quant_batch(np.ones((1, 64), np.float32), h, 7, 4)  # GGUF type 7 (Q5_1): not on this path
     finally:
         gpu.free_weight(h)
 
