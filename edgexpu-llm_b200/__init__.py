@@ -28,6 +28,7 @@ TYPE_Q8_0 = 8
 TYPE_Q4_K = 12
 TYPE_Q5_K, TYPE_Q6_K = 13, 14
 QK8_0, QK_K = 32, 256
+ORDER_X86, ORDER_RELAXED = 0, 1  # EDGEXPU_CUDA_ORDER_* (include/edgexpu_cuda.h)
 Q8_0_BYTES, Q8_K_BYTES, Q4_K_BYTES = 34, 292, 144
 
 _c_u8p = ctypes.POINTER(ctypes.c_uint8)
@@ -40,6 +41,8 @@ _c_str = ctypes.c_char_p
 
 _CUDA_SIGS = {
     "edgexpu_cuda_abi_version": (_c_int, []),
+    "edgexpu_cuda_set_float_order": (_c_int, [_c_int]),
+    "edgexpu_cuda_float_order": (_c_int, []),
     "edgexpu_cuda_init": (_c_int, [_c_int, _c_str, _c_sz]),
     "edgexpu_cuda_shutdown": (_c_int, []),
     "edgexpu_cuda_last_error": (_c_str, []),
@@ -87,6 +90,8 @@ _HOST_SIGS = {
     "edgexpu_gguf_dot_quant": (ctypes.c_float, [_c_u32, _c_vp, _c_vp, _c_int]),
     "edgexpu_b200_init": (_c_int, [_c_int, _c_str, _c_sz]),
     "edgexpu_b200_shutdown": (None, []),
+    "edgexpu_b200_resident": (_c_vp, [_c_vp, _c_sz, _c_u32, _c_int, _c_int, _c_str, _c_sz]),
+    "edgexpu_b200_release_range": (None, [_c_vp, _c_sz]),
     "edgexpu_b200_last_error": (_c_str, []),
     "edgexpu_b200_clear_error": (None, []),
     "edgexpu_b200_logits_greedy": (_c_int, [_c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp, ctypes.POINTER(_c_u32), _c_str, _c_sz]),

@@ -54,6 +54,9 @@ struct Ctx {
 
 Ctx g;
 std::recursive_mutex g_mu;
+// EDGEXPU_CUDA_ORDER_X86 (default) or EDGEXPU_CUDA_ORDER_RELAXED; process-wide, survives shutdown.
+int g_order = EDGEXPU_CUDA_ORDER_X86;
+bool exact_order() { return g_order == EDGEXPU_CUDA_ORDER_X86; }
 char g_err[512] = "";
 
 int fail(char* error, size_t error_size, const char* fmt, ...) {
@@ -193,13 +196,19 @@ int run_rows_dev(float* out, const void* act, bool act_f32, const uint8_t* weigh
     a.out = out + static_cast<size_t>(t0) * n_out;
     a.out_stride = n_out;
     a.status = g.d_status;
+    a.exact = exact_order();
     EX_CUDA(ex::launch_rowstream(a, g.info, st), error, error_size);
   }
   return 1;
 }
 
-// Prefill-sized Q4_K batches run as a tensor-core GEMM (gemm_tc.cu).
-bool use_tc(uint32_t type, int m, int n_in) { return type == ex::TYPE_Q4_K && m >= ex::TC_MIN_M && n_in % ex::QK_K == 0; }
+// Prefill-sized Q4_K batches run as a tensor-core GEMM (gemm_tc.cu): always for the integer partials
+// (bit-exact either way), for float outputs only in the relaxed order (its epilogue sums the
+// super-blocks in its own order).
+bool use_tc_partials(uint32_t type, int m, int n_in) {
+  return type == ex::TYPE_Q4_K && m >= ex::TC_MIN_M && n_in % ex::QK_K == 0;
+}
+bool use_tc(uint32_t type, int m, int n_in) { return !exact_order() && use_tc_partials(type, m, n_in); }
 
 // Pack m activation rows (fp32 x, or Q8_K rows xq) into the GEMM's tile layout in g.xq.
 int tc_pack(const float* x, const uint8_t* xq, int m, int n_in, cudaStream_t st, char* error, size_t error_size) {
@@ -281,6 +290,7 @@ int run_logits_dev(const uint8_t* weight, uint32_t type, const float* hidden, in
   a.act = hidden;
   a.act_f32 = true;
   a.fmt = ex::logits_fmt(type);
+  a.exact = exact_order();
   if (ex::acts_are_q8_0(type)) {
     // native.c:2317-2319: Q8_0-class logits weights (can_dot_q8) see a Q8_0-quantized hidden
     // state (the kernel quantizes it in its prologue).
@@ -322,6 +332,16 @@ int sync_and_check(cudaStream_t st, char* error, size_t error_size) {
 extern "C" {
 
 int edgexpu_cuda_abi_version(void) { return EDGEXPU_CUDA_ABI_VERSION; }
+
+int edgexpu_cuda_set_float_order(int order) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (order != EDGEXPU_CUDA_ORDER_X86 && order != EDGEXPU_CUDA_ORDER_RELAXED)
+    return fail(nullptr, 0, "set_float_order: unknown order %d", order);
+  g_order = order;
+  return 1;
+}
+
+int edgexpu_cuda_float_order(void) { return g_order; }
 
 const char* edgexpu_cuda_last_error(void) { return g_err; }
 
@@ -669,6 +689,7 @@ int edgexpu_cuda_linear_quant_multi_dev(int n, float* const* outs, const uint8_t
     a.act_f32 = fused;
     a.status = g.d_status;
     a.n_seg = n;
+    a.exact = exact_order();
     for (int i = 0; i < n; ++i)
       a.seg[i] = ex::RowSeg{weights[i], n_outs[i], biases != nullptr ? biases[i] : nullptr,
                             outs[i] + static_cast<size_t>(t0) * n_outs[i], 0};
@@ -704,7 +725,7 @@ int edgexpu_cuda_block_partials_dev(int32_t* partials, const uint8_t* xq, const 
   if (!need_ready(nullptr, 0)) return 0;
   if (partials == nullptr || xq == nullptr || m <= 0) return fail(nullptr, 0, "invalid arguments");
   if (!lookup(weight, type, n_out, n_in, nullptr, 0)) return 0;
-  if (use_tc(type, m, n_in))
+  if (use_tc_partials(type, m, n_in))
     return tc_pack(nullptr, xq, m, n_in, pick(stream), nullptr, 0) &&
            tc_gemm(nullptr, partials, weight, nullptr, m, n_out, n_in, pick(stream), nullptr, 0);
   ex::RowStreamArgs a{};
@@ -729,7 +750,7 @@ int edgexpu_cuda_reserve(int m, int n_in, char* error, size_t error_size) {
   if (!need_ready(error, error_size)) return 0;
   if (m <= 0 || n_in <= 0) return fail(error, error_size, "invalid arguments");
   size_t need = static_cast<size_t>(m) * std::max(act_row_bytes_of(ex::TYPE_Q8_0, n_in), act_row_bytes_of(ex::TYPE_Q4_K, n_in)) + 64;
-  if (use_tc(ex::TYPE_Q4_K, m, n_in)) need = std::max(need, ex::tc_act_bytes(m, n_in) + 64);
+  if (use_tc_partials(ex::TYPE_Q4_K, m, n_in)) need = std::max(need, ex::tc_act_bytes(m, n_in) + 64);
   return grow_dev(g.xq, need, g.stream, error, error_size);
 }
 
@@ -758,6 +779,7 @@ int api_fail(char* error, size_t error_size, const char* fmt, ...) {
 }
 const DeviceInfo& api_device_info() { return g.info; }
 int api_device() { return g.device; }
+bool api_exact_order() { return exact_order(); }
 uint32_t* api_status_word() { return g.d_status; }
 size_t api_row_bytes(uint32_t type, int n) { return row_bytes_of(type, n); }
 size_t api_act_row_bytes(uint32_t type, int n) { return act_row_bytes_of(type, n); }

@@ -62,6 +62,8 @@ int api_lookup(const uint8_t* weight, uint32_t type, int n_out, int n_in, char* 
 int api_fail(char* error, size_t error_size, const char* fmt, ...);
 const DeviceInfo& api_device_info();
 int api_device();
+// True when float outputs follow the reference x86 build's order (EDGEXPU_CUDA_ORDER_X86).
+bool api_exact_order();
 uint32_t* api_status_word();
 size_t api_row_bytes(uint32_t type, int n);
 size_t api_act_row_bytes(uint32_t type, int n);

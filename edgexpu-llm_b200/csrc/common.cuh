@@ -168,7 +168,7 @@ __device__ __forceinline__ void q4k_scales_half(uint32_t s0, uint32_t s1, uint32
 // NaN and -inf never win (the reference compares with strict '>' against -inf, :2373).
 __device__ __forceinline__ unsigned long long argmax_key(float score, uint32_t id) {
   if (!(score > -INFINITY)) return 0ull;
-  uint32_t u = __float_as_uint(score);
+  uint32_t u = score == 0.0f ? 0u : __float_as_uint(score);  // -0 and +0 compare equal there
   u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   return (static_cast<unsigned long long>(u) << 32) | static_cast<unsigned long long>(0xFFFFFFFFu - id);
 }

@@ -105,6 +105,7 @@ struct RowStreamArgs {
   int n_seg;              // 0: one tensor (w, n_rows, bias, out, out_stride); 1..MAX_SEGS: seg[] (Store only)
   RowSeg seg[MAX_SEGS];
   TpArgs tp;              // Store, one tensor: sum the outputs of all ranks into out (column-sharded weights)
+  bool exact;             // Store / Argmax: reproduce the reference x86 build's float order bit for bit
 };
 
 struct DeviceInfo {

@@ -86,6 +86,7 @@ extern "C" int edgexpu_cuda_linear_quant_batch_noalloc(float* out, const float* 
     a.out = out + static_cast<size_t>(t0) * n_out;
     a.out_stride = n_out;
     a.status = ex::api_status_word();
+    a.exact = ex::api_exact_order();
     e = ex::launch_rowstream(a, ex::api_device_info(), st);
     if (e != cudaSuccess) return ex::api_fail(nullptr, 0, "noalloc linear: GEMV launch: %s", cudaGetErrorString(e));
   }

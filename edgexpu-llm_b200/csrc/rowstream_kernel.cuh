@@ -75,7 +75,8 @@ constexpr unsigned long long HOLD_LIMIT_NS = 20000;  // the hold is a scheduling
 // ---- activation layout in shared memory ----------------------------------------------------------
 //   Q8_0 x Q8_0 : unit = block (U = K/32): q chunks (t*2 + j)*U + u, then d[t*U + u]
 //   Q4_K x Q8_K : unit = half super-block (U = K/128): q chunks (t*8 + j)*U + u, then bsum chunks
-//                 [t*U + u] (4 ints: sub-blocks 4h..4h+3), then d[t*(U/2) + sb]
+//                 [t*U + u] (4 ints: sub-blocks 4h..4h+3), then d[t*(U/2) + sb], then the int16
+//                 bsums of the unit's 8 groups of 16 [t*U + u][8] (the Q6_K exact-order path reads them)
 //   Q4_K x fp32 : unit = half super-block: x chunks (t*32 + j)*U + u, then sum chunks [t*U + u]
 //                 (4 floats: sub-block sums)
 __host__ __device__ __forceinline__ int units_per_row(Fmt f, int K) { return act_of(f) == Act::Q8_0 ? K / QK8_0 : K / 128; }
@@ -83,7 +84,7 @@ __host__ __device__ __forceinline__ int units_per_row(Fmt f, int K) { return act
 __host__ __device__ __forceinline__ int act_bytes_total(Fmt f, int K, int m) {
   const int U = units_per_row(f, K);
   if (act_of(f) == Act::Q8_0) return m * U * 32 + m * U * 4;
-  if (act_of(f) == Act::Q8_K) return m * U * 128 + m * U * 16 + m * (U / 2) * 4;
+  if (act_of(f) == Act::Q8_K) return m * U * 128 + m * U * 16 + m * (U / 2) * 4 + m * U * 16;
   return m * U * 512 + m * U * 16;
 }
 
@@ -169,6 +170,7 @@ __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct, uint64_t*
     int4* xq = reinterpret_cast<int4*>(act);
     int* xb = reinterpret_cast<int*>(act + m * U * 128);
     float* xd = reinterpret_cast<float*>(act + m * U * 128 + m * U * 16);
+    int16_t* xb16 = reinterpret_cast<int16_t*>(act + m * U * 144 + m * nb * 4);
     if (a.act_f32) {  // quantize in place: one warp per 256-block (quant.cuh), loads of a batch issued first
       const float* x = static_cast<const float*>(a.act);
       const int nblk = m * nb;
@@ -207,6 +209,7 @@ __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct, uint64_t*
             // sub-block (32 elements) sums: lanes 4s .. 4s+3 (gsum already covers lane pairs)
             const int s32 = gsum + __shfl_down_sync(0xFFFFFFFFu, gsum, 2);
             if ((lane & 3) == 0) xb[(t * U + u) * 4 + ((lane >> 2) & 3)] = s32;
+            if ((lane & 1) == 0) xb16[(t * U + u) * 8 + ((lane >> 1) & 7)] = static_cast<int16_t>(gsum);
             if (lane == 0) xd[t * nb + sb] = d;
           }
         }
@@ -227,6 +230,8 @@ __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct, uint64_t*
           const int s = wi - 65;  // sub-block s: bsum groups 2s, 2s+1
           const int lo = static_cast<int16_t>(v & 0xFFFFu), hi = static_cast<int16_t>(v >> 16);
           xb[(t * U + 2 * sb + (s >> 2)) * 4 + (s & 3)] = lo + hi;
+          xb16[(t * U + 2 * sb + (s >> 2)) * 8 + (s & 3) * 2] = static_cast<int16_t>(lo);
+          xb16[(t * U + 2 * sb + (s >> 2)) * 8 + (s & 3) * 2 + 1] = static_cast<int16_t>(hi);
         }
       }
     }
@@ -897,6 +902,330 @@ __device__ __forceinline__ void row_k56_f32(const RowStreamArgs& a, const uint8_
   }
 }
 
+// ---- the x86 float order (exact mode) -------------------------------------------------------------
+// The reference's x86 Release build (AVX2 + FMA) keeps 8 float lanes per row: lane m adds, block
+// after block, fma(d_block, (float)P_m, lane) where P_m is an exact int32 partial over bytes
+// 4m..4m+3 of each 32-byte group of the block (gguf_dot_q8.c:436-1002, SIMD branches), and sums the
+// lanes with a fixed tree (hsum_float_8, :125-131).  Exact mode reproduces that order bit for bit:
+// a warp takes 4 rows at a time, lane 8r + m runs lane m of row r over the whole row in block order,
+// and the 8 lanes of a row combine with xor-shuffles in the same tree.  Non-fused float steps of the
+// reference (its C is compiled in ISO mode, no contraction) use the _rn intrinsics so that the
+// compiler does not fuse them.
+
+// A 32-bit word at a 2-byte aligned shared-memory address.
+__device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) {
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~static_cast<uintptr_t>(3));
+  const uint32_t lo = w[0];
+  if ((reinterpret_cast<uintptr_t>(p) & 2u) == 0) return lo;
+  return __funnelshift_r(lo, w[1], 16);
+}
+
+__device__ __forceinline__ uint32_t ld_u16_a2(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+
+// hsum_float_8 (gguf_dot_q8.c:125-131) over the 8 lanes of a row: ((v0+v4)+(v2+v6)) + ((v1+v5)+(v3+v7)).
+// Every lane of the 8 ends with the same bits (float addition is commutative).
+__device__ __forceinline__ float hsum8_dot(float v) {
+  v = v + __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+  v = v + __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+  return v + __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+}
+
+// hsum256 (gguf_quant.c:488-495): ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7)).
+__device__ __forceinline__ float hsum8_quant(float v) {
+  v = v + __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+  v = v + __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+  return v + __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+}
+
+// Byte k of the 6-bit scale/min word pairs of a Q4_K/Q5_K super-block header: scale (mins = false)
+// or min of sub-block j (get_scale_min_k4, gguf_quant.c:212-220).
+__device__ __forceinline__ int k4_field(const uint4& hdr, int j, bool mins) {
+  uint32_t sc4, mn4;
+  q4k_scales_half(hdr.y, hdr.z, hdr.w, j >> 2, sc4, mn4);
+  return static_cast<int>(((mins ? mn4 : sc4) >> (8 * (j & 3))) & 0xFFu);
+}
+
+// Q8_0 / Q4_0 / Q5_0 rows x Q8_0 activations in the x86 order (gguf_dot_q8.c:440-452, :486-503,
+// :556-569): lane m of the row, for every block: P = sum of the products of elements 4m..4m+3,
+// d = d_w * d_x, lane = fma(d, (float)P, lane).
+template <Fmt F, int MTOK>
+__device__ __forceinline__ void exact_b32(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int m,
+                                          float (&y)[MTOK]) {
+  constexpr int BB = F == Fmt::Q8_0xQ8_0 ? Q8_0_BYTES : (F == Fmt::Q4_0xQ8_0 ? Q4_0_BYTES : Q5_0_BYTES);
+  constexpr int SH = F == Fmt::Q8_0xQ8_0 ? 0 : (F == Fmt::Q4_0xQ8_0 ? 4 : 3);
+  const int U = a.K / QK8_0;
+  const int4* xq = reinterpret_cast<const int4*>(act);
+  const float* xd = reinterpret_cast<const float*>(act + a.m * U * 32);
+  float lane[MTOK];
+#pragma unroll
+  for (int t = 0; t < MTOK; ++t) lane[t] = 0.0f;
+  for (int b = 0; b < U; ++b) {
+    const uint8_t* blk = rowp + b * BB;
+    int w;
+    if constexpr (F == Fmt::Q8_0xQ8_0) {
+      w = static_cast<int>(ld_u32_a2(blk + 2 + 4 * m));
+    } else if constexpr (F == Fmt::Q4_0xQ8_0) {  // 16*(q - 8): low nibbles for m < 4, high for m >= 4
+      const uint32_t q = ld_u32_a2(blk + 2 + 4 * (m & 3));
+      w = static_cast<int>(((m < 4 ? (q << 4) : q) & 0xF0F0F0F0u) ^ 0x80808080u);
+    } else {  // 8*(q - 16) with the fifth bit of element 4m + k at bit 4m + k of qh
+      const uint32_t qh = ld_u32_a2(blk + 2), q = ld_u32_a2(blk + 6 + 4 * (m & 3));
+      w = static_cast<int>((((m < 4 ? (q << 3) : (q >> 1)) & 0x78787878u) | spread4_msb(qh, 4 * m)) ^ 0x80808080u);
+    }
+    const float dw = fp16_bits_to_float(ld_u16_a2(blk));
+#pragma unroll
+    for (int t = 0; t < MTOK; ++t) {
+      if (MTOK == 1 || t < a.m) {
+        const int xw = reinterpret_cast<const int*>(xq + (t * 2 + (m >> 2)) * U + b)[m & 3];
+        const int p = dp4a(w, xw, 0) >> SH;
+        lane[t] = fmaf(__fmul_rn(dw, xd[t * U + b]), static_cast<float>(p), lane[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < MTOK; ++t) y[t] = hsum8_dot(lane[t]);
+}
+
+// Q4_K / Q5_K / Q6_K rows x Q8_K activations in the x86 order (gguf_dot_q8.c:612-664, :772-830,
+// :905-963).  Lane m's partial per super-block: Q4_K / Q5_K sum_j sc_2j * sum(elements 64j+4m..) +
+// sc_2j+1 * sum(elements 64j+32+4m..); Q6_K sum over the eight 32-element groups g of
+// sc[2g + (m >= 4)] * sum(elements 32g+4m..) minus 32 * (bsum_2m * sc_2m + bsum_2m+1 * sc_2m+1).  The Q4_K
+// mins run in 4 more lanes (fma(dmin, m_2k*S_2k + m_2k+1*S_2k+1)), summed as (m0+m2) + (m1+m3) and added
+// after the lanes; Q5_K adds dmin * (float)(all mins) to one scalar per super-block.
+template <Fmt F, int MTOK>
+__device__ __forceinline__ void exact_k(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int m,
+                                        float (&y)[MTOK]) {
+  constexpr bool Q6 = F == Fmt::Q6_KxQ8_K, Q5 = F == Fmt::Q5_KxQ8_K;
+  constexpr int BB = Q6 ? Q6_K_BYTES : (Q5 ? Q5_K_BYTES : Q4_K_BYTES);
+  const int U = a.K / 128, nb = U / 2;
+  const int4* xq = reinterpret_cast<const int4*>(act);
+  const int* xb = reinterpret_cast<const int*>(act + a.m * U * 128);
+  const float* xd = reinterpret_cast<const float*>(act + a.m * U * 128 + a.m * U * 16);
+  const int16_t* xb16 = reinterpret_cast<const int16_t*>(act + a.m * U * 144 + a.m * nb * 4);
+  float lane[MTOK], mins[MTOK];
+#pragma unroll
+  for (int t = 0; t < MTOK; ++t) lane[t] = mins[t] = 0.0f;
+  for (int sb = 0; sb < nb; ++sb) {
+    const uint8_t* blk = rowp + sb * BB;
+    if constexpr (Q6) {
+      int v[8];   // group g = 4j + k: unsigned 6-bit values of elements 128j + 32k + 4m ..
+      int scg[8];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t qh = ld_u32_a2(blk + 128 + 32 * j + 4 * m);
+        const uint32_t l0 = ld_u32_a2(blk + 64 * j + 4 * m), l1 = ld_u32_a2(blk + 64 * j + 32 + 4 * m);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t src = (k & 1) ? l1 : l0;
+          const uint32_t nib = (k & 2) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
+          v[4 * j + k] = static_cast<int>(nib | (((qh >> (2 * k)) & 0x03030303u) << 4));
+          scg[4 * j + k] = static_cast<int8_t>(blk[192 + 8 * j + 2 * k + (m >= 4 ? 1 : 0)]);
+        }
+      }
+      const int sc_a = static_cast<int8_t>(blk[192 + 2 * m]), sc_b = static_cast<int8_t>(blk[192 + 2 * m + 1]);
+      const float dw = fp16_bits_to_float(ld_u16_a2(blk + 208));
+#pragma unroll
+      for (int t = 0; t < MTOK; ++t) {
+        if (MTOK == 1 || t < a.m) {
+          int p = 0;
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {  // element 32g + 4m: unit 2sb + g/4, chunk 2(g%4) + m/4, word m%4
+            const int xw = reinterpret_cast<const int*>(xq + (t * 8 + 2 * (g & 3) + (m >> 2)) * U + 2 * sb + (g >> 2))[m & 3];
+            p += scg[g] * dp4a(v[g], xw, 0);
+          }
+          // bsums 2m, 2m+1: unit 2sb + m/4, groups 2(m%4), 2(m%4)+1 of that unit
+          const int16_t* bs = xb16 + (t * U + 2 * sb + (m >> 2)) * 8 + 2 * (m & 3);
+          p -= 32 * (static_cast<int>(bs[0]) * sc_a + static_cast<int>(bs[1]) * sc_b);
+          lane[t] = fmaf(__fmul_rn(xd[t * nb + sb], dw), static_cast<float>(p), lane[t]);
+        }
+      }
+    } else {
+      const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+      uint32_t lo[4], hi[4];  // values of elements 64j + 4m .. (lo) and 64j + 32 + 4m .. (hi)
+      const uint32_t qh = Q5 ? *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * m) : 0u;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t q = *reinterpret_cast<const uint32_t*>(blk + (Q5 ? 48 : 16) + 32 * j + 4 * m);
+        lo[j] = q & 0x0F0F0F0Fu;
+        hi[j] = (q >> 4) & 0x0F0F0F0Fu;
+        if constexpr (Q5) {
+          lo[j] |= ((qh >> (2 * j)) & 0x01010101u) << 4;
+          hi[j] |= ((qh >> (2 * j + 1)) & 0x01010101u) << 4;
+        }
+      }
+      int sc[8], mn[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sc[j] = k4_field(hdr, j, false);
+        mn[j] = k4_field(hdr, j, true);
+      }
+      const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
+#pragma unroll
+      for (int t = 0; t < MTOK; ++t) {
+        if (MTOK == 1 || t < a.m) {
+          int p = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // element 64j + 4m (+32): unit 2sb + j/2, chunk 4(j%2) + m/4 (+2)
+            const int* xc = reinterpret_cast<const int*>(xq + (t * 8 + 4 * (j & 1) + (m >> 2)) * U + 2 * sb + (j >> 1));
+            const int* xh = reinterpret_cast<const int*>(xq + (t * 8 + 4 * (j & 1) + 2 + (m >> 2)) * U + 2 * sb + (j >> 1));
+            p += sc[2 * j] * dp4a(static_cast<int>(lo[j]), xc[m & 3], 0) +
+                 sc[2 * j + 1] * dp4a(static_cast<int>(hi[j]), xh[m & 3], 0);
+          }
+          const float xdt = xd[t * nb + sb];
+          lane[t] = fmaf(__fmul_rn(xdt, dw), static_cast<float>(p), lane[t]);
+          const float dmin = __fmul_rn(-xdt, dmw);
+          const int* S = xb + (t * U + 2 * sb) * 4;  // S_0..S_7 of the super-block (two units)
+          if constexpr (Q5) {
+            int tot = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tot += mn[j] * S[j];
+            mins[t] = __fadd_rn(mins[t], __fmul_rn(dmin, static_cast<float>(tot)));
+          } else {
+            const int k = m & 3;  // lanes m < 4 carry the 4 mins lanes
+            const int prod = mn[2 * k] * S[2 * k] + mn[2 * k + 1] * S[2 * k + 1];
+            mins[t] = fmaf(dmin, static_cast<float>(prod), mins[t]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < MTOK; ++t) {
+    const float s8 = hsum8_dot(lane[t]);
+    if constexpr (Q6) {
+      y[t] = s8;
+    } else if constexpr (Q5) {
+      y[t] = s8 + mins[t];
+    } else {  // (m0 + m2) + (m1 + m3) from lanes 0..3 of the row, then added after the lanes
+      float mm = mins[t] + __shfl_xor_sync(0xFFFFFFFFu, mins[t], 2);
+      mm = mm + __shfl_xor_sync(0xFFFFFFFFu, mm, 1);
+      mm = __shfl_sync(0xFFFFFFFFu, mm, (threadIdx.x & 31) & ~7);
+      y[t] = s8 + mm;
+    }
+  }
+}
+
+// Q4_K / Q5_K / Q6_K rows x fp32 activations (the greedy-logits path) in the x86 order.
+// Q4_K (gguf_quant.c:704-752 with the AVX2 dot_u4_f32_32 :545-565): per sub-block s, lane m runs
+// fma(q, x) and x + ... over elements 32s + 8i + m (i < 4), both reduced by hsum256, then
+// acc = acc + ((d*sc)*qx - (dmin*mn)*sx).  Q5_K and Q6_K have no SIMD branch (gguf_quant.c:837-892,
+// :754-794): one scalar sum over the row in the reference's element order, run by lane 0 of the row.
+template <Fmt F, int MTOK>
+__device__ __forceinline__ void exact_f32(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int m,
+                                          float (&y)[MTOK]) {
+  const int U = a.K / 128, nb = U / 2;
+  const float4* xf = reinterpret_cast<const float4*>(act);
+  // element e of the row, token t: unit e/128, float4 chunk (e%128)/4
+  auto xat = [&](int t, int e) -> float {
+    return reinterpret_cast<const float*>(xf + (t * 32 + ((e & 127) >> 2)) * U + (e >> 7))[e & 3];
+  };
+#pragma unroll
+  for (int t = 0; t < MTOK; ++t) y[t] = 0.0f;
+  if constexpr (F == Fmt::Q4_KxF32) {
+    float acc[MTOK];
+#pragma unroll
+    for (int t = 0; t < MTOK; ++t) acc[t] = 0.0f;
+    for (int sb = 0; sb < nb; ++sb) {
+      const uint8_t* blk = rowp + sb * Q4_K_BYTES;
+      const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+      const float d = fp16_bits_to_float(hdr.x), dmin = fp16_bits_to_float(hdr.x >> 16);
+      for (int s = 0; s < 8; ++s) {
+        const float d1 = __fmul_rn(d, static_cast<float>(k4_field(hdr, s, false)));
+        const float m1 = __fmul_rn(dmin, static_cast<float>(k4_field(hdr, s, true)));
+        float q[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int byte = blk[16 + 32 * (s >> 1) + 8 * i + m];
+          q[i] = static_cast<float>((s & 1) ? (byte >> 4) : (byte & 0xF));
+        }
+#pragma unroll
+        for (int t = 0; t < MTOK; ++t) {
+          if (MTOK == 1 || t < a.m) {
+            float vq = 0.0f, vx = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float xv = xat(t, sb * QK_K + 32 * s + 8 * i + m);
+              vq = fmaf(q[i], xv, vq);
+              vx = vx + xv;
+            }
+            const float qx = hsum8_quant(vq), sx = hsum8_quant(vx);
+            acc[t] = __fadd_rn(acc[t], __fsub_rn(__fmul_rn(d1, qx), __fmul_rn(m1, sx)));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < MTOK; ++t) y[t] = acc[t];
+  } else {
+    // The scalar loops, in lane 0 of the row; the other lanes take the result by shuffle.
+    float acc[MTOK];
+#pragma unroll
+    for (int t = 0; t < MTOK; ++t) acc[t] = 0.0f;
+    if (m == 0) {
+      for (int sb = 0; sb < nb; ++sb) {
+        if constexpr (F == Fmt::Q5_KxF32) {  // gguf_quant.c:866-887: acc += (d1*q0 - m1)*x[l]; acc += (d2*q1 - m2)*x[l+32]
+          const uint8_t* blk = rowp + sb * Q5_K_BYTES;
+          const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+          const float d = fp16_bits_to_float(hdr.x), dmin = fp16_bits_to_float(hdr.x >> 16);
+          for (int g = 0; g < 4; ++g) {
+            const float d1 = __fmul_rn(d, static_cast<float>(k4_field(hdr, 2 * g, false)));
+            const float m1 = __fmul_rn(dmin, static_cast<float>(k4_field(hdr, 2 * g, true)));
+            const float d2 = __fmul_rn(d, static_cast<float>(k4_field(hdr, 2 * g + 1, false)));
+            const float m2 = __fmul_rn(dmin, static_cast<float>(k4_field(hdr, 2 * g + 1, true)));
+            for (int l = 0; l < 32; ++l) {
+              const int ql = blk[48 + 32 * g + l], qh = blk[16 + l];
+              const float q0 = static_cast<float>((ql & 0xF) + (((qh >> (2 * g)) & 1) << 4));
+              const float q1 = static_cast<float>((ql >> 4) + (((qh >> (2 * g + 1)) & 1) << 4));
+#pragma unroll
+              for (int t = 0; t < MTOK; ++t) {
+                if (MTOK == 1 || t < a.m) {
+                  const int e = sb * QK_K + 64 * g + l;
+                  acc[t] = __fadd_rn(acc[t], __fmul_rn(__fsub_rn(__fmul_rn(d1, q0), m1), xat(t, e)));
+                  acc[t] = __fadd_rn(acc[t], __fmul_rn(__fsub_rn(__fmul_rn(d2, q1), m2), xat(t, e + 32)));
+                }
+              }
+            }
+          }
+        } else {  // Q6_K, gguf_quant.c:771-791: acc += d*sc*q*x for the four quarters of each l
+          const uint8_t* blk = rowp + sb * Q6_K_BYTES;
+          const float d = fp16_bits_to_float(ld_u16_a2(blk + 208));
+          for (int h = 0; h < 2; ++h) {
+            for (int l = 0; l < 32; ++l) {
+              const int qh = blk[128 + 32 * h + l], l0 = blk[64 * h + l], l1 = blk[64 * h + 32 + l];
+              const int qv[4] = {(l0 & 0xF) | ((qh & 3) << 4), (l1 & 0xF) | (((qh >> 2) & 3) << 4),
+                                 (l0 >> 4) | (((qh >> 4) & 3) << 4), (l1 >> 4) | (((qh >> 6) & 3) << 4)};
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq) {
+                const float sc = static_cast<float>(static_cast<int8_t>(blk[192 + 8 * h + l / 16 + 2 * qq]));
+                const float wv = __fmul_rn(__fmul_rn(d, sc), static_cast<float>(qv[qq] - 32));
+#pragma unroll
+                for (int t = 0; t < MTOK; ++t) {
+                  if (MTOK == 1 || t < a.m) {
+                    acc[t] = __fadd_rn(acc[t], __fmul_rn(wv, xat(t, sb * QK_K + 128 * h + 32 * qq + l)));
+                  }
+                }
+              }
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < MTOK; ++t) y[t] = __shfl_sync(0xFFFFFFFFu, acc[t], (threadIdx.x & 31) & ~7);
+  }
+}
+
+template <Fmt F, int MTOK>
+__device__ __forceinline__ void exact_row(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int m,
+                                          float (&y)[MTOK]) {
+  if constexpr (act_of(F) == Act::Q8_0) {
+    exact_b32<F, MTOK>(a, act, rowp, m, y);
+  } else if constexpr (act_of(F) == Act::Q8_K) {
+    exact_k<F, MTOK>(a, act, rowp, m, y);
+  } else {
+    exact_f32<F, MTOK>(a, act, rowp, m, y);
+  }
+}
+
 // ---- the kernel ---------------------------------------------------------------------------------
 
 // Tile -> (segment, first row, rows, weight base, output, bias, output stride).
@@ -1024,7 +1353,7 @@ __device__ void tp_finalize(const RowStreamArgs& a, const Layout& L, uint32_t e,
   }
 }
 
-template <Fmt F, RowOut MODE, int MTOK, bool XREG>
+template <Fmt F, RowOut MODE, int MTOK, bool XREG, bool EXACT>
 __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamArgs a, const Layout L) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -1115,6 +1444,57 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   bool dead = false;
   int s = 0;
   uint32_t fphase = 0;
+  if constexpr (EXACT) {
+    // Exact mode: slot g of a tile is rows 4g .. 4g+3; slot g belongs to consumer warp
+    // (it*G + g) % CONSUMER_WARPS.  Lane 8r + m runs lane m of row 4g + r (the x86 float order).
+    const int G = (R + 3) >> 2;
+    const int stepg = G % CONSUMER_WARPS;
+    const int m8 = lane & 7, rq = lane >> 3;
+    int firstg = cw;
+    for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
+      if (!dead && !wait_or_abort(&full[s], fphase, abort_flag)) {
+        atomicOr(a.status, ST_TIMEOUT_FULL);
+        *abort_flag = 1;
+        dead = true;
+      }
+      if (!dead && firstg < G) {
+        const TileDesc tr = descs[s];
+        const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + tr.misalign;
+        const int groups = (tr.nr + 3) >> 2;
+        for (int g = firstg; g < groups; g += CONSUMER_WARPS) {
+          const int r = 4 * g + rq;
+          const bool valid = r < tr.nr;
+          const uint8_t* rowp = tb + static_cast<size_t>(valid ? r : 4 * g) * a.row_bytes;
+          float y[MTOK];
+          exact_row<F, MTOK>(a, act, rowp, m8, y);
+          const long long row = static_cast<long long>(tr.r0) + r;
+          if constexpr (MODE == RowOut::Store) {
+            float mine = 0.0f;
+#pragma unroll
+            for (int t = 0; t < MTOK; ++t)
+              if (m8 == t) mine = y[t];
+            // cpu_kernel.c:594-597: out = b + dot with b = bias or 0.0f
+            if (valid && m8 < a.m) tr.out[static_cast<size_t>(m8) * tr.stride + row] = (tr.bias != nullptr ? tr.bias[row] : 0.0f) + mine;
+          } else if constexpr (MODE == RowOut::Argmax) {
+            // native.c:500-514: score = dot, plus the output bias when there is one
+            const float sc = tr.bias != nullptr ? y[0] + tr.bias[row] : y[0];
+            if (valid && m8 == 0) {
+              const unsigned long long k = argmax_key(sc, static_cast<uint32_t>(a.row0 + row));
+              best = k > best ? k : best;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      firstg -= stepg;
+      if (firstg < 0) firstg += CONSUMER_WARPS;
+      if (++s == S) {
+        s = 0;
+        fphase ^= 1u;
+      }
+    }
+  } else {
   const int step = R % CONSUMER_WARPS;
   int first = cw;  // first slot of this warp in the current tile: (cw - it*R) mod CONSUMER_WARPS
   for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
@@ -1198,6 +1578,7 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
       fphase ^= 1u;
     }
   }
+  }  // EXACT
   if constexpr (TP) tp_finalize(a, L, tp_e, threadIdx.x - 32);
   if constexpr (MODE == RowOut::Argmax) {
 #pragma unroll
@@ -1209,10 +1590,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   }
 }
 
-template <Fmt F, RowOut MODE, int MTOK, bool XREG = false>
+template <Fmt F, RowOut MODE, int MTOK, bool XREG = false, bool EXACT = false>
 cudaError_t launch_impl(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
   static int configured_smem = 0;  // per instantiation; the host API serialises its callers
-  auto kern = rowstream_kernel<F, MODE, MTOK, XREG>;
+  auto kern = rowstream_kernel<F, MODE, MTOK, XREG, EXACT>;
   if (L.smem_total > configured_smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_total);
     if (e != cudaSuccess) return e;
@@ -1231,8 +1612,23 @@ cudaError_t launch_impl(const RowStreamArgs& a, const Layout& L, int grid, cudaS
   return cudaLaunchKernelEx(&cfg, kern, a, L);
 }
 
+// The x86-float-order variants (RowStreamArgs::exact): Store and Argmax epilogues.
+template <Fmt F, RowOut MODE>
+cudaError_t launch_exact(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
+  if (a.m <= 1) return launch_impl<F, MODE, 1, false, true>(a, L, grid, st);
+  if constexpr (MODE == RowOut::Store) {
+    if (a.m <= 2) return launch_impl<F, MODE, 2, false, true>(a, L, grid, st);
+    if (a.m <= 4) return launch_impl<F, MODE, 4, false, true>(a, L, grid, st);
+    return launch_impl<F, MODE, 8, false, true>(a, L, grid, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
 template <Fmt F, RowOut MODE>
 cudaError_t launch_mtok(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
+  if constexpr (MODE == RowOut::Store || MODE == RowOut::Argmax) {
+    if (a.exact) return launch_exact<F, MODE>(a, L, grid, st);
+  }
   if constexpr (F == Fmt::Q8_0xQ8_0 || F == Fmt::Q4_KxQ8_K) {  // activations held in registers
     if (a.m == 1 && units_per_row(F, a.K) <= 32) return launch_impl<F, MODE, 1, true>(a, L, grid, st);
   }

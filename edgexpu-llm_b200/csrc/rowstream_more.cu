@@ -10,7 +10,9 @@ namespace {
 template <Fmt F>
 cudaError_t launch_modes(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
   if constexpr (act_of(F) == Act::F32) {  // the logits path: one hidden state, argmax epilogue
-    if (a.mode == RowOut::Argmax && a.m == 1) return launch_impl<F, RowOut::Argmax, 1>(a, L, grid, st);
+    if (a.mode == RowOut::Argmax && a.m == 1)
+      return a.exact ? launch_impl<F, RowOut::Argmax, 1, false, true>(a, L, grid, st)
+                     : launch_impl<F, RowOut::Argmax, 1>(a, L, grid, st);
   } else {
     if (a.mode == RowOut::Store) return launch_mtok<F, RowOut::Store>(a, L, grid, st);
     if (a.mode == RowOut::Argmax) return launch_mtok<F, RowOut::Argmax>(a, L, grid, st);

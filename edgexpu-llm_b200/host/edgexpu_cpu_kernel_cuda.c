@@ -14,7 +14,9 @@
 #include "../../include/edgexpu_b200_host.h"
 
 #include <math.h>
+#include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "../../include/edgexpu_cuda.h"
@@ -47,7 +49,153 @@ int edgexpu_b200_init(int device, char *error, size_t error_size) {
     return edgexpu_cuda_init(device, error, error_size);
 }
 
+/* ---- weight residency: host tensor bytes -> device handle, uploaded once ------------------
+ * Open-addressed table keyed by the host address of a tensor's first byte (the reference's mmap
+ * offset).  Entries are released by address range when the model file is unmapped. */
+typedef struct {
+    const uint8_t *host;
+    const uint8_t *dev;
+    size_t nbytes;
+    uint32_t type;
+    int n_out;
+    int n_in;
+} resident_entry;
+
+static resident_entry *g_res;
+static size_t g_res_cap;
+static size_t g_res_used;
+
+static size_t res_slot(const uint8_t *host) {
+    uint64_t h = (uint64_t)(uintptr_t)host;
+    h ^= h >> 33;
+    h *= 0xff51afd7ed558ccdull;
+    h ^= h >> 33;
+    return (size_t)h & (g_res_cap - 1);
+}
+
+static int res_grow(void) {
+    size_t old_cap = g_res_cap, i;
+    resident_entry *old = g_res;
+    size_t cap = old_cap ? 2 * old_cap : 1024;
+    resident_entry *t = (resident_entry *)calloc(cap, sizeof *t);
+    if (t == NULL) {
+        return 0;
+    }
+    g_res = t;
+    g_res_cap = cap;
+    g_res_used = 0;
+    for (i = 0; i < old_cap; i++) {
+        if (old[i].host != NULL) {
+            size_t k = res_slot(old[i].host);
+            while (g_res[k].host != NULL) {
+                k = (k + 1) & (cap - 1);
+            }
+            g_res[k] = old[i];
+            g_res_used++;
+        }
+    }
+    free(old);
+    return 1;
+}
+
+/* Binds the library to EDGEXPU_B200_DEVICE (default 0) on first use; edgexpu_cuda_init returns 1
+ * at once when this process already bound that device. */
+static int ensure_device(char *error, size_t error_size) {
+    const char *env = getenv("EDGEXPU_B200_DEVICE");
+    if (edgexpu_cuda_abi_version() != EDGEXPU_CUDA_ABI_VERSION) {
+        snprintf(error, error_size, "libedgexpu_cuda ABI %d, expected %d", edgexpu_cuda_abi_version(),
+                 EDGEXPU_CUDA_ABI_VERSION);
+        return 0;
+    }
+    return edgexpu_cuda_init(env != NULL ? atoi(env) : 0, error, error_size);
+}
+
+const uint8_t *edgexpu_b200_resident(const uint8_t *host, size_t nbytes, uint32_t type, int n_out, int n_in,
+                                     char *error, size_t error_size) {
+    const uint8_t *dev = NULL;
+    size_t k;
+    if (host == NULL || nbytes == 0 || n_out <= 0 || n_in <= 0) {
+        if (error != NULL && error_size > 0) {
+            snprintf(error, error_size, "resident: invalid tensor arguments");
+        }
+        return NULL;
+    }
+    if (g_res_cap != 0) {
+        for (k = res_slot(host); g_res[k].host != NULL; k = (k + 1) & (g_res_cap - 1)) {
+            if (g_res[k].host == host) {
+                resident_entry *e = &g_res[k];
+                if (e->nbytes == nbytes && e->type == type && e->n_out == n_out && e->n_in == n_in) {
+                    return e->dev;
+                }
+                snprintf(error, error_size, "resident: tensor at %p was uploaded with another shape or type", host);
+                return NULL;
+            }
+        }
+    }
+    if (!ensure_device(error, error_size)) {
+        return NULL;
+    }
+    if ((g_res_used + 1) * 2 > g_res_cap && !res_grow()) {
+        snprintf(error, error_size, "resident: out of host memory");
+        return NULL;
+    }
+    if (!edgexpu_cuda_upload_weight(host, nbytes, type, n_out, n_in, &dev, error, error_size)) {
+        return NULL;
+    }
+    k = res_slot(host);
+    while (g_res[k].host != NULL) {
+        k = (k + 1) & (g_res_cap - 1);
+    }
+    g_res[k].host = host;
+    g_res[k].dev = dev;
+    g_res[k].nbytes = nbytes;
+    g_res[k].type = type;
+    g_res[k].n_out = n_out;
+    g_res[k].n_in = n_in;
+    g_res_used++;
+    return dev;
+}
+
+void edgexpu_b200_release_range(const void *base, size_t size) {
+    const uint8_t *lo = (const uint8_t *)base;
+    size_t i;
+    resident_entry *old = g_res;
+    size_t cap = g_res_cap;
+    if (base == NULL || size == 0 || cap == 0) {
+        return;
+    }
+    /* rebuild the table without the released entries (keeps the probe chains intact) */
+    g_res = (resident_entry *)calloc(cap, sizeof *g_res);
+    if (g_res == NULL) {
+        g_res = old;
+        return;
+    }
+    g_res_used = 0;
+    for (i = 0; i < cap; i++) {
+        if (old[i].host == NULL) {
+            continue;
+        }
+        if (old[i].host >= lo && old[i].host < lo + size) {
+            edgexpu_cuda_free_weight(old[i].dev);
+            continue;
+        }
+        {
+            size_t k = res_slot(old[i].host);
+            while (g_res[k].host != NULL) {
+                k = (k + 1) & (cap - 1);
+            }
+            g_res[k] = old[i];
+            g_res_used++;
+        }
+    }
+    free(old);
+}
+
 void edgexpu_b200_shutdown(void) {
+    free(g_res);
+    g_res = NULL;
+    g_res_cap = 0;
+    g_res_used = 0;
     edgexpu_cuda_shutdown();
 }
 

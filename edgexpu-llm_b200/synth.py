@@ -26,6 +26,12 @@ BLOCK = {TYPE_Q4_0: (32, 18), TYPE_Q5_0: (32, 22), TYPE_Q8_0: (32, 34), TYPE_Q4_
          TYPE_Q5_K: (256, 176), TYPE_Q6_K: (256, 210)}
 
 
+def row_bytes(wtype: int, n: int) -> int:
+    """Bytes of one packed row of n elements (edgexpu_gguf_row_bytes, gguf_quant.c:468-480)."""
+    qk, bb = BLOCK[wtype]
+    return n // qk * bb
+
+
 def _fp16_bits(v: np.ndarray) -> np.ndarray:
     return v.astype(np.float16).view(np.uint8).reshape(v.shape + (2,))
 

@@ -29,9 +29,11 @@
  * on a GPU-side failure.  Their weight row may be a row of an uploaded tensor (device handle) or
  * host memory such as the reference's mmap'd tensor bytes.
  *
- * The shim adds three calls the reference has no counterpart for: init/shutdown of the device,
- * the sticky error, and the greedy logits call that replaces sample_next_token's chunk loop
- * (src/native.c:2355-2400).
+ * The shim adds calls the reference has no counterpart for: init/shutdown of the device, the
+ * sticky error, weight residency (edgexpu_b200_resident / _release_range, which replace the
+ * per-token staging copy) and the greedy logits call that replaces sample_next_token's chunk loop
+ * (src/native.c:2355-2400).  integration/edgexpu_b200.patch shows the four places of
+ * src/native.c that call them.
  */
 #ifndef EDGEXPU_B200_HOST_H
 #define EDGEXPU_B200_HOST_H
@@ -58,9 +60,22 @@ float edgexpu_gguf_dot_quant_q8(uint32_t type, const uint8_t *wrow, const uint8_
 float edgexpu_gguf_dot_quant_q8k(uint32_t type, const uint8_t *wrow, const uint8_t *x_q8k, int n);
 float edgexpu_gguf_dot_quant(uint32_t type, const uint8_t *row, const float *x, int n);
 
-/* Binds the shim to a CUDA device; must run before the first linear call (edgexpu_native_load). */
+/* Binds the shim to a CUDA device.  Optional: edgexpu_b200_resident binds device
+ * EDGEXPU_B200_DEVICE (default 0) on first use. */
 int edgexpu_b200_init(int device, char *error, size_t error_size);
+/* Frees every resident tensor and the device context. */
 void edgexpu_b200_shutdown(void);
+
+/* Device handle of a packed GGUF tensor that lives in host memory (the reference's mmap'd tensor
+ * bytes, tensor_bytes native.c:165-178): uploaded to HBM on the first call for `host`, the same
+ * handle on every later call.  Replaces the per-layer, per-token staging copy of load_qweight
+ * (native.c:593-655, stage_copy_bytes :350-380); the handle goes into edgexpu_qweight.data.  NULL
+ * and a message in `error` on failure, or when `host` was uploaded with another shape or type. */
+const uint8_t *edgexpu_b200_resident(const uint8_t *host, size_t nbytes, uint32_t type, int n_out, int n_in,
+                                     char *error, size_t error_size);
+/* Frees the resident tensors whose host bytes lie in [base, base + size): the model file is being
+ * unmapped (edgexpu_native_free, native.c:1203-1233), so a later mapping may reuse the addresses. */
+void edgexpu_b200_release_range(const void *base, size_t size);
 /* Sticky message of the first failure since the last clear ("" if none). */
 const char *edgexpu_b200_last_error(void);
 void edgexpu_b200_clear_error(void);

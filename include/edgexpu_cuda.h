@@ -61,6 +61,20 @@ extern "C" {
 
 int edgexpu_cuda_abi_version(void);
 
+/* Float order of every float output (linear, single-row dots, logits scores).  No counterpart in
+ * the reference.
+ *   EDGEXPU_CUDA_ORDER_X86 (the default): bit-identical to the reference's x86 Release build
+ *     (AVX2 + FMA): the same exact integer partials summed in the same float steps
+ *     (gguf_dot_q8.c:436-1002, gguf_quant.c:539-918).  Every GGUF type; batches stream the weight
+ *     once per 8 activation rows.
+ *   EDGEXPU_CUDA_ORDER_RELAXED: the same integer partials, float sums in the GEMV's own order, within
+ *     1e-5 * sum |w*x| of the reference; Q4_K batches of 64 rows and more run on the tensor-core GEMM.
+ * Integer outputs (quantized activations, block partials) are bit-exact in both.  Process-wide. */
+#define EDGEXPU_CUDA_ORDER_X86 0
+#define EDGEXPU_CUDA_ORDER_RELAXED 1
+int edgexpu_cuda_set_float_order(int order);
+int edgexpu_cuda_float_order(void);
+
 /* Bind the library to CUDA device `device` (creates its stream and scratch). */
 int edgexpu_cuda_init(int device, char *error, size_t error_size);
 /* Free every uploaded weight and all scratch; the library can be initialised again. */
@@ -89,9 +103,9 @@ int edgexpu_cuda_quantize_q8_k(const float *x, int n, uint8_t *dst, char *error,
 /* out[t*n_out + o] = bias[o] + dot(W_o, quantize(x_t)) for t < m, o < n_out; x is [m][n_in]
  * row-major, out is [m][n_out]; bias may be NULL.  Q8_0/Q5_0/Q4_0 weights use Q8_0 activations,
  * Q4_K/Q5_K/Q6_K weights use Q8_K activations (cpu_kernel.c:577-631), F16/F32 weights the fp32
- * activations (:633-643).  The GEMV kernel streams the weight once per 8 activation rows; Q4_K
- * batches of 64 rows and more (prefill) run as a tensor-core GEMM (tcgen05 kind::i8) with the
- * same integer partials. */
+ * activations (:633-643).  The GEMV kernel streams the weight once per 8 activation rows; in the
+ * relaxed float order Q4_K batches of 64 rows and more (prefill) run as a tensor-core GEMM
+ * (tcgen05 kind::i8) with the same integer partials. */
 int edgexpu_cuda_linear_quant_batch(float *out, const float *x, const uint8_t *weight, uint32_t type,
                                     const float *bias, int m, int n_out, int n_in, char *error,
                                     size_t error_size);

@@ -473,6 +473,186 @@ float eo_dot_q8(uint32_t type, const uint8_t *wrow, const uint8_t *xq, int n) {
     return eo_act_is_q8_0(type) ? dot_b32_q8_0(type, wrow, xq, n) : dot_k_q8_k(type, wrow, xq, n);
 }
 
+/* ---- float dots in the x86 Release build's order (AVX2 + FMA) ----------------------------------
+ * The SIMD branches of gguf_dot_q8.c keep 8 float lanes per row; lane m accumulates, block after
+ * block, fma(d_block, (float)P_m, lane) where P_m is an exact int32 partial over bytes 4m..4m+3 of
+ * each 32-byte group of the block; the lanes are then summed by hsum_float_8 (:125-131).  The Q4_K
+ * mins use 4 more lanes, Q5_K a scalar accumulator.  With the same integer partials and the same
+ * float steps the result is bit-identical to that build. */
+
+/* hsum_float_8, gguf_dot_q8.c:125-131: ((v0+v4) + (v2+v6)) + ((v1+v5) + (v3+v7)). */
+static float hsum8_dot(const float v[8]) {
+    float r0 = v[0] + v[4], r1 = v[1] + v[5], r2 = v[2] + v[6], r3 = v[3] + v[7];
+    return (r0 + r2) + (r1 + r3);
+}
+
+/* hsum256, gguf_quant.c:488-495: ((v0+v4) + (v1+v5)) + ((v2+v6) + (v3+v7)). */
+static float hsum8_quant(const float v[8]) {
+    float r0 = v[0] + v[4], r1 = v[1] + v[5], r2 = v[2] + v[6], r3 = v[3] + v[7];
+    return (r0 + r1) + (r2 + r3);
+}
+
+/* Q8_0 / Q4_0 / Q5_0 (gguf_dot_q8.c:440-452, :486-503, :556-569): d = d_w * d_x per block,
+ * P_m = sum of the 4 products of elements 4m..4m+3. */
+static float dot_b32_x86(uint32_t type, const uint8_t *wrow, const uint8_t *xq, int n) {
+    size_t bb = eo_block_bytes(type);
+    float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int b, m, k;
+    for (b = 0; b < n / EO_QK8_0; b++) {
+        const uint8_t *wb = wrow + (size_t)b * bb;
+        const uint8_t *xb = xq + (size_t)b * EO_Q8_0_BYTES;
+        float d = eo_fp16_to_fp32(rd_u16(wb)) * eo_fp16_to_fp32(rd_u16(xb));
+        for (m = 0; m < 8; m++) {
+            int32_t p = 0;
+            for (k = 0; k < 4; k++) {
+                p += (int32_t)b32_value(type, wb, 4 * m + k) * (int32_t)(int8_t)xb[2 + 4 * m + k];
+            }
+            lane[m] = fmaf(d, (float)p, lane[m]);
+        }
+    }
+    return hsum8_dot(lane);
+}
+
+/* Q4_K / Q5_K / Q6_K (gguf_dot_q8.c:612-664, :772-830, :905-963). */
+static float dot_k_x86(uint32_t type, const uint8_t *wrow, const uint8_t *xq, int n) {
+    size_t bb = eo_block_bytes(type);
+    float lane[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float mins[4] = {0, 0, 0, 0};
+    float summs = 0.0f;
+    int b, m, j, k, t;
+    for (b = 0; b < n / EO_QK_K; b++) {
+        const uint8_t *blk = wrow + (size_t)b * bb;
+        const uint8_t *yb = xq + (size_t)b * EO_Q8_K_BYTES;
+        const int8_t *q8 = (const int8_t *)(yb + 4);
+        int32_t p[8];
+        if (type == EO_TYPE_Q6_K) {
+            const int8_t *sc = (const int8_t *)(blk + 192);
+            float d = rd_f32(yb) * eo_fp16_to_fp32(rd_u16(blk + 208));
+            for (m = 0; m < 8; m++) {
+                int32_t acc = 0;
+                for (j = 0; j < 2; j++) {          /* 128-element halves */
+                    for (k = 0; k < 4; k++) {      /* 32-element groups, scale per 16 */
+                        int32_t s = 0;
+                        for (t = 0; t < 4; t++) {
+                            int e = 128 * j + 32 * k + 4 * m + t;
+                            s += (int32_t)(q6_k_value(blk, e) + 32) * (int32_t)q8[e];
+                        }
+                        acc += (int32_t)sc[8 * j + 2 * k + (m >= 4)] * s;
+                    }
+                }
+                acc -= 32 * ((int32_t)rd_i16(yb + 260 + 4 * m) * (int32_t)sc[2 * m] +
+                             (int32_t)rd_i16(yb + 262 + 4 * m) * (int32_t)sc[2 * m + 1]);
+                p[m] = acc;
+            }
+            for (m = 0; m < 8; m++) {
+                lane[m] = fmaf(d, (float)p[m], lane[m]);
+            }
+            continue;
+        }
+        {
+            float d = rd_f32(yb) * eo_fp16_to_fp32(rd_u16(blk));
+            float dmin = -rd_f32(yb) * eo_fp16_to_fp32(rd_u16(blk + 2));
+            uint8_t sc[8], mn[8];
+            int32_t prod[4];
+            for (j = 0; j < 8; j++) {
+                eo_q4_k_scale_min(blk + 4, j, &sc[j], &mn[j]);
+            }
+            for (k = 0; k < 4; k++) {
+                int32_t s0 = (int32_t)rd_i16(yb + 260 + 8 * k) + (int32_t)rd_i16(yb + 262 + 8 * k);
+                int32_t s1 = (int32_t)rd_i16(yb + 264 + 8 * k) + (int32_t)rd_i16(yb + 266 + 8 * k);
+                prod[k] = (int32_t)mn[2 * k] * s0 + (int32_t)mn[2 * k + 1] * s1;
+            }
+            for (m = 0; m < 8; m++) {
+                int32_t acc = 0;
+                for (j = 0; j < 4; j++) {          /* 64-element groups: low then high nibbles */
+                    int32_t lo = 0, hi = 0;
+                    for (t = 0; t < 4; t++) {
+                        int e = 64 * j + 4 * m + t;
+                        lo += (int32_t)kmin_value(type, blk, e) * (int32_t)q8[e];
+                        hi += (int32_t)kmin_value(type, blk, e + 32) * (int32_t)q8[e + 32];
+                    }
+                    acc += (int32_t)sc[2 * j] * lo + (int32_t)sc[2 * j + 1] * hi;
+                }
+                p[m] = acc;
+            }
+            if (type == EO_TYPE_Q4_K) {
+                for (k = 0; k < 4; k++) {
+                    mins[k] = fmaf(dmin, (float)prod[k], mins[k]);
+                }
+            } else {
+                summs += dmin * (float)(prod[0] + prod[1] + prod[2] + prod[3]);
+            }
+            for (m = 0; m < 8; m++) {
+                lane[m] = fmaf(d, (float)p[m], lane[m]);
+            }
+        }
+    }
+    if (type == EO_TYPE_Q4_K) {
+        /* :659-661: (m0 + m2) + (m1 + m3), added after the lane sum */
+        return hsum8_dot(lane) + ((mins[0] + mins[2]) + (mins[1] + mins[3]));
+    }
+    if (type == EO_TYPE_Q5_K) {
+        return hsum8_dot(lane) + summs;
+    }
+    return hsum8_dot(lane);
+}
+
+float eo_dot_q8_x86(uint32_t type, const uint8_t *wrow, const uint8_t *xq, int n) {
+    if (wrow == NULL || xq == NULL || eo_row_bytes(type, n) == 0) {
+        return 0.0f;
+    }
+    return eo_act_is_q8_0(type) ? dot_b32_x86(type, wrow, xq, n) : dot_k_x86(type, wrow, xq, n);
+}
+
+/* fp32 activations in the x86 order: Q4_K (gguf_quant.c:704-752 with the AVX2 dot_u4_f32_32
+ * :545-565: per 32 elements 8 fma lanes over 4 steps and 8 add lanes, each reduced by hsum256;
+ * acc += d1*qx - m1*sx) and Q8_0 (:628-645: 8 fma lanes per block, acc += d * hsum256).  The
+ * other types have no SIMD branch there: their order is eo_dot_f32's. */
+float eo_dot_f32_x86(uint32_t type, const uint8_t *wrow, const float *x, int n) {
+    int b, j, i, l;
+    float acc = 0.0f;
+    if (wrow == NULL || x == NULL || eo_row_bytes(type, n) == 0) {
+        return 0.0f;
+    }
+    if (type == EO_TYPE_Q8_0) {
+        for (b = 0; b < n / EO_QK8_0; b++) {
+            const uint8_t *blk = wrow + (size_t)b * EO_Q8_0_BYTES;
+            const float *xx = x + (size_t)b * EO_QK8_0;
+            float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (i = 0; i < EO_QK8_0; i += 8) {
+                for (l = 0; l < 8; l++) {
+                    v[l] = fmaf((float)(int8_t)blk[2 + i + l], xx[i + l], v[l]);
+                }
+            }
+            acc += eo_fp16_to_fp32(rd_u16(blk)) * hsum8_quant(v);
+        }
+        return acc;
+    }
+    if (type != EO_TYPE_Q4_K) {
+        return eo_dot_f32(type, wrow, x, n);
+    }
+    for (b = 0; b < n / EO_QK_K; b++) {
+        const uint8_t *blk = wrow + (size_t)b * EO_Q4_K_BYTES;
+        const float *xx = x + (size_t)b * EO_QK_K;
+        float d = eo_fp16_to_fp32(rd_u16(blk));
+        float mn16 = eo_fp16_to_fp32(rd_u16(blk + 2));
+        for (j = 0; j < 8; j++) {              /* sub-block j: low nibbles for even j, high for odd */
+            uint8_t sc, mn;
+            float vq[8] = {0, 0, 0, 0, 0, 0, 0, 0}, vx[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            eo_q4_k_scale_min(blk + 4, j, &sc, &mn);
+            for (i = 0; i < 32; i += 8) {
+                for (l = 0; l < 8; l++) {
+                    float xv = xx[32 * j + i + l];
+                    vq[l] = fmaf((float)q4_k_nibble(blk + 16, 32 * j + i + l), xv, vq[l]);
+                    vx[l] = vx[l] + xv;
+                }
+            }
+            acc += (d * (float)sc) * hsum8_quant(vq) - (mn16 * (float)mn) * hsum8_quant(vx);
+        }
+    }
+    return acc;
+}
+
 /* ---- float dots with fp32 activations (gguf_quant.c, scalar branches) ---------------------- */
 
 /* gguf_quant.c:704-752 (scalar dot_u4_f32_32 :596-600): per sub-block of 32,
@@ -805,6 +985,34 @@ int eo_linear_quant_batch(float *out, const float *x, const uint8_t *weight, uin
     return 1;
 }
 
+/* eo_linear_quant_batch with the dots in the x86 Release build's float order: bit-identical to
+ * that build's edgexpu_cpu_linear_quant_batch (out = b + dot, cpu_kernel.c:594-597). */
+int eo_linear_quant_batch_x86(float *out, const float *x, const uint8_t *weight, uint32_t type,
+                              const float *bias, int m, int n_out, int n_in) {
+    size_t rb = eo_row_bytes(type, n_in), qb;
+    uint8_t *xq;
+    int o;
+    if (out == NULL || x == NULL || weight == NULL || m <= 0 || n_out <= 0 || rb == 0) {
+        return 0;
+    }
+    qb = eo_act_row_bytes(type, n_in);
+    xq = quantize_rows(type, x, m, n_in);
+    if (xq == NULL) {
+        return 0;
+    }
+#pragma omp parallel for schedule(static)
+    for (o = 0; o < n_out; o++) {
+        const uint8_t *wrow = weight + (size_t)o * rb;
+        float bv = bias != NULL ? bias[o] : 0.0f;
+        int t;
+        for (t = 0; t < m; t++) {
+            out[(size_t)t * n_out + o] = bv + eo_dot_q8_x86(type, wrow, xq + (size_t)t * qb, n_in);
+        }
+    }
+    free(xq);
+    return 1;
+}
+
 int eo_linear_quant_batch_bound(double *bound, const float *x, const uint8_t *weight, uint32_t type,
                                 int m, int n_out, int n_in) {
     size_t rb = eo_row_bytes(type, n_in), qb;
@@ -834,9 +1042,24 @@ int eo_linear_quant_batch_bound(double *bound, const float *x, const uint8_t *we
  * hidden state through edgexpu_gguf_dot_quant (logit_dot_row :445-462).  Serial semantics of the
  * OpenMP merge (:2373-2383): strictly greater wins, equal scores keep the lowest id, NaN never
  * wins. */
+static int logits_argmax(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
+                         const float *bias, uint32_t *token_id, float *best_score, float *scores, int x86);
+
 int eo_logits_argmax(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd,
                      int vocab, const float *bias, uint32_t *token_id, float *best_score,
                      float *scores) {
+    return logits_argmax(weight, type, hidden, n_embd, vocab, bias, token_id, best_score, scores, 0);
+}
+
+/* The same with every score in the x86 Release build's float order (bit-identical scores). */
+int eo_logits_argmax_x86(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd,
+                         int vocab, const float *bias, uint32_t *token_id, float *best_score,
+                         float *scores) {
+    return logits_argmax(weight, type, hidden, n_embd, vocab, bias, token_id, best_score, scores, 1);
+}
+
+static int logits_argmax(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
+                         const float *bias, uint32_t *token_id, float *best_score, float *scores, int x86) {
     size_t rb = eo_row_bytes(type, n_embd);
     uint8_t *xq = NULL;
     float *sc;
@@ -860,7 +1083,8 @@ int eo_logits_argmax(const uint8_t *weight, uint32_t type, const float *hidden, 
 #pragma omp parallel for schedule(static)
     for (i = 0; i < vocab; i++) {
         const uint8_t *wrow = weight + (size_t)i * rb;
-        float s = xq != NULL ? eo_dot_q8(type, wrow, xq, n_embd) : eo_dot_f32(type, wrow, hidden, n_embd);
+        float s = xq != NULL ? (x86 ? eo_dot_q8_x86(type, wrow, xq, n_embd) : eo_dot_q8(type, wrow, xq, n_embd))
+                             : (x86 ? eo_dot_f32_x86(type, wrow, hidden, n_embd) : eo_dot_f32(type, wrow, hidden, n_embd));
         if (bias != NULL) {
             s += bias[i];
         }

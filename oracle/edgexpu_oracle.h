@@ -21,6 +21,8 @@
  *   eo_dot_f32              edgexpu_gguf_dot_quant src/gguf_quant.c:894-918 and the per-type
  *                           scalar dots :606-892
  *   eo_dequantize_row       src/gguf_quant.c:139-353 (one row)
+ *   eo_dot_q8_x86           the SIMD branches of gguf_dot_q8.c:436-1002 (AVX2 + FMA float order)
+ *   eo_dot_f32_x86          the SIMD branches of gguf_quant.c:539-670 (AVX2 + FMA float order)
  *   eo_linear_quant_batch   src/cpu_kernel.c:545-644
  *   eo_logits_argmax        src/native.c:2292-2401 greedy branch (ties -> lowest id)
  *
@@ -89,6 +91,10 @@ float eo_dot_q4_k_f32(const uint8_t *wrow, const float *x, int n);
 float eo_dot_q8_0_f32(const uint8_t *wrow, const float *x, int n);
 float eo_dot_q8(uint32_t type, const uint8_t *wrow, const uint8_t *xq, int n);
 float eo_dot_f32(uint32_t type, const uint8_t *wrow, const float *x, int n);
+/* The same dots in the float order of the reference's x86 Release build (AVX2 + FMA SIMD
+ * branches): bit-identical to that build's results. */
+float eo_dot_q8_x86(uint32_t type, const uint8_t *wrow, const uint8_t *xq, int n);
+float eo_dot_f32_x86(uint32_t type, const uint8_t *wrow, const float *x, int n);
 
 /* Tolerance bounds: sum_k |w_k * x_k| with w dequantized and x either the dequantized
  * quantized activation (q8 variants) or the fp32 activation (f32 variant). */
@@ -100,6 +106,9 @@ int eo_dequantize_row(uint32_t type, const uint8_t *wrow, int n, float *dst);
 /* out[t*n_out + o] = bias[o] + dot(W_o, quantize(x_t)); returns 0 for unsupported types. */
 int eo_linear_quant_batch(float *out, const float *x, const uint8_t *weight, uint32_t type,
                           const float *bias, int m, int n_out, int n_in);
+/* The same in the x86 Release build's float order: bit-identical to that build's linear. */
+int eo_linear_quant_batch_x86(float *out, const float *x, const uint8_t *weight, uint32_t type,
+                              const float *bias, int m, int n_out, int n_in);
 /* Same as eo_linear_quant_batch but also returns the per-(token, row) tolerance bound. */
 int eo_linear_quant_batch_bound(double *bound, const float *x, const uint8_t *weight, uint32_t type,
                                 int m, int n_out, int n_in);
@@ -108,6 +117,11 @@ int eo_linear_quant_batch_bound(double *bound, const float *x, const uint8_t *we
 int eo_logits_argmax(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd,
                      int vocab, const float *bias, uint32_t *token_id, float *best_score,
                      float *scores);
+
+/* The same with the scores in the x86 Release build's float order. */
+int eo_logits_argmax_x86(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd,
+                         int vocab, const float *bias, uint32_t *token_id, float *best_score,
+                         float *scores);
 
 #ifdef __cplusplus
 }

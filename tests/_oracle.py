@@ -82,6 +82,11 @@ class Port:
             "eo_partials_k": (_int, [_u32, _vp, _vp, _int, _vp, _vp]),
             "eo_dot_q8": (ctypes.c_float, [_u32, _vp, _vp, _int]),
             "eo_dot_f32": (ctypes.c_float, [_u32, _vp, _vp, _int]),
+            "eo_dot_q8_x86": (ctypes.c_float, [_u32, _vp, _vp, _int]),
+            "eo_dot_f32_x86": (ctypes.c_float, [_u32, _vp, _vp, _int]),
+            "eo_linear_quant_batch_x86": (_int, [_vp, _vp, _vp, _u32, _vp, _int, _int, _int]),
+            "eo_logits_argmax_x86": (_int, [_vp, _u32, _vp, _int, _int, _vp, ctypes.POINTER(_u32),
+                                            ctypes.POINTER(ctypes.c_float), _vp]),
             "eo_dot_q8_0_q8_0": (ctypes.c_float, [_vp, _vp, _int]),
             "eo_dot_q4_k_q8_k": (ctypes.c_float, [_vp, _vp, _int]),
             "eo_dot_q4_k_f32": (ctypes.c_float, [_vp, _vp, _int]),
@@ -140,7 +145,8 @@ class Port:
                 out[t, o, :, 1] = sm
         return out
 
-    def linear(self, x, w, wtype, n_out, bias=None):
+    def linear(self, x, w, wtype, n_out, bias=None, x86=False):
+        """x86=True: the reference x86 build's float order (bit-identical), else its scalar order."""
         x = np.ascontiguousarray(x, np.float32)
         if x.ndim == 1:
             x = x[None]
@@ -148,8 +154,9 @@ class Port:
         m, n_in = x.shape
         out = np.empty((m, n_out), np.float32)
         b = None if bias is None else np.ascontiguousarray(bias, np.float32)
-        assert self.lib.eo_linear_quant_batch(out.ctypes.data, x.ctypes.data, w.ctypes.data, wtype,
-                                              None if b is None else b.ctypes.data, m, n_out, n_in) == 1
+        fn = self.lib.eo_linear_quant_batch_x86 if x86 else self.lib.eo_linear_quant_batch
+        assert fn(out.ctypes.data, x.ctypes.data, w.ctypes.data, wtype, None if b is None else b.ctypes.data, m,
+                  n_out, n_in) == 1
         return out
 
     def linear_bound(self, x, w, wtype, n_out):
@@ -163,14 +170,15 @@ class Port:
                                                     m, n_out, n_in) == 1
         return out
 
-    def logits(self, w, wtype, hidden, vocab, bias=None):
+    def logits(self, w, wtype, hidden, vocab, bias=None, x86=False):
         w = np.ascontiguousarray(w, np.uint8)
         h = np.ascontiguousarray(hidden, np.float32).ravel()
         b = None if bias is None else np.ascontiguousarray(bias, np.float32)
         tok = _u32()
         sc = ctypes.c_float()
         scores = np.empty(vocab, np.float32)
-        assert self.lib.eo_logits_argmax(w.ctypes.data, wtype, h.ctypes.data, h.size, vocab,
+        fn = self.lib.eo_logits_argmax_x86 if x86 else self.lib.eo_logits_argmax
+        assert fn(w.ctypes.data, wtype, h.ctypes.data, h.size, vocab,
                                          None if b is None else b.ctypes.data, ctypes.byref(tok),
                                          ctypes.byref(sc), scores.ctypes.data) == 1
         return int(tok.value), float(sc.value), scores

@@ -19,6 +19,16 @@ from test_oracle import _synth
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def relaxed_order(gpu):
+    """The GEMM serves float outputs in the relaxed float order (include/edgexpu_cuda.h); the x86
+    order routes those batches to the GEMV.  Integer partials use the GEMM in both."""
+    cuda = gpu.load_cuda()
+    assert cuda.edgexpu_cuda_set_float_order(gpu.ORDER_RELAXED) == 1
+    yield
+    cuda.edgexpu_cuda_set_float_order(gpu.ORDER_X86)
+
+
 def pack_scales(sc, mn):
     """Inverse of get_scale_min_k4 (gguf_quant.c:212-220): eight 6-bit (scale, min) pairs -> 12 bytes."""
     s = np.zeros(12, np.uint8)

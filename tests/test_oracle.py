@@ -451,3 +451,43 @@ def test_other_types_linear_and_logits_match_reference(port, ref, wtype):
     srt = np.sort(rscores)
     if srt[-1] - srt[-2] > 2e-5 * lb.max():
         assert tok == rtok
+
+
+# ---- the x86 Release build's float order: bit-identical ---------------------------------------
+
+ALL = (TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K)
+
+
+@pytest.mark.parametrize("wtype", ALL)
+@pytest.mark.parametrize("n", [256, 1536, 4096])
+def test_x86_order_dots_bit_exact(port, ref, wtype, n):
+    """eo_dot_q8_x86 / eo_dot_f32_x86 restate the SIMD branches' float steps: every result equals
+    the reference AVX2 build's bit for bit."""
+    s = _synth()
+    rng = np.random.default_rng(wtype * 7 + n)
+    w = s.weight(rng, wtype, 16, n)
+    x = s.activations(rng, 2, n)
+    x[1, ::5] = 0.0
+    xq = port.quantize(x, wtype)
+    for t in range(2):
+        for o in range(16):
+            got = np.float32(port.lib.eo_dot_q8_x86(wtype, w[o].ctypes.data, xq[t].ctypes.data, n))
+            want = np.float32(ref.dot_q8(wtype, w[o], xq[t], n))
+            assert got.view(np.uint32) == want.view(np.uint32), ("q8", t, o)
+            got = np.float32(port.lib.eo_dot_f32_x86(wtype, w[o].ctypes.data, x[t].ctypes.data, n))
+            want = np.float32(ref.dot_f32(wtype, w[o], x[t], n))
+            assert got.view(np.uint32) == want.view(np.uint32), ("f32", t, o)
+
+
+@pytest.mark.parametrize("wtype", ALL)
+def test_x86_order_linear_bit_exact(port, ref, wtype):
+    s = _synth()
+    rng = np.random.default_rng(wtype + 31)
+    n_out, n_in, m = 70, 1024, 5
+    w = s.weight(rng, wtype, n_out, n_in)
+    x = s.activations(rng, m, n_in)
+    bias = rng.standard_normal(n_out).astype(np.float32)
+    for b in (None, bias):
+        got = port.linear(x, w, wtype, n_out, b, x86=True)
+        want = ref.linear(x, w, wtype, n_out, b)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
