@@ -32,16 +32,39 @@ cudaError_t launch_rowstream(const RowStreamArgs& in, const DeviceInfo& dev, cud
   Layout L{};
   L.stage_bytes = STAGE_TARGET;
   if (a.row_bytes + STAGE_SLACK > L.stage_bytes) L.stage_bytes = (a.row_bytes + STAGE_SLACK + 127) & ~127;
-  const int r_cap = (L.stage_bytes - STAGE_SLACK) / a.row_bytes;
+  const bool exact = a.exact && (a.mode == RowOut::Store || a.mode == RowOut::Argmax);
+  const int act = (act_bytes_total(a.fmt, a.K, a.m) + 127) & ~127;
+  L.row_stride = a.row_bytes;
+  if (exact) {
+    // The EX_ROWS rows of a warp pass are read at the same offsets at once: rows whose length is a
+    // multiple of 128 bytes would all fall in the same shared-memory banks.  Rows of 16-byte multiples
+    // are copied one by one into slots of stride = 32 (mod 128) bytes, which spreads a pass over all
+    // banks; other lengths are already staggered.
+    if (a.row_bytes % 16 == 0) L.row_stride = a.row_bytes + ((32 - a.row_bytes % 128) + 128) % 128;
+    // A warp owns its rows for a whole row's chain: stages of exactly EX_ROWS rows (where 3 fit) keep
+    // as many warp passes in flight as shared memory allows.
+    const int want = (EX_ROWS * L.row_stride + STAGE_SLACK + 127) & ~127;
+    if (3 * want <= dev.max_smem_optin - BAR_BYTES - act) {
+      L.stage_bytes = want;
+    } else {
+      L.row_stride = a.row_bytes;
+    }
+  }
+  const int r_cap = (L.stage_bytes - STAGE_SLACK) / L.row_stride;
   long long r_want = (a.n_rows + 3LL * dev.sm_count - 1) / (3LL * dev.sm_count);
   if (r_want < 1) r_want = 1;
-  L.tile_rows = static_cast<int>(r_want < r_cap ? r_want : r_cap);
+  if (exact) {  // tiles of whole warp passes
+    r_want = (r_want + EX_ROWS - 1) / EX_ROWS * EX_ROWS;
+    const int cap8 = r_cap / EX_ROWS * EX_ROWS;
+    L.tile_rows = static_cast<int>(cap8 == 0 ? r_cap : (r_want < cap8 ? r_want : cap8));
+  } else {
+    L.tile_rows = static_cast<int>(r_want < r_cap ? r_want : r_cap);
+  }
   L.n_tiles = 0;
   for (int i = 0; i < a.n_seg; ++i) {  // tiles never straddle two tensors
     a.seg[i].tile0 = L.n_tiles;
     L.n_tiles += (a.seg[i].n_rows + L.tile_rows - 1) / L.tile_rows;
   }
-  const int act = (act_bytes_total(a.fmt, a.K, a.m) + 127) & ~127;
   L.act_off = BAR_BYTES;
   L.stage_off = L.act_off + act;
   int S = (dev.max_smem_optin - L.stage_off) / L.stage_bytes;

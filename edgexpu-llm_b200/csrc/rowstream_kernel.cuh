@@ -45,6 +45,7 @@ struct Layout {
   int act_off;
   int stage_off;
   int smem_total;
+  int row_stride;  // bytes between rows in a stage: row_bytes, or padded (each row its own copy)
 };
 
 // Launches the formats of the other GGUF types (rowstream_more.cu).
@@ -59,8 +60,9 @@ constexpr int THREADS = CONSUMERS + 32;
 #define EX_RS_STAGE 32768
 #endif
 constexpr int STAGE_TARGET = EX_RS_STAGE;
-constexpr int MAX_STAGES = 8;
-constexpr int BAR_BYTES = 512;        // full[8], empty[8], abort flag, tile descriptors[8] at 256
+constexpr int MAX_STAGES = 16;
+constexpr int BAR_BYTES = 1024;       // full[16], empty[16], abort flag, xin barrier; tile descriptors[16] at 512
+constexpr int DESC_OFF = 512;
 constexpr int ACT_BUDGET = 96 * 1024;
 constexpr int STAGE_SLACK = 48;       // alignment round-down (<16) + over-read of the last block
 constexpr int MAX_M = 8;              // activation rows (tokens) per launch; the host splits more
@@ -81,10 +83,13 @@ constexpr unsigned long long HOLD_LIMIT_NS = 20000;  // the hold is a scheduling
 //                 (4 floats: sub-block sums)
 __host__ __device__ __forceinline__ int units_per_row(Fmt f, int K) { return act_of(f) == Act::Q8_0 ? K / QK8_0 : K / 128; }
 
+// Byte offset of the int16 bsums of the Q8_K layout (16-byte aligned: they are read as 64-bit words).
+__host__ __device__ __forceinline__ int xb16_off(int m, int U) { return (m * U * 144 + m * (U / 2) * 4 + 15) & ~15; }
+
 __host__ __device__ __forceinline__ int act_bytes_total(Fmt f, int K, int m) {
   const int U = units_per_row(f, K);
   if (act_of(f) == Act::Q8_0) return m * U * 32 + m * U * 4;
-  if (act_of(f) == Act::Q8_K) return m * U * 128 + m * U * 16 + m * (U / 2) * 4 + m * U * 16;
+  if (act_of(f) == Act::Q8_K) return xb16_off(m, U) + m * U * 16;
   return m * U * 512 + m * U * 16;
 }
 
@@ -170,7 +175,7 @@ __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct, uint64_t*
     int4* xq = reinterpret_cast<int4*>(act);
     int* xb = reinterpret_cast<int*>(act + m * U * 128);
     float* xd = reinterpret_cast<float*>(act + m * U * 128 + m * U * 16);
-    int16_t* xb16 = reinterpret_cast<int16_t*>(act + m * U * 144 + m * nb * 4);
+    int16_t* xb16 = reinterpret_cast<int16_t*>(act + xb16_off(m, U));
     if (a.act_f32) {  // quantize in place: one warp per 256-block (quant.cuh), loads of a batch issued first
       const float* x = static_cast<const float*>(a.act);
       const int nblk = m * nb;
@@ -243,17 +248,22 @@ __device__ void load_act(const RowStreamArgs& a, uint8_t* act, int ct, uint64_t*
       const int t = i / (U * 32), rem = i - t * U * 32, u = rem >> 5, j = rem & 31;
       xf[(t * 32 + j) * U + u] = reinterpret_cast<const float4*>(x)[i];
     }
-    for (int i = ct; i < m * U * 4; i += CONSUMERS) {  // sub-block sums, sequential order
+    for (int i = ct; i < m * U * 4; i += CONSUMERS) {
+      // Sub-block sums in the order of the reference's x86 build (dot_u4_f32_32, gguf_quant.c:545-565:
+      // lane l adds elements l, l+8, l+16, l+24; hsum256 then sums the 8 lanes), which the exact-order
+      // logits use as they are.
       const float4* p = reinterpret_cast<const float4*>(x + static_cast<size_t>(i) * 32);
-      float s = 0.0f;
+      float4 q[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float4 v = p[k];
-        s += v.x;
-        s += v.y;
-        s += v.z;
-        s += v.w;
-      }
+      for (int k = 0; k < 8; ++k) q[k] = p[k];
+      const float e[32] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
+                           q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w,
+                           q[4].x, q[4].y, q[4].z, q[4].w, q[5].x, q[5].y, q[5].z, q[5].w,
+                           q[6].x, q[6].y, q[6].z, q[6].w, q[7].x, q[7].y, q[7].z, q[7].w};
+      float v[8];
+#pragma unroll
+      for (int l = 0; l < 8; ++l) v[l] = ((e[l] + e[l + 8]) + e[l + 16]) + e[l + 24];
+      const float s = ((v[0] + v[4]) + (v[1] + v[5])) + ((v[2] + v[6]) + (v[3] + v[7]));
       const int t = i / (U * 4), rem = i - t * U * 4;
       xs[(t * U + (rem >> 2)) * 4 + (rem & 3)] = s;
     }
@@ -903,14 +913,17 @@ __device__ __forceinline__ void row_k56_f32(const RowStreamArgs& a, const uint8_
 }
 
 // ---- the x86 float order (exact mode) -------------------------------------------------------------
-// The reference's x86 Release build (AVX2 + FMA) keeps 8 float lanes per row: lane m adds, block
-// after block, fma(d_block, (float)P_m, lane) where P_m is an exact int32 partial over bytes
-// 4m..4m+3 of each 32-byte group of the block (gguf_dot_q8.c:436-1002, SIMD branches), and sums the
-// lanes with a fixed tree (hsum_float_8, :125-131).  Exact mode reproduces that order bit for bit:
-// a warp takes 4 rows at a time, lane 8r + m runs lane m of row r over the whole row in block order,
-// and the 8 lanes of a row combine with xor-shuffles in the same tree.  Non-fused float steps of the
-// reference (its C is compiled in ISO mode, no contraction) use the _rn intrinsics so that the
-// compiler does not fuse them.
+// The reference's x86 Release build (AVX2 + FMA) keeps 8 float accumulators per row: accumulator m
+// adds, block after block, fma(d_block, (float)P_m, acc_m) where P_m is an exact int32 partial over
+// bytes 4m..4m+3 of each 32-byte group of the block (gguf_dot_q8.c:436-1002, SIMD branches), and
+// the 8 are summed by a fixed tree (hsum_float_8, :125-131).  Exact mode reproduces that order bit
+// for bit: a warp takes EX_ROWS rows at a time; lane EX_LPR*r + c runs accumulators m = 2c and 2c+1
+// of row r over the whole row in block order (their bytes are 8 consecutive bytes of each group, so
+// weights and activations load as 64-bit words), and the 4 lanes of a row finish with the same
+// tree through xor-shuffles.  Non-fused float steps of the reference (its C is compiled in ISO mode,
+// without contraction) use the _rn intrinsics so that the compiler cannot fuse them.
+constexpr int EX_LPR = 4;              // lanes per row
+constexpr int EX_ROWS = 32 / EX_LPR;   // rows per warp pass
 
 // A 32-bit word at a 2-byte aligned shared-memory address.
 __device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) {
@@ -922,167 +935,207 @@ __device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t* p) {
 
 __device__ __forceinline__ uint32_t ld_u16_a2(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
-// hsum_float_8 (gguf_dot_q8.c:125-131) over the 8 lanes of a row: ((v0+v4)+(v2+v6)) + ((v1+v5)+(v3+v7)).
-// Every lane of the 8 ends with the same bits (float addition is commutative).
-__device__ __forceinline__ float hsum8_dot(float v) {
-  v = v + __shfl_xor_sync(0xFFFFFFFFu, v, 4);
-  v = v + __shfl_xor_sync(0xFFFFFFFFu, v, 2);
-  return v + __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+__device__ __forceinline__ int2 ld_i2(const int* p) { return *reinterpret_cast<const int2*>(p); }
+
+// hsum_float_8 (gguf_dot_q8.c:125-131), ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)), of the row's 8
+// accumulators held as (v0, v1) = (a_2c, a_2c+1) by lane c of the row.  Lanes c and c^2 hold m and
+// m + 4; every lane of the row ends with the same bits (float addition is commutative).
+__device__ __forceinline__ float hsum8_dot_pairs(float v0, float v1) {
+  const float r0 = v0 + __shfl_xor_sync(0xFFFFFFFFu, v0, 2);  // c = 0: a0+a4, c = 1: a2+a6
+  const float r1 = v1 + __shfl_xor_sync(0xFFFFFFFFu, v1, 2);  // c = 0: a1+a5, c = 1: a3+a7
+  return (r0 + __shfl_xor_sync(0xFFFFFFFFu, r0, 1)) + (r1 + __shfl_xor_sync(0xFFFFFFFFu, r1, 1));
 }
 
-// hsum256 (gguf_quant.c:488-495): ((v0+v4)+(v1+v5)) + ((v2+v6)+(v3+v7)).
-__device__ __forceinline__ float hsum8_quant(float v) {
-  v = v + __shfl_xor_sync(0xFFFFFFFFu, v, 4);
-  v = v + __shfl_xor_sync(0xFFFFFFFFu, v, 1);
-  return v + __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+// hsum256 (gguf_quant.c:488-495), ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7)), same holding.
+__device__ __forceinline__ float hsum8_quant_pairs(float v0, float v1) {
+  const float r0 = v0 + __shfl_xor_sync(0xFFFFFFFFu, v0, 2);
+  const float r1 = v1 + __shfl_xor_sync(0xFFFFFFFFu, v1, 2);
+  const float h = r0 + r1;  // c = 0: (a0+a4)+(a1+a5), c = 1: (a2+a6)+(a3+a7)
+  return h + __shfl_xor_sync(0xFFFFFFFFu, h, 1);
 }
 
-// Byte k of the 6-bit scale/min word pairs of a Q4_K/Q5_K super-block header: scale (mins = false)
-// or min of sub-block j (get_scale_min_k4, gguf_quant.c:212-220).
-__device__ __forceinline__ int k4_field(const uint4& hdr, int j, bool mins) {
-  uint32_t sc4, mn4;
-  q4k_scales_half(hdr.y, hdr.z, hdr.w, j >> 2, sc4, mn4);
-  return static_cast<int>(((mins ? mn4 : sc4) >> (8 * (j & 3))) & 0xFFu);
-}
-
-// Q8_0 / Q4_0 / Q5_0 rows x Q8_0 activations in the x86 order (gguf_dot_q8.c:440-452, :486-503,
-// :556-569): lane m of the row, for every block: P = sum of the products of elements 4m..4m+3,
-// d = d_w * d_x, lane = fma(d, (float)P, lane).
+// Q8_0 / Q4_0 / Q5_0 rows x Q8_0 activations (gguf_dot_q8.c:440-452, :486-503, :556-569): for every
+// block, P_m = sum of the products of elements 4m..4m+3, d = d_w * d_x, acc_m = fma(d, (float)P_m, acc_m).
 template <Fmt F, int MTOK>
-__device__ __forceinline__ void exact_b32(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int m,
+__device__ __forceinline__ void exact_b32(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int c,
                                           float (&y)[MTOK]) {
   constexpr int BB = F == Fmt::Q8_0xQ8_0 ? Q8_0_BYTES : (F == Fmt::Q4_0xQ8_0 ? Q4_0_BYTES : Q5_0_BYTES);
   constexpr int SH = F == Fmt::Q8_0xQ8_0 ? 0 : (F == Fmt::Q4_0xQ8_0 ? 4 : 3);
   const int U = a.K / QK8_0;
-  const int4* xq = reinterpret_cast<const int4*>(act);
+  const int* xq = reinterpret_cast<const int*>(act);
   const float* xd = reinterpret_cast<const float*>(act + a.m * U * 32);
-  float lane[MTOK];
+  float a0[MTOK], a1[MTOK];
 #pragma unroll
-  for (int t = 0; t < MTOK; ++t) lane[t] = 0.0f;
+  for (int t = 0; t < MTOK; ++t) a0[t] = a1[t] = 0.0f;
+#pragma unroll 2
   for (int b = 0; b < U; ++b) {
     const uint8_t* blk = rowp + b * BB;
-    int w;
+    int w0, w1;  // elements 8c .. 8c+3 and 8c+4 .. 8c+7, as signed bytes scaled by 2^SH
     if constexpr (F == Fmt::Q8_0xQ8_0) {
-      w = static_cast<int>(ld_u32_a2(blk + 2 + 4 * m));
-    } else if constexpr (F == Fmt::Q4_0xQ8_0) {  // 16*(q - 8): low nibbles for m < 4, high for m >= 4
-      const uint32_t q = ld_u32_a2(blk + 2 + 4 * (m & 3));
-      w = static_cast<int>(((m < 4 ? (q << 4) : q) & 0xF0F0F0F0u) ^ 0x80808080u);
-    } else {  // 8*(q - 16) with the fifth bit of element 4m + k at bit 4m + k of qh
-      const uint32_t qh = ld_u32_a2(blk + 2), q = ld_u32_a2(blk + 6 + 4 * (m & 3));
-      w = static_cast<int>((((m < 4 ? (q << 3) : (q >> 1)) & 0x78787878u) | spread4_msb(qh, 4 * m)) ^ 0x80808080u);
+      w0 = static_cast<int>(ld_u32_a2(blk + 2 + 8 * c));
+      w1 = static_cast<int>(ld_u32_a2(blk + 6 + 8 * c));
+    } else {
+      const uint32_t q0 = ld_u32_a2(blk + (BB - 16) + 8 * (c & 1)), q1 = ld_u32_a2(blk + (BB - 16) + 8 * (c & 1) + 4);
+      if constexpr (F == Fmt::Q4_0xQ8_0) {  // 16*(q - 8): low nibbles for elements < 16, high for >= 16
+        w0 = static_cast<int>(((c < 2 ? (q0 << 4) : q0) & 0xF0F0F0F0u) ^ 0x80808080u);
+        w1 = static_cast<int>(((c < 2 ? (q1 << 4) : q1) & 0xF0F0F0F0u) ^ 0x80808080u);
+      } else {  // 8*(q - 16), the fifth bit of element e at bit e of qh
+        const uint32_t qh = ld_u32_a2(blk + 2);
+        w0 = static_cast<int>((((c < 2 ? (q0 << 3) : (q0 >> 1)) & 0x78787878u) | spread4_msb(qh, 8 * c)) ^ 0x80808080u);
+        w1 = static_cast<int>((((c < 2 ? (q1 << 3) : (q1 >> 1)) & 0x78787878u) | spread4_msb(qh, 8 * c + 4)) ^ 0x80808080u);
+      }
     }
     const float dw = fp16_bits_to_float(ld_u16_a2(blk));
 #pragma unroll
     for (int t = 0; t < MTOK; ++t) {
       if (MTOK == 1 || t < a.m) {
-        const int xw = reinterpret_cast<const int*>(xq + (t * 2 + (m >> 2)) * U + b)[m & 3];
-        const int p = dp4a(w, xw, 0) >> SH;
-        lane[t] = fmaf(__fmul_rn(dw, xd[t * U + b]), static_cast<float>(p), lane[t]);
+        // words 2c, 2c+1 of the block's 8 activation words: chunk c/2, words 2(c%2), 2(c%2)+1
+        const int2 xw = ld_i2(xq + ((t * 2 + (c >> 1)) * U + b) * 4 + 2 * (c & 1));
+        const float d = __fmul_rn(dw, xd[t * U + b]);
+        a0[t] = fmaf(d, static_cast<float>(dp4a(w0, xw.x, 0) >> SH), a0[t]);
+        a1[t] = fmaf(d, static_cast<float>(dp4a(w1, xw.y, 0) >> SH), a1[t]);
       }
     }
   }
 #pragma unroll
-  for (int t = 0; t < MTOK; ++t) y[t] = hsum8_dot(lane[t]);
+  for (int t = 0; t < MTOK; ++t) y[t] = hsum8_dot_pairs(a0[t], a1[t]);
 }
 
-// Q4_K / Q5_K / Q6_K rows x Q8_K activations in the x86 order (gguf_dot_q8.c:612-664, :772-830,
-// :905-963).  Lane m's partial per super-block: Q4_K / Q5_K sum_j sc_2j * sum(elements 64j+4m..) +
-// sc_2j+1 * sum(elements 64j+32+4m..); Q6_K sum over the eight 32-element groups g of
-// sc[2g + (m >= 4)] * sum(elements 32g+4m..) minus 32 * (bsum_2m * sc_2m + bsum_2m+1 * sc_2m+1).  The Q4_K
-// mins run in 4 more lanes (fma(dmin, m_2k*S_2k + m_2k+1*S_2k+1)), summed as (m0+m2) + (m1+m3) and added
-// after the lanes; Q5_K adds dmin * (float)(all mins) to one scalar per super-block.
+// Q4_K / Q5_K / Q6_K rows x Q8_K activations (gguf_dot_q8.c:612-664, :772-830, :905-963).  P_m per
+// super-block: Q4_K / Q5_K sum_j sc_2j * sum(elements 64j+4m..) + sc_2j+1 * sum(elements 64j+32+4m..);
+// Q6_K sum over the eight 32-element groups g of sc[2g + (m >= 4)] * sum(elements 32g+4m..) minus
+// 32 * (bsum_2m * sc_2m + bsum_2m+1 * sc_2m+1).  The Q4_K mins run in 4 more accumulators
+// (fma(dmin, mn_2k*S_2k + mn_2k+1*S_2k+1)), summed as (m0+m2) + (m1+m3) and added after the tree;
+// Q5_K adds dmin * (float)(all mins) to one scalar per super-block.
 template <Fmt F, int MTOK>
-__device__ __forceinline__ void exact_k(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int m,
+__device__ __forceinline__ void exact_k(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int c,
                                         float (&y)[MTOK]) {
   constexpr bool Q6 = F == Fmt::Q6_KxQ8_K, Q5 = F == Fmt::Q5_KxQ8_K;
   constexpr int BB = Q6 ? Q6_K_BYTES : (Q5 ? Q5_K_BYTES : Q4_K_BYTES);
   const int U = a.K / 128, nb = U / 2;
-  const int4* xq = reinterpret_cast<const int4*>(act);
+  const int* xq = reinterpret_cast<const int*>(act);
   const int* xb = reinterpret_cast<const int*>(act + a.m * U * 128);
   const float* xd = reinterpret_cast<const float*>(act + a.m * U * 128 + a.m * U * 16);
-  const int16_t* xb16 = reinterpret_cast<const int16_t*>(act + a.m * U * 144 + a.m * nb * 4);
-  float lane[MTOK], mins[MTOK];
+  const int16_t* xb16 = reinterpret_cast<const int16_t*>(act + xb16_off(a.m, U));
+  float a0[MTOK], a1[MTOK], m0[MTOK], m1[MTOK];
 #pragma unroll
-  for (int t = 0; t < MTOK; ++t) lane[t] = mins[t] = 0.0f;
+  for (int t = 0; t < MTOK; ++t) a0[t] = a1[t] = m0[t] = m1[t] = 0.0f;
+#pragma unroll 2
   for (int sb = 0; sb < nb; ++sb) {
     const uint8_t* blk = rowp + sb * BB;
     if constexpr (Q6) {
-      int v[8];   // group g = 4j + k: unsigned 6-bit values of elements 128j + 32k + 4m ..
-      int scg[8];
+      // group g = 4j + k: unsigned 6-bit values of elements 128j + 32k + 8c .. +7 (two words)
+      uint32_t v[8][2];
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const uint32_t qh = ld_u32_a2(blk + 128 + 32 * j + 4 * m);
-        const uint32_t l0 = ld_u32_a2(blk + 64 * j + 4 * m), l1 = ld_u32_a2(blk + 64 * j + 32 + 4 * m);
+        const uint32_t h0 = ld_u32_a2(blk + 128 + 32 * j + 8 * c), h1 = ld_u32_a2(blk + 132 + 32 * j + 8 * c);
+        const uint32_t l00 = ld_u32_a2(blk + 64 * j + 8 * c), l01 = ld_u32_a2(blk + 64 * j + 4 + 8 * c);
+        const uint32_t l10 = ld_u32_a2(blk + 64 * j + 32 + 8 * c), l11 = ld_u32_a2(blk + 64 * j + 36 + 8 * c);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint32_t src = (k & 1) ? l1 : l0;
-          const uint32_t nib = (k & 2) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
-          v[4 * j + k] = static_cast<int>(nib | (((qh >> (2 * k)) & 0x03030303u) << 4));
-          scg[4 * j + k] = static_cast<int8_t>(blk[192 + 8 * j + 2 * k + (m >= 4 ? 1 : 0)]);
+          const uint32_t s0 = (k & 1) ? l10 : l00, s1 = (k & 1) ? l11 : l01;
+          const uint32_t n0 = (k & 2) ? ((s0 >> 4) & 0x0F0F0F0Fu) : (s0 & 0x0F0F0F0Fu);
+          const uint32_t n1 = (k & 2) ? ((s1 >> 4) & 0x0F0F0F0Fu) : (s1 & 0x0F0F0F0Fu);
+          v[4 * j + k][0] = n0 | (((h0 >> (2 * k)) & 0x03030303u) << 4);
+          v[4 * j + k][1] = n1 | (((h1 >> (2 * k)) & 0x03030303u) << 4);
         }
       }
-      const int sc_a = static_cast<int8_t>(blk[192 + 2 * m]), sc_b = static_cast<int8_t>(blk[192 + 2 * m + 1]);
+      // scales: group g uses sc[2g + (m >= 4)] (m = 2c, 2c+1 share it); the subtracted bsum terms use
+      // sc_2m, sc_2m+1 = sc[4c .. 4c+3]
+      const uint32_t s_lo = ld_u32_a2(blk + 192), s_hi = ld_u32_a2(blk + 196), s_lo2 = ld_u32_a2(blk + 200),
+                     s_hi2 = ld_u32_a2(blk + 204);
+      const uint32_t sw[4] = {s_lo, s_hi, s_lo2, s_hi2};
+      int scg[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        const int idx = 2 * g + (c >= 2 ? 1 : 0);
+        scg[g] = static_cast<int8_t>(sw[idx >> 2] >> (8 * (idx & 3)));
+      }
+      const uint32_t own = c == 0 ? s_lo : (c == 1 ? s_hi : (c == 2 ? s_lo2 : s_hi2));  // sc[4c .. 4c+3]
       const float dw = fp16_bits_to_float(ld_u16_a2(blk + 208));
 #pragma unroll
       for (int t = 0; t < MTOK; ++t) {
         if (MTOK == 1 || t < a.m) {
-          int p = 0;
+          int p0 = 0, p1 = 0;
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {  // element 32g + 4m: unit 2sb + g/4, chunk 2(g%4) + m/4, word m%4
-            const int xw = reinterpret_cast<const int*>(xq + (t * 8 + 2 * (g & 3) + (m >> 2)) * U + 2 * sb + (g >> 2))[m & 3];
-            p += scg[g] * dp4a(v[g], xw, 0);
+          for (int g = 0; g < 8; ++g) {  // element 32g + 8c: unit 2sb + g/4, chunk 2(g%4) + c/2, words 2(c%2)..
+            const int2 xw = ld_i2(xq + ((t * 8 + 2 * (g & 3) + (c >> 1)) * U + 2 * sb + (g >> 2)) * 4 + 2 * (c & 1));
+            p0 += scg[g] * dp4a(static_cast<int>(v[g][0]), xw.x, 0);
+            p1 += scg[g] * dp4a(static_cast<int>(v[g][1]), xw.y, 0);
           }
-          // bsums 2m, 2m+1: unit 2sb + m/4, groups 2(m%4), 2(m%4)+1 of that unit
-          const int16_t* bs = xb16 + (t * U + 2 * sb + (m >> 2)) * 8 + 2 * (m & 3);
-          p -= 32 * (static_cast<int>(bs[0]) * sc_a + static_cast<int>(bs[1]) * sc_b);
-          lane[t] = fmaf(__fmul_rn(xd[t * nb + sb], dw), static_cast<float>(p), lane[t]);
+          // bsums 4c .. 4c+3: unit 2sb + c/2, groups 4(c%2) .. of that unit
+          const int2 bsw = ld_i2(reinterpret_cast<const int*>(xb16 + (t * U + 2 * sb + (c >> 1)) * 8 + 4 * (c & 1)));
+          const int b0 = static_cast<int16_t>(bsw.x & 0xFFFF), b1 = bsw.x >> 16;
+          const int b2 = static_cast<int16_t>(bsw.y & 0xFFFF), b3 = bsw.y >> 16;
+          p0 -= 32 * (b0 * static_cast<int8_t>(own) + b1 * static_cast<int8_t>(own >> 8));
+          p1 -= 32 * (b2 * static_cast<int8_t>(own >> 16) + b3 * static_cast<int8_t>(own >> 24));
+          const float d = __fmul_rn(xd[t * nb + sb], dw);
+          a0[t] = fmaf(d, static_cast<float>(p0), a0[t]);
+          a1[t] = fmaf(d, static_cast<float>(p1), a1[t]);
         }
       }
     } else {
       const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-      uint32_t lo[4], hi[4];  // values of elements 64j + 4m .. (lo) and 64j + 32 + 4m .. (hi)
-      const uint32_t qh = Q5 ? *reinterpret_cast<const uint32_t*>(blk + 16 + 4 * m) : 0u;
+      // elements 64j + 8c .. +7 (lo) and 64j + 32 + 8c .. (hi) of the lane's two accumulators
+      uint32_t lo[4][2], hi[4][2];
+      uint2 qh = make_uint2(0u, 0u);
+      if constexpr (Q5) qh = *reinterpret_cast<const uint2*>(blk + 16 + 8 * c);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t q = *reinterpret_cast<const uint32_t*>(blk + (Q5 ? 48 : 16) + 32 * j + 4 * m);
-        lo[j] = q & 0x0F0F0F0Fu;
-        hi[j] = (q >> 4) & 0x0F0F0F0Fu;
+        const uint2 q = *reinterpret_cast<const uint2*>(blk + (Q5 ? 48 : 16) + 32 * j + 8 * c);
+        lo[j][0] = q.x & 0x0F0F0F0Fu;
+        lo[j][1] = q.y & 0x0F0F0F0Fu;
+        hi[j][0] = (q.x >> 4) & 0x0F0F0F0Fu;
+        hi[j][1] = (q.y >> 4) & 0x0F0F0F0Fu;
         if constexpr (Q5) {
-          lo[j] |= ((qh >> (2 * j)) & 0x01010101u) << 4;
-          hi[j] |= ((qh >> (2 * j + 1)) & 0x01010101u) << 4;
+          lo[j][0] |= ((qh.x >> (2 * j)) & 0x01010101u) << 4;
+          lo[j][1] |= ((qh.y >> (2 * j)) & 0x01010101u) << 4;
+          hi[j][0] |= ((qh.x >> (2 * j + 1)) & 0x01010101u) << 4;
+          hi[j][1] |= ((qh.y >> (2 * j + 1)) & 0x01010101u) << 4;
         }
       }
-      int sc[8], mn[8];
+      uint32_t sc_lo, mn_lo, sc_hi, mn_hi;  // the eight 6-bit scales and mins (get_scale_min_k4)
+      q4k_scales_half(hdr.y, hdr.z, hdr.w, 0, sc_lo, mn_lo);
+      q4k_scales_half(hdr.y, hdr.z, hdr.w, 1, sc_hi, mn_hi);
+      int sc[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        sc[j] = k4_field(hdr, j, false);
-        mn[j] = k4_field(hdr, j, true);
+      for (int j = 0; j < 4; ++j) {
+        sc[j] = static_cast<int>((sc_lo >> (8 * j)) & 0xFFu);
+        sc[4 + j] = static_cast<int>((sc_hi >> (8 * j)) & 0xFFu);
       }
+      // mins accumulators k = 2(c%2), 2(c%2)+1 use mins 4(c%2) .. 4(c%2)+3 and S of the same indices
+      const uint32_t mw = (c & 1) ? mn_hi : mn_lo;
       const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
 #pragma unroll
       for (int t = 0; t < MTOK; ++t) {
         if (MTOK == 1 || t < a.m) {
-          int p = 0;
+          int p0 = 0, p1 = 0;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {  // element 64j + 4m (+32): unit 2sb + j/2, chunk 4(j%2) + m/4 (+2)
-            const int* xc = reinterpret_cast<const int*>(xq + (t * 8 + 4 * (j & 1) + (m >> 2)) * U + 2 * sb + (j >> 1));
-            const int* xh = reinterpret_cast<const int*>(xq + (t * 8 + 4 * (j & 1) + 2 + (m >> 2)) * U + 2 * sb + (j >> 1));
-            p += sc[2 * j] * dp4a(static_cast<int>(lo[j]), xc[m & 3], 0) +
-                 sc[2 * j + 1] * dp4a(static_cast<int>(hi[j]), xh[m & 3], 0);
+          for (int j = 0; j < 4; ++j) {  // element 64j + 8c (+32): unit 2sb + j/2, chunk 4(j%2) + c/2 (+2)
+            const int* xr = xq + ((t * 8 + 4 * (j & 1) + (c >> 1)) * U + 2 * sb + (j >> 1)) * 4 + 2 * (c & 1);
+            const int2 xl = ld_i2(xr), xh = ld_i2(xr + 8 * U);
+            p0 += sc[2 * j] * dp4a(static_cast<int>(lo[j][0]), xl.x, 0) + sc[2 * j + 1] * dp4a(static_cast<int>(hi[j][0]), xh.x, 0);
+            p1 += sc[2 * j] * dp4a(static_cast<int>(lo[j][1]), xl.y, 0) + sc[2 * j + 1] * dp4a(static_cast<int>(hi[j][1]), xh.y, 0);
           }
           const float xdt = xd[t * nb + sb];
-          lane[t] = fmaf(__fmul_rn(xdt, dw), static_cast<float>(p), lane[t]);
+          const float d = __fmul_rn(xdt, dw);
+          a0[t] = fmaf(d, static_cast<float>(p0), a0[t]);
+          a1[t] = fmaf(d, static_cast<float>(p1), a1[t]);
           const float dmin = __fmul_rn(-xdt, dmw);
-          const int* S = xb + (t * U + 2 * sb) * 4;  // S_0..S_7 of the super-block (two units)
           if constexpr (Q5) {
-            int tot = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) tot += mn[j] * S[j];
-            mins[t] = __fadd_rn(mins[t], __fmul_rn(dmin, static_cast<float>(tot)));
+            const int4 s0 = *reinterpret_cast<const int4*>(xb + (t * U + 2 * sb) * 4);
+            const int4 s1 = *reinterpret_cast<const int4*>(xb + (t * U + 2 * sb + 1) * 4);
+            const int tot = static_cast<int>(mn_lo & 0xFFu) * s0.x + static_cast<int>((mn_lo >> 8) & 0xFFu) * s0.y +
+                            static_cast<int>((mn_lo >> 16) & 0xFFu) * s0.z + static_cast<int>(mn_lo >> 24) * s0.w +
+                            static_cast<int>(mn_hi & 0xFFu) * s1.x + static_cast<int>((mn_hi >> 8) & 0xFFu) * s1.y +
+                            static_cast<int>((mn_hi >> 16) & 0xFFu) * s1.z + static_cast<int>(mn_hi >> 24) * s1.w;
+            m0[t] = __fadd_rn(m0[t], __fmul_rn(dmin, static_cast<float>(tot)));
           } else {
-            const int k = m & 3;  // lanes m < 4 carry the 4 mins lanes
-            const int prod = mn[2 * k] * S[2 * k] + mn[2 * k + 1] * S[2 * k + 1];
-            mins[t] = fmaf(dmin, static_cast<float>(prod), mins[t]);
+            const int4 S = *reinterpret_cast<const int4*>(xb + (t * U + 2 * sb + (c & 1)) * 4);
+            const int pr0 = static_cast<int>(mw & 0xFFu) * S.x + static_cast<int>((mw >> 8) & 0xFFu) * S.y;
+            const int pr1 = static_cast<int>((mw >> 16) & 0xFFu) * S.z + static_cast<int>(mw >> 24) * S.w;
+            m0[t] = fmaf(dmin, static_cast<float>(pr0), m0[t]);
+            m1[t] = fmaf(dmin, static_cast<float>(pr1), m1[t]);
           }
         }
       }
@@ -1090,37 +1143,33 @@ __device__ __forceinline__ void exact_k(const RowStreamArgs& a, const uint8_t* a
   }
 #pragma unroll
   for (int t = 0; t < MTOK; ++t) {
-    const float s8 = hsum8_dot(lane[t]);
+    const float s8 = hsum8_dot_pairs(a0[t], a1[t]);
     if constexpr (Q6) {
       y[t] = s8;
     } else if constexpr (Q5) {
-      y[t] = s8 + mins[t];
-    } else {  // (m0 + m2) + (m1 + m3) from lanes 0..3 of the row, then added after the lanes
-      float mm = mins[t] + __shfl_xor_sync(0xFFFFFFFFu, mins[t], 2);
-      mm = mm + __shfl_xor_sync(0xFFFFFFFFu, mm, 1);
-      mm = __shfl_sync(0xFFFFFFFFu, mm, (threadIdx.x & 31) & ~7);
+      y[t] = s8 + m0[t];
+    } else {  // lane c%2 = 0 holds mins 0, 1, lane c%2 = 1 mins 2, 3: (m0 + m2) + (m1 + m3)
+      const float mm = (m0[t] + __shfl_xor_sync(0xFFFFFFFFu, m0[t], 1)) + (m1[t] + __shfl_xor_sync(0xFFFFFFFFu, m1[t], 1));
       y[t] = s8 + mm;
     }
   }
 }
 
 // Q4_K / Q5_K / Q6_K rows x fp32 activations (the greedy-logits path) in the x86 order.
-// Q4_K (gguf_quant.c:704-752 with the AVX2 dot_u4_f32_32 :545-565): per sub-block s, lane m runs
-// fma(q, x) and x + ... over elements 32s + 8i + m (i < 4), both reduced by hsum256, then
-// acc = acc + ((d*sc)*qx - (dmin*mn)*sx).  Q5_K and Q6_K have no SIMD branch (gguf_quant.c:837-892,
-// :754-794): one scalar sum over the row in the reference's element order, run by lane 0 of the row.
+// Q4_K (gguf_quant.c:704-752 with the AVX2 dot_u4_f32_32 :545-565): per sub-block s, accumulator m runs
+// fma(q, x) over elements 32s + 8i + m (i < 4) and hsum256 sums the 8; the x sums of the sub-block are
+// the ones the activation prologue formed in the same order; acc = acc + ((d*sc)*qx - (dmin*mn)*sx).
+// Q5_K and Q6_K have no SIMD branch there (gguf_quant.c:837-892, :754-794): one scalar sum over the
+// row in the reference's element order, run by lane 0 of the row.
 template <Fmt F, int MTOK>
-__device__ __forceinline__ void exact_f32(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int m,
+__device__ __forceinline__ void exact_f32(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int c,
                                           float (&y)[MTOK]) {
   const int U = a.K / 128, nb = U / 2;
-  const float4* xf = reinterpret_cast<const float4*>(act);
-  // element e of the row, token t: unit e/128, float4 chunk (e%128)/4
-  auto xat = [&](int t, int e) -> float {
-    return reinterpret_cast<const float*>(xf + (t * 32 + ((e & 127) >> 2)) * U + (e >> 7))[e & 3];
-  };
-#pragma unroll
-  for (int t = 0; t < MTOK; ++t) y[t] = 0.0f;
+  const float* xf = reinterpret_cast<const float*>(act);
+  // element e of the row, token t: unit e/128, float4 chunk (e%128)/4, component e%4
+  auto xat = [&](int t, int e) -> const float* { return xf + ((t * 32 + ((e & 127) >> 2)) * U + (e >> 7)) * 4 + (e & 3); };
   if constexpr (F == Fmt::Q4_KxF32) {
+    const float* xs = reinterpret_cast<const float*>(act + a.m * U * 512);  // [t][K/32] sums, x86 order
     float acc[MTOK];
 #pragma unroll
     for (int t = 0; t < MTOK; ++t) acc[t] = 0.0f;
@@ -1128,27 +1177,34 @@ __device__ __forceinline__ void exact_f32(const RowStreamArgs& a, const uint8_t*
       const uint8_t* blk = rowp + sb * Q4_K_BYTES;
       const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
       const float d = fp16_bits_to_float(hdr.x), dmin = fp16_bits_to_float(hdr.x >> 16);
-      for (int s = 0; s < 8; ++s) {
-        const float d1 = __fmul_rn(d, static_cast<float>(k4_field(hdr, s, false)));
-        const float m1 = __fmul_rn(dmin, static_cast<float>(k4_field(hdr, s, true)));
-        float q[4];
+      uint32_t sc_lo, mn_lo, sc_hi, mn_hi;
+      q4k_scales_half(hdr.y, hdr.z, hdr.w, 0, sc_lo, mn_lo);
+      q4k_scales_half(hdr.y, hdr.z, hdr.w, 1, sc_hi, mn_hi);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int byte = blk[16 + 32 * (s >> 1) + 8 * i + m];
-          q[i] = static_cast<float>((s & 1) ? (byte >> 4) : (byte & 0xF));
-        }
+      for (int g = 0; g < 4; ++g) {  // 32 bytes of group g: sub-block 2g (low nibbles), 2g+1 (high)
+        uint32_t qb[4];  // bytes 8i + 2c, 8i + 2c + 1 for i < 4 (two per 16-bit load)
 #pragma unroll
-        for (int t = 0; t < MTOK; ++t) {
-          if (MTOK == 1 || t < a.m) {
-            float vq = 0.0f, vx = 0.0f;
+        for (int i = 0; i < 4; ++i) qb[i] = *reinterpret_cast<const uint16_t*>(blk + 16 + 32 * g + 8 * i + 2 * c);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float xv = xat(t, sb * QK_K + 32 * s + 8 * i + m);
-              vq = fmaf(q[i], xv, vq);
-              vx = vx + xv;
+        for (int h = 0; h < 2; ++h) {
+          const int s = 2 * g + h;
+          const uint32_t scw = s < 4 ? sc_lo : sc_hi, mnw = s < 4 ? mn_lo : mn_hi;
+          const float d1 = __fmul_rn(d, static_cast<float>((scw >> (8 * (s & 3))) & 0xFFu));
+          const float m1 = __fmul_rn(dmin, static_cast<float>((mnw >> (8 * (s & 3))) & 0xFFu));
+#pragma unroll
+          for (int t = 0; t < MTOK; ++t) {
+            if (MTOK == 1 || t < a.m) {
+              float v0 = 0.0f, v1 = 0.0f;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float2 xv = *reinterpret_cast<const float2*>(xat(t, sb * QK_K + 32 * s + 8 * i + 2 * c));
+                const uint32_t nb2 = h ? (qb[i] >> 4) : qb[i];
+                v0 = fmaf(static_cast<float>(nb2 & 0xFu), xv.x, v0);
+                v1 = fmaf(static_cast<float>((nb2 >> 8) & 0xFu), xv.y, v1);
+              }
+              const float qx = hsum8_quant_pairs(v0, v1), sx = xs[t * (U * 4) + sb * 8 + s];
+              acc[t] = __fadd_rn(acc[t], __fsub_rn(__fmul_rn(d1, qx), __fmul_rn(m1, sx)));
             }
-            const float qx = hsum8_quant(vq), sx = hsum8_quant(vx);
-            acc[t] = __fadd_rn(acc[t], __fsub_rn(__fmul_rn(d1, qx), __fmul_rn(m1, sx)));
           }
         }
       }
@@ -1160,17 +1216,22 @@ __device__ __forceinline__ void exact_f32(const RowStreamArgs& a, const uint8_t*
     float acc[MTOK];
 #pragma unroll
     for (int t = 0; t < MTOK; ++t) acc[t] = 0.0f;
-    if (m == 0) {
+    if (c == 0) {
       for (int sb = 0; sb < nb; ++sb) {
         if constexpr (F == Fmt::Q5_KxF32) {  // gguf_quant.c:866-887: acc += (d1*q0 - m1)*x[l]; acc += (d2*q1 - m2)*x[l+32]
           const uint8_t* blk = rowp + sb * Q5_K_BYTES;
           const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
           const float d = fp16_bits_to_float(hdr.x), dmin = fp16_bits_to_float(hdr.x >> 16);
+          uint32_t sc_lo, mn_lo, sc_hi, mn_hi;
+          q4k_scales_half(hdr.y, hdr.z, hdr.w, 0, sc_lo, mn_lo);
+          q4k_scales_half(hdr.y, hdr.z, hdr.w, 1, sc_hi, mn_hi);
           for (int g = 0; g < 4; ++g) {
-            const float d1 = __fmul_rn(d, static_cast<float>(k4_field(hdr, 2 * g, false)));
-            const float m1 = __fmul_rn(dmin, static_cast<float>(k4_field(hdr, 2 * g, true)));
-            const float d2 = __fmul_rn(d, static_cast<float>(k4_field(hdr, 2 * g + 1, false)));
-            const float m2 = __fmul_rn(dmin, static_cast<float>(k4_field(hdr, 2 * g + 1, true)));
+            const uint32_t scw = g < 2 ? sc_lo : sc_hi, mnw = g < 2 ? mn_lo : mn_hi;
+            const int sh = 16 * (g & 1);
+            const float d1 = __fmul_rn(d, static_cast<float>((scw >> sh) & 0xFFu));
+            const float m1 = __fmul_rn(dmin, static_cast<float>((mnw >> sh) & 0xFFu));
+            const float d2 = __fmul_rn(d, static_cast<float>((scw >> (sh + 8)) & 0xFFu));
+            const float m2 = __fmul_rn(dmin, static_cast<float>((mnw >> (sh + 8)) & 0xFFu));
             for (int l = 0; l < 32; ++l) {
               const int ql = blk[48 + 32 * g + l], qh = blk[16 + l];
               const float q0 = static_cast<float>((ql & 0xF) + (((qh >> (2 * g)) & 1) << 4));
@@ -1179,8 +1240,8 @@ __device__ __forceinline__ void exact_f32(const RowStreamArgs& a, const uint8_t*
               for (int t = 0; t < MTOK; ++t) {
                 if (MTOK == 1 || t < a.m) {
                   const int e = sb * QK_K + 64 * g + l;
-                  acc[t] = __fadd_rn(acc[t], __fmul_rn(__fsub_rn(__fmul_rn(d1, q0), m1), xat(t, e)));
-                  acc[t] = __fadd_rn(acc[t], __fmul_rn(__fsub_rn(__fmul_rn(d2, q1), m2), xat(t, e + 32)));
+                  acc[t] = __fadd_rn(acc[t], __fmul_rn(__fsub_rn(__fmul_rn(d1, q0), m1), *xat(t, e)));
+                  acc[t] = __fadd_rn(acc[t], __fmul_rn(__fsub_rn(__fmul_rn(d2, q1), m2), *xat(t, e + 32)));
                 }
               }
             }
@@ -1200,7 +1261,7 @@ __device__ __forceinline__ void exact_f32(const RowStreamArgs& a, const uint8_t*
 #pragma unroll
                 for (int t = 0; t < MTOK; ++t) {
                   if (MTOK == 1 || t < a.m) {
-                    acc[t] = __fadd_rn(acc[t], __fmul_rn(wv, xat(t, sb * QK_K + 128 * h + 32 * qq + l)));
+                    acc[t] = __fadd_rn(acc[t], __fmul_rn(wv, *xat(t, sb * QK_K + 128 * h + 32 * qq + l)));
                   }
                 }
               }
@@ -1210,19 +1271,19 @@ __device__ __forceinline__ void exact_f32(const RowStreamArgs& a, const uint8_t*
       }
     }
 #pragma unroll
-    for (int t = 0; t < MTOK; ++t) y[t] = __shfl_sync(0xFFFFFFFFu, acc[t], (threadIdx.x & 31) & ~7);
+    for (int t = 0; t < MTOK; ++t) y[t] = __shfl_sync(0xFFFFFFFFu, acc[t], (threadIdx.x & 31) & ~(EX_LPR - 1));
   }
 }
 
 template <Fmt F, int MTOK>
-__device__ __forceinline__ void exact_row(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int m,
+__device__ __forceinline__ void exact_row(const RowStreamArgs& a, const uint8_t* act, const uint8_t* rowp, int c,
                                           float (&y)[MTOK]) {
   if constexpr (act_of(F) == Act::Q8_0) {
-    exact_b32<F, MTOK>(a, act, rowp, m, y);
+    exact_b32<F, MTOK>(a, act, rowp, c, y);
   } else if constexpr (act_of(F) == Act::Q8_K) {
-    exact_k<F, MTOK>(a, act, rowp, m, y);
+    exact_k<F, MTOK>(a, act, rowp, c, y);
   } else {
-    exact_f32<F, MTOK>(a, act, rowp, m, y);
+    exact_f32<F, MTOK>(a, act, rowp, c, y);
   }
 }
 
@@ -1360,8 +1421,9 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   uint64_t* empty = full + MAX_STAGES;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 2 * MAX_STAGES * 8);
   uint64_t* xin = reinterpret_cast<uint64_t*>(smem + 2 * MAX_STAGES * 8 + 8);
-  TileDesc* descs = reinterpret_cast<TileDesc*>(smem + 256);
-  static_assert(256 + MAX_STAGES * sizeof(TileDesc) <= BAR_BYTES, "tile descriptors fit the header");
+  TileDesc* descs = reinterpret_cast<TileDesc*>(smem + DESC_OFF);
+  static_assert(2 * MAX_STAGES * 8 + 16 <= DESC_OFF, "barriers fit below the descriptors");
+  static_assert(DESC_OFF + MAX_STAGES * sizeof(TileDesc) <= BAR_BYTES, "tile descriptors fit the header");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = L.n_stages;
 
@@ -1402,7 +1464,6 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
       const TileRef tr = tile_ref(a, L, tile);
       const uintptr_t start = reinterpret_cast<uintptr_t>(tr.w) + static_cast<uintptr_t>(tr.r0) * a.row_bytes;
       const uintptr_t al = start & ~static_cast<uintptr_t>(15);
-      const uint32_t bytes = static_cast<uint32_t>((start - al + static_cast<long long>(tr.nr) * a.row_bytes + 15) & ~15ull);
       TileDesc& td = descs[s];
       td.out = tr.out;
       td.bias = tr.bias;
@@ -1410,8 +1471,17 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
       td.nr = tr.nr;
       td.stride = static_cast<int>(tr.stride);
       td.misalign = static_cast<int>(start - al);
-      mbar_arrive_expect_tx(&full[s], bytes);
-      bulk_g2s(smem + L.stage_off + s * L.stage_bytes, reinterpret_cast<const void*>(al), bytes, &full[s], pol);
+      uint8_t* dst = smem + L.stage_off + s * L.stage_bytes;
+      if (L.row_stride != a.row_bytes) {  // padded rows (16-byte multiples, so start == al): one copy per row
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(tr.nr) * a.row_bytes);
+        for (int i = 0; i < tr.nr; ++i)
+          bulk_g2s(dst + i * L.row_stride, reinterpret_cast<const void*>(start + static_cast<uintptr_t>(i) * a.row_bytes),
+                   a.row_bytes, &full[s], pol);
+      } else {
+        const uint32_t bytes = static_cast<uint32_t>((start - al + static_cast<long long>(tr.nr) * a.row_bytes + 15) & ~15ull);
+        mbar_arrive_expect_tx(&full[s], bytes);
+        bulk_g2s(dst, reinterpret_cast<const void*>(al), bytes, &full[s], pol);
+      }
       if (++s == S) {
         s = 0;
         ephase ^= 1u;
@@ -1445,11 +1515,12 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   int s = 0;
   uint32_t fphase = 0;
   if constexpr (EXACT) {
-    // Exact mode: slot g of a tile is rows 4g .. 4g+3; slot g belongs to consumer warp
-    // (it*G + g) % CONSUMER_WARPS.  Lane 8r + m runs lane m of row 4g + r (the x86 float order).
-    const int G = (R + 3) >> 2;
+    // Exact mode: slot g of a tile is rows EX_ROWS*g .. EX_ROWS*g + EX_ROWS-1; slot g belongs to
+    // consumer warp (it*G + g) % CONSUMER_WARPS.  Lane EX_LPR*r + c runs accumulators 2c, 2c+1 of row
+    // EX_ROWS*g + r (the x86 float order).
+    const int G = (R + EX_ROWS - 1) / EX_ROWS;
     const int stepg = G % CONSUMER_WARPS;
-    const int m8 = lane & 7, rq = lane >> 3;
+    const int c = lane & (EX_LPR - 1), rq = lane / EX_LPR;
     int firstg = cw;
     for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
       if (!dead && !wait_or_abort(&full[s], fphase, abort_flag)) {
@@ -1460,25 +1531,24 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
       if (!dead && firstg < G) {
         const TileDesc tr = descs[s];
         const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + tr.misalign;
-        const int groups = (tr.nr + 3) >> 2;
+        const int groups = (tr.nr + EX_ROWS - 1) / EX_ROWS;
         for (int g = firstg; g < groups; g += CONSUMER_WARPS) {
-          const int r = 4 * g + rq;
+          const int r = EX_ROWS * g + rq;
           const bool valid = r < tr.nr;
-          const uint8_t* rowp = tb + static_cast<size_t>(valid ? r : 4 * g) * a.row_bytes;
+          const uint8_t* rowp = tb + static_cast<size_t>(valid ? r : EX_ROWS * g) * L.row_stride;
           float y[MTOK];
-          exact_row<F, MTOK>(a, act, rowp, m8, y);
+          exact_row<F, MTOK>(a, act, rowp, c, y);
           const long long row = static_cast<long long>(tr.r0) + r;
           if constexpr (MODE == RowOut::Store) {
-            float mine = 0.0f;
+            // cpu_kernel.c:594-597: out = b + dot with b = bias or 0.0f; lane c stores tokens c, c + EX_LPR, ...
 #pragma unroll
             for (int t = 0; t < MTOK; ++t)
-              if (m8 == t) mine = y[t];
-            // cpu_kernel.c:594-597: out = b + dot with b = bias or 0.0f
-            if (valid && m8 < a.m) tr.out[static_cast<size_t>(m8) * tr.stride + row] = (tr.bias != nullptr ? tr.bias[row] : 0.0f) + mine;
+              if (valid && t < a.m && (t % EX_LPR) == c)
+                tr.out[static_cast<size_t>(t) * tr.stride + row] = (tr.bias != nullptr ? tr.bias[row] : 0.0f) + y[t];
           } else if constexpr (MODE == RowOut::Argmax) {
             // native.c:500-514: score = dot, plus the output bias when there is one
             const float sc = tr.bias != nullptr ? y[0] + tr.bias[row] : y[0];
-            if (valid && m8 == 0) {
+            if (valid && c == 0) {
               const unsigned long long k = argmax_key(sc, static_cast<uint32_t>(a.row0 + row));
               best = k > best ? k : best;
             }
