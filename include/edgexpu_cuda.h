@@ -155,14 +155,17 @@ int edgexpu_cuda_linear_quant_multi_dev(int n, float *const *outs, const uint8_t
 
 /* Same result as edgexpu_cuda_linear_quant_batch_dev, but the call allocates no memory: no
  * cudaMalloc, no cudaFree, no allocating library routine.  It has no counterpart in the reference;
- * it is for callers that cannot allocate once running -- code recorded into a CUDA graph, runtimes
- * whose HBM budget is fixed at model load, and decode loops that must not risk the device-wide
- * synchronisation an allocation or free can cause.  The quantized activations go to one fixed
- * 1 MiB device array compiled into the library (held on every GPU that loads it until exit), so
- * m * (quantized row bytes) must fit in 1 MiB (e.g. 224 rows of 4096 for Q4_K, 60 rows of 16384
- * for Q8_0); larger batches are rejected with an error.  The first call on a device looks up the
- * array's device address; make it before any stream capture.  All calls share the array, so calls
- * whose GPU work overlaps (two streams at once) race and must be serialised by the caller. */
+ * it is for callers that cannot allocate once running -- runtimes whose HBM budget is fixed at model
+ * load, and decode loops that must not risk the device-wide synchronisation an allocation or free can
+ * cause.  Batches of one or two rows use no scratch (the GEMV quantizes them itself); larger batches
+ * put their quantized activations in one fixed 1 MiB device array compiled into the library (held on
+ * every GPU that loads it until exit), so m * (quantized row bytes) must fit in 1 MiB (e.g. 224 rows of
+ * 4096 for Q4_K, 60 rows of 16384 for Q8_0); larger batches are rejected with an error.  The first
+ * call on a device looks up the array's device address; make it before any stream capture.  All calls
+ * share the array, so calls whose GPU work overlaps (two streams at once) race and must be serialised
+ * by the caller.  Meant for decode-sized batches: where the regular entry point would run a Q4_K
+ * prefill batch on the tensor-core GEMM (relaxed float order), this one streams the weight once per
+ * 8 rows. */
 int edgexpu_cuda_linear_quant_batch_noalloc(float *out, const float *x, const uint8_t *weight, uint32_t type,
                                             const float *bias, int m, int n_out, int n_in, void *stream);
 
