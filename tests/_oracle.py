@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import importlib.util
+import os
 import pathlib
 import subprocess
 import sys
@@ -20,7 +21,10 @@ ORACLE_DIR = REPO / "oracle"
 PORT_LIB = ORACLE_DIR / "liboracle_port.so"
 REF_AVX2 = ORACLE_DIR / "_ref" / "libedgexpu_ref_avx2.so"
 REF_SCALAR = ORACLE_DIR / "_ref" / "libedgexpu_ref_scalar.so"
-REF_SRC = pathlib.Path("/root/reference/src")
+# The reference checkout (development container only): $EDGEXPU_REFERENCE, else a sibling directory
+# of this repository named "reference".
+REFERENCE = pathlib.Path(os.environ.get("EDGEXPU_REFERENCE", str(REPO.parent / "reference")))
+REF_SRC = REFERENCE / "src"
 
 TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 2, 6, 8, 12, 13, 14
 ALL_TYPES = (TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K)
@@ -59,7 +63,7 @@ def ensure_ref() -> bool:
     if REF_AVX2.exists() and REF_SCALAR.exists():
         return True
     if REF_SRC.exists():
-        subprocess.run(["make", "-s", "-C", str(ORACLE_DIR), "ref"], check=True)
+        subprocess.run(["make", "-s", "-C", str(ORACLE_DIR), "ref", f"REF={REFERENCE}"], check=True)
         return REF_AVX2.exists()
     return False
 
