@@ -18,6 +18,14 @@ Workloads (``--workload``):
   max-reduction of packed (score, id) keys.  Total work is fixed, so scaling is "strong".
 * ``smollm2_q8_0_decode``: configuration 1's weight stream (30 layers of SmolLM2-135M-shaped
   Q8_0 projections + the tied 49152x576 Q8_0 logits), replicas only at N > 1.
+* ``native_greedy``: configurations 1 and 4 end to end -- greedy decode tok/s through the reference's
+  own layer loop (src/native.c) with the B200 path dropped in (integration/_build/
+  libedgexpu_native_b200.so: every linear and the greedy logits on the GPU, weights resident in HBM,
+  the rest of the loop on the host), on a seeded synthetic GGUF model (``--model smollm2``: SmolLM2-
+  135M-shaped Q8_0, or ``llama3``: Llama-3-8B-shaped Q4_K, ``--layers`` to shorten it), ``--prompt``
+  prompt ids, then ``--steps`` greedy tokens; the reference arm runs the unchanged reference runtime
+  (oracle/_ref/libedgexpu_ref_runtime.so) on the same file.  The line also states whether the token
+  ids of both are identical.  N > 1: independent replicas, one per GPU.
 * ``llama3_8b_q4k_prefill``: configuration 3 -- one step = every quantized projection of the
   32 Llama-3-8B-shaped layers (``--layers`` fewer for small profiling cases) for a prompt of
   ``--batch`` tokens (default 2048), run by the tensor-core GEMM (tcgen05 kind::i8).  Metric:
@@ -1133,13 +1141,132 @@ def run_prefill(args):
         dist.destroy_process_group()
 
 
+# ---- end to end through the reference's layer loop ---------------------------------------------
+
+NATIVE_B200 = ROOT / "integration" / "_build" / "libedgexpu_native_b200.so"
+NATIVE_REF = ROOT / "oracle" / "_ref" / "libedgexpu_ref_runtime.so"
+
+
+def _bind_greedy(path):
+    lib = ctypes.CDLL(str(path))
+    f = lib.edgexpu_greedy_run
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                  ctypes.c_int, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
+    return f
+
+
+def _greedy(fn, path, prompt, n_new):
+    import numpy as np
+
+    ids = np.zeros(n_new, np.uint32)
+    secs = np.zeros(2)
+    err = ctypes.create_string_buffer(1024)
+    made = fn(str(path).encode(), prompt.ctypes.data, prompt.size, n_new, ids.ctypes.data, None, 0, secs.ctypes.data,
+              err, 1024)
+    if made != n_new:
+        raise RuntimeError(err.value.decode(errors="replace"))
+    return ids, secs
+
+
+def run_native(args):
+    import tempfile
+
+    world, rank, local = dist_env()
+    os.environ["EDGEXPU_B200_DEVICE"] = str(local)
+    pkg = load_pkg()
+    from edgexpu_llm_b200 import gguf_synth as gs
+
+    shape = gs.SMOLLM2_135M_Q8_0 if args.model == "smollm2" else gs.LLAMA3_8B_Q4_K
+    if args.layers:
+        shape = shape.with_layers(args.layers)
+    n_prompt = args.prompt or (128 if args.model == "smollm2" else 512)
+    n_new = args.steps
+    is_ref = args.impl == "reference"
+    if is_ref and rank != 0:
+        return
+    with tempfile.TemporaryDirectory() as td:
+        path = gs.write_llama_gguf(pathlib.Path(td) / f"{shape.name}.gguf", shape, seed=0)
+        prompt = gs.prompt_ids(shape, n_prompt, seed=0)
+        ref_fn = _bind_greedy(NATIVE_REF) if NATIVE_REF.exists() else None
+        if is_ref:
+            if ref_fn is None:
+                print(json.dumps({"impl": "reference", "unavailable": f"{NATIVE_REF} not built"}))
+                return
+            _greedy(ref_fn, path, prompt, min(n_new, max(1, args.warmup)))  # warm-up (thread probe, page cache)
+            ids, secs = _greedy(ref_fn, path, prompt, n_new)
+        else:
+            pkg.load_cuda()
+            if not pkg.load_cuda().edgexpu_cuda_set_float_order(0 if args.float_order == "x86" else 1):
+                raise RuntimeError("set_float_order")
+            fn = _bind_greedy(NATIVE_B200)
+            _greedy(fn, path, prompt, min(n_new, max(1, args.warmup)))  # warm-up (first uploads, kernel attributes)
+            ids, secs = _greedy(fn, path, prompt, n_new)
+        tok_s = n_new / secs[1]
+        ref_line = None
+        if not is_ref and rank == 0 and world == 1 and ref_fn is not None and not args.no_cpu_baseline:
+            r_ids, r_secs = _greedy(ref_fn, path, prompt, n_new)
+            ref_line = {"value": round(n_new / r_secs[1], 3), "unit": "tok/s", "cores": host_threads(), "kind": "reference",
+                        "sample": f"the same {n_prompt}-token prompt and {n_new} greedy tokens through the unchanged "
+                                  f"reference runtime (oracle/_ref, AVX2 + OpenMP); prefill {r_secs[0]:.3f} s",
+                        "greedy_ids_identical": bool((r_ids == ids).all())}
+    wb = shape.weight_bytes_per_token()
+    tot = torch_all_sum(tok_s, world) if (world > 1 and not is_ref) else tok_s
+    peak, peak_kind = peak_hbm()
+    line = {
+        "metric": f"decode tok/s through the reference's layer loop ({shape.name}, batch 1)",
+        "value": round(tot, 3), "unit": "tok/s", "n_gpus": 1 if is_ref else world, "steps": n_new,
+        "warmup": args.warmup, "ms_per_step": round(secs[1] / n_new * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "i8 x i8 -> i32 -> f32" if shape.wtype == 8 else "u4/i8 x i8 -> i32 -> f32",
+        "data": "synthetic (seeded random-init GGUF model, uniform random prompt ids)",
+        "config": {"workload": "native_greedy", "model": shape.name, "layers": shape.n_layers, "prompt": n_prompt,
+                   "greedy_tokens": n_new, "prefill_s": round(float(secs[0]), 4),
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "float_order": None if is_ref else args.float_order,
+                   "path": "reference runtime, unchanged, CPU" if is_ref else
+                           "reference runtime + integration/edgexpu_b200.patch + host shim, linear and logits on B200"},
+        "e2e": {"value": round(tot, 3), "unit": "tok/s", "h2d_bytes_per_step": 0 if is_ref else
+                4 * shape.n_layers * (4 * shape.n_embd + shape.n_ff) + 4 * shape.n_embd,
+                "d2h_bytes_per_step": 0 if is_ref else
+                4 * shape.n_layers * (2 * shape.n_embd + 2 * shape.n_kv_heads * shape.head_dim + 2 * shape.n_ff) + 8},
+    }
+    if is_ref:
+        line["impl"] = "reference"
+        line["cpu_baseline"] = {"value": round(tok_s, 3), "unit": "tok/s", "cores": host_threads(), "kind": "reference",
+                                "sample": f"{n_new} greedy tokens after a {n_prompt}-token prompt"}
+    else:
+        line["roofline"] = {"bound": "hbm", "achieved": round(wb / (secs[1] / n_new) / 1e9, 1), "peak": peak,
+                            "unit": "GB/s", "frac": round(wb / (secs[1] / n_new) / 1e9 / peak, 4),
+                            "note": "weight bytes per token / wall time per token: the host layer loop and one "
+                                    "synchronous call per projection bound this path, not the kernels",
+                            "peak_source": f"{peak_kind} hbm_gbs"}
+        line["config"]["l2"] = "no flush: the weights of one token exceed L2 for llama3 and fit it for smollm2"
+        line["cpu_baseline"] = ref_line
+        # one fused quantize+GEMV launch per projection (7 per layer at batch 1) and one logits launch
+        line["gpu_launches"] = n_new * (7 * shape.n_layers + 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def torch_all_sum(v, world):
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t)
+    return float(t.item())
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gemv", "llama3_8b_q4k_prefill"],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gemv", "llama3_8b_q4k_prefill", "native_greedy"],
                     default="llama3_8b_q4k_decode")
     ap.add_argument("--wtype", choices=["q4_k", "q8_0"], default="q4_k", help="gemv workload: weight type")
     ap.add_argument("--shape", default="14336,4096", help="gemv workload: n_out,n_in")
@@ -1149,6 +1276,8 @@ def main():
     ap.add_argument("--ref-layers", type=int, default=0,
                     help="reference arm: layers per step (0 = a sample of about 0.6 GB per step)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model", choices=["smollm2", "llama3"], default="smollm2", help="native_greedy workload: model")
+    ap.add_argument("--prompt", type=int, default=0, help="native_greedy workload: prompt ids (128 / 512 by model)")
     ap.add_argument("--float-order", choices=["x86", "relaxed"], default="relaxed",
                     help="relaxed: the GEMV's own summation order, within 1e-5 * sum|w x| of the reference; x86: float "
                          "outputs bit-identical to the reference's x86 build (the library's default order, the one "
@@ -1162,6 +1291,11 @@ def main():
         args.batch = 2048 if args.workload == "llama3_8b_q4k_prefill" else 1
     if args.workload == "llama3_8b_q4k_prefill":
         (run_prefill_reference if args.impl == "reference" else run_prefill)(args)
+        return
+    if args.workload == "native_greedy":
+        if args.float_order == "relaxed" and "--float-order" not in sys.argv:
+            args.float_order = "x86"  # the token-identical order is this workload's point
+        run_native(args)
         return
     if args.workload == "gemv":
         if args.impl == "reference":
