@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -50,6 +52,12 @@ struct Ctx {
   uint32_t* d_status = nullptr;
   unsigned long long* h_key = nullptr;
   uint32_t* h_status = nullptr;
+  // Mapped pinned buffer of the synchronous host-buffer calls (zerocopy.cu): control words
+  // [sequence, status] at 0, then the call's inputs and outputs at 256-byte aligned offsets.
+  uint8_t* zc_h = nullptr;
+  uint8_t* zc_d = nullptr;  // the same buffer's device address
+  size_t zc_cap = 0;
+  uint32_t zc_seq = 0;
 };
 
 Ctx g;
@@ -145,6 +153,54 @@ int grow_host(HostBuf& b, size_t need, char* error, size_t error_size) {
   EX_CUDA(cudaHostAlloc(&b.p, cap, cudaHostAllocDefault), error, error_size);
   b.cap = cap;
   return 1;
+}
+
+size_t al256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+int grow_zc(size_t need, char* error, size_t error_size) {
+  if (g.zc_cap >= need) return 1;
+  size_t cap = std::max<size_t>(need, 2 * g.zc_cap);
+  cap = (cap + 65535) & ~static_cast<size_t>(65535);
+  if (g.zc_h != nullptr) {
+    EX_CUDA(cudaDeviceSynchronize(), error, error_size);
+    cudaFreeHost(g.zc_h);
+  }
+  g.zc_h = g.zc_d = nullptr;
+  g.zc_cap = 0;
+  EX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&g.zc_h), cap, cudaHostAllocMapped), error, error_size);
+  EX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&g.zc_d), g.zc_h, 0), error, error_size);
+  std::memset(g.zc_h, 0, 256);
+  g.zc_cap = cap;
+  return 1;
+}
+
+int check_status(char* error, size_t error_size);
+
+// Launch the finish kernel for the call's outputs (n floats at src -> offset `off` of the mapped
+// buffer) and wait until its sequence number arrives.  The wait is bounded: the stream is
+// polled for errors every ~1000 spins, and after 60 s the call fails.
+int zc_finish_and_wait(const float* src, int n, size_t off, cudaStream_t st, char* error, size_t error_size) {
+  if (++g.zc_seq == 0) g.zc_seq = 1;
+  const uint32_t seq = g.zc_seq;
+  EX_CUDA(ex::launch_zc_finish(src, reinterpret_cast<float*>(g.zc_d + off), n, g.d_status,
+                               reinterpret_cast<uint32_t*>(g.zc_d), seq, st),
+          error, error_size);
+  volatile uint32_t* ctrl = reinterpret_cast<volatile uint32_t*>(g.zc_h);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (unsigned it = 1;; ++it) {
+    if (ctrl[0] == seq) break;
+    if ((it & 1023) == 0) {
+      const cudaError_t e = cudaStreamQuery(st);
+      if (e != cudaSuccess && e != cudaErrorNotReady) return fail(error, error_size, "device work failed: %s", cudaGetErrorString(e));
+      if (e == cudaSuccess && ctrl[0] != seq) return fail(error, error_size, "the call's completion word did not arrive");
+      if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(60)) {
+        return fail(error, error_size, "the call did not complete within 60 s");
+      }
+    }
+  }
+  std::atomic_thread_fence(std::memory_order_acquire);
+  *g.h_status = ctrl[1];
+  return check_status(error, error_size);
 }
 
 // Find the registered tensor holding rows [weight, weight + n_out rows) of width n_in.
@@ -390,6 +446,7 @@ int edgexpu_cuda_shutdown(void) {
   cudaFree(g.d_status);
   cudaFreeHost(g.h_key);
   cudaFreeHost(g.h_status);
+  if (g.zc_h != nullptr) cudaFreeHost(g.zc_h);
   cudaStreamDestroy(g.stream);
   g = Ctx{};
   return 1;
@@ -487,6 +544,24 @@ int edgexpu_cuda_linear_quant_batch(float* out, const float* x, const uint8_t* w
   cudaStream_t st = g.stream;
   const size_t xb = static_cast<size_t>(m) * n_in * 4, ob = static_cast<size_t>(m) * n_out * 4;
   const size_t bb = bias != nullptr ? static_cast<size_t>(n_out) * 4 : 0;
+  if (al256(xb) + bb <= ex::ZC_MAX_BYTES && ob <= ex::ZC_MAX_BYTES) {
+    // Decode-sized call: inputs pulled from and outputs pushed to the mapped buffer by kernels.
+    const size_t xoff = 256, ooff = xoff + al256(al256(xb) + bb);
+    if (!grow_zc(ooff + al256(ob), error, error_size) || !grow_dev(g.x, al256(xb) + bb + 64, st, error, error_size) ||
+        !grow_dev(g.out, ob, st, error, error_size))
+      return 0;
+    std::memcpy(g.zc_h + xoff, x, xb);
+    if (bb) std::memcpy(g.zc_h + xoff + al256(xb), bias, bb);
+    float* xd = static_cast<float*>(g.x.p);
+    EX_CUDA(ex::launch_zc_pull(reinterpret_cast<const float*>(g.zc_d + xoff), xd, static_cast<int>((al256(xb) + bb) / 4), st),
+            error, error_size);
+    if (!run_linear_dev(static_cast<float*>(g.out.p), xd, weight, type, bb ? xd + al256(xb) / 4 : nullptr, m, n_out,
+                        n_in, st, error, error_size))
+      return 0;
+    if (!zc_finish_and_wait(static_cast<const float*>(g.out.p), m * n_out, ooff, st, error, error_size)) return 0;
+    std::memcpy(out, g.zc_h + ooff, ob);
+    return 1;
+  }
   if (!grow_host(g.hx, xb, error, error_size) || !grow_dev(g.x, xb, st, error, error_size) ||
       !grow_host(g.hout, ob, error, error_size) || !grow_dev(g.out, ob, st, error, error_size))
     return 0;
@@ -514,20 +589,36 @@ int edgexpu_cuda_logits_argmax(const uint8_t* weight, uint32_t type, const float
   if (hidden == nullptr || token_id == nullptr || n_embd <= 0 || vocab <= 0) return fail(error, error_size, "invalid arguments");
   cudaStream_t st = g.stream;
   const size_t hb = static_cast<size_t>(n_embd) * 4, bb = bias != nullptr ? static_cast<size_t>(vocab) * 4 : 0;
-  if (!grow_host(g.hx, hb, error, error_size) || !grow_dev(g.x, hb, st, error, error_size)) return 0;
-  if (bb && (!grow_host(g.hbias, bb, error, error_size) || !grow_dev(g.bias, bb, st, error, error_size))) return 0;
-  std::memcpy(g.hx.p, hidden, hb);
-  EX_CUDA(cudaMemcpyAsync(g.x.p, g.hx.p, hb, cudaMemcpyHostToDevice, st), error, error_size);
-  if (bb) {
-    std::memcpy(g.hbias.p, bias, bb);
-    EX_CUDA(cudaMemcpyAsync(g.bias.p, g.hbias.p, bb, cudaMemcpyHostToDevice, st), error, error_size);
+  unsigned long long key = 0;
+  if (al256(hb) + bb <= ex::ZC_MAX_BYTES) {  // through the mapped buffer (zerocopy.cu)
+    const size_t xoff = 256, koff = xoff + al256(al256(hb) + bb);
+    if (!grow_zc(koff + 256, error, error_size) || !grow_dev(g.x, al256(hb) + bb + 64, st, error, error_size)) return 0;
+    std::memcpy(g.zc_h + xoff, hidden, hb);
+    if (bb) std::memcpy(g.zc_h + xoff + al256(hb), bias, bb);
+    float* xd = static_cast<float*>(g.x.p);
+    EX_CUDA(ex::launch_zc_pull(reinterpret_cast<const float*>(g.zc_d + xoff), xd, static_cast<int>((al256(hb) + bb) / 4), st),
+            error, error_size);
+    if (!run_logits_dev(weight, type, xd, n_embd, vocab, bb ? xd + al256(hb) / 4 : nullptr, 0, g.d_key, st, error,
+                        error_size))
+      return 0;
+    if (!zc_finish_and_wait(reinterpret_cast<const float*>(g.d_key), 2, koff, st, error, error_size)) return 0;
+    std::memcpy(&key, g.zc_h + koff, 8);
+  } else {
+    if (!grow_host(g.hx, hb, error, error_size) || !grow_dev(g.x, hb, st, error, error_size)) return 0;
+    if (bb && (!grow_host(g.hbias, bb, error, error_size) || !grow_dev(g.bias, bb, st, error, error_size))) return 0;
+    std::memcpy(g.hx.p, hidden, hb);
+    EX_CUDA(cudaMemcpyAsync(g.x.p, g.hx.p, hb, cudaMemcpyHostToDevice, st), error, error_size);
+    if (bb) {
+      std::memcpy(g.hbias.p, bias, bb);
+      EX_CUDA(cudaMemcpyAsync(g.bias.p, g.hbias.p, bb, cudaMemcpyHostToDevice, st), error, error_size);
+    }
+    if (!run_logits_dev(weight, type, static_cast<const float*>(g.x.p), n_embd, vocab,
+                        bb ? static_cast<const float*>(g.bias.p) : nullptr, 0, g.d_key, st, error, error_size))
+      return 0;
+    EX_CUDA(cudaMemcpyAsync(g.h_key, g.d_key, 8, cudaMemcpyDeviceToHost, st), error, error_size);
+    if (!sync_and_check(st, error, error_size)) return 0;
+    key = *g.h_key;
   }
-  if (!run_logits_dev(weight, type, static_cast<const float*>(g.x.p), n_embd, vocab,
-                      bb ? static_cast<const float*>(g.bias.p) : nullptr, 0, g.d_key, st, error, error_size))
-    return 0;
-  EX_CUDA(cudaMemcpyAsync(g.h_key, g.d_key, 8, cudaMemcpyDeviceToHost, st), error, error_size);
-  if (!sync_and_check(st, error, error_size)) return 0;
-  const unsigned long long key = *g.h_key;
   *token_id = edgexpu_cuda_argmax_key_id(key);
   if (best_score != nullptr) {
     uint32_t u = static_cast<uint32_t>(key >> 32);

@@ -24,6 +24,17 @@ cudaError_t launch_dot_f32(uint32_t type, const uint8_t* w, size_t row_bytes, in
 //   atomicMax of argmax_key(scores[i], row0 + i) over i < n into *key (the caller zeroes *key).
 cudaError_t launch_argmax_key(const float* scores, int n, long long row0, unsigned long long* key, cudaStream_t st);
 
+// Synchronous host-buffer calls through one mapped pinned buffer (zerocopy.cu).
+constexpr int ZC_FINISH_THREADS = 128;  // small enough to share an SM with a running GEMV CTA
+constexpr int ZC_PULL_MAX_CTAS = 16;
+constexpr size_t ZC_MAX_BYTES = 256 * 1024;  // per direction; larger calls use copy-engine transfers
+//   dst[0 .. n) = src[0 .. n): src in mapped host memory, both 16-byte aligned.
+cudaError_t launch_zc_pull(const float* src, float* dst, int n, cudaStream_t st);
+//   After the previous grid completes: dst[0 .. n) = src[0 .. n) (dst in mapped host memory),
+//   ctrl[1] = *d_status (and *d_status = 0), then ctrl[0] = seq.
+cudaError_t launch_zc_finish(const float* src, float* dst, int n, uint32_t* d_status, uint32_t* ctrl, uint32_t seq,
+                             cudaStream_t st);
+
 // What the row-stream kernel does with each finished row.
 enum class RowOut : int {
   Store = 0,     // out[t*out_stride + r] = bias[r] + dot

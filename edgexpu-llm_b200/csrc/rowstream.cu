@@ -66,7 +66,9 @@ cudaError_t launch_rowstream(const RowStreamArgs& in, const DeviceInfo& dev, cud
     L.n_tiles += (a.seg[i].n_rows + L.tile_rows - 1) / L.tile_rows;
   }
   L.act_off = BAR_BYTES;
-  L.stage_off = L.act_off + act;
+  L.part_off = L.act_off + act;
+  const int part = rowstream_sliced(a) ? (MAX_STAGES * L.tile_rows * (SLICE_UNITS * 4 + 4) + 127) & ~127 : 0;
+  L.stage_off = L.part_off + part;
   int S = (dev.max_smem_optin - L.stage_off) / L.stage_bytes;
   if (S > MAX_STAGES) S = MAX_STAGES;
   if (S < 2) return cudaErrorInvalidConfiguration;

@@ -46,10 +46,20 @@ struct Layout {
   int stage_off;
   int smem_total;
   int row_stride;  // bytes between rows in a stage: row_bytes, or padded (each row its own copy)
+  int part_off;    // sliced rows: per-(stage, row) slice partials and arrival counters
 };
 
 // Launches the formats of the other GGUF types (rowstream_more.cu).
 cudaError_t launch_rowstream_more(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st);
+
+// Q4_K rows longer than one warp pass (K > 4096) at batch 1 in the relaxed order run sliced: each
+// consumer warp keeps 16 units' activations in registers and computes that slice of two rows at
+// a time (rowstream_kernel, SLICE).  At most 15 slices: K <= 30720.
+inline bool rowstream_sliced(const RowStreamArgs& a) {
+  const int U = a.K / 128;
+  return a.fmt == Fmt::Q4_KxQ8_K && a.m == 1 && !a.exact && (a.mode == RowOut::Store || a.mode == RowOut::Argmax) &&
+         U > 32 && (U + 15) / 16 <= 15;
+}
 
 namespace {
 
@@ -68,6 +78,7 @@ constexpr int STAGE_SLACK = 48;       // alignment round-down (<16) + over-read 
 constexpr int MAX_M = 8;              // activation rows (tokens) per launch; the host splits more
 constexpr int PROLOGUE_QUANT_MAX_M = 2;
 constexpr int PRO_BATCH = 4;          // activation blocks a consumer warp loads before quantizing them
+constexpr int SLICE_UNITS = 16;       // sliced rows: units per slice (half a warp)
 #ifndef EX_RS_PRE
 #define EX_RS_PRE 2
 #endif
@@ -1414,8 +1425,10 @@ __device__ void tp_finalize(const RowStreamArgs& a, const Layout& L, uint32_t e,
   }
 }
 
-template <Fmt F, RowOut MODE, int MTOK, bool XREG, bool EXACT>
+template <Fmt F, RowOut MODE, int MTOK, bool XREG, bool EXACT, bool SLICE>
 __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamArgs a, const Layout L) {
+  static_assert(!SLICE || (F == Fmt::Q4_KxQ8_K && MTOK == 1 && !XREG && !EXACT &&
+                           (MODE == RowOut::Store || MODE == RowOut::Argmax)), "sliced rows: Q4_K, batch 1");
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAX_STAGES;
@@ -1438,6 +1451,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
     }
     mbar_init(xin, CONSUMER_WARPS);
     *abort_flag = 0;
+    if constexpr (SLICE) {
+      int* cnt = reinterpret_cast<int*>(smem + L.part_off + MAX_STAGES * R * SLICE_UNITS * 4);
+      for (int i = 0; i < MAX_STAGES * R; ++i) cnt[i] = 0;
+    }
     fence_mbar_init();
   }
   __syncthreads();
@@ -1514,7 +1531,74 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   bool dead = false;
   int s = 0;
   uint32_t fphase = 0;
-  if constexpr (EXACT) {
+  if constexpr (SLICE) {
+    // Long Q4_K rows at batch 1 (U > 32 units): the row is cut into NSL slices of 16 units.  Warp cw
+    // owns slice sl = cw % NSL for good, so the activations of its lane's unit stay in registers,
+    // and takes the row pairs p = j, j + G, ... of every tile (j = cw / NSL): half-warp h computes
+    // row 2p + h.  The slice partials of a row meet in shared memory; the warp that adds the
+    // last one sums them in slice order (a fixed order: deterministic results) and stores.
+    const int U = a.K / 128;
+    const int NSL = (U + SLICE_UNITS - 1) / SLICE_UNITS;
+    const int G = CONSUMER_WARPS / NSL;
+    const int sl = cw % NSL, j = cw / NSL;
+    const int h = lane >> 4;
+    const int u = sl * SLICE_UNITS + (lane & (SLICE_UNITS - 1));
+    const bool unit_live = u < U;
+    const int ue = unit_live ? u : 0;  // dead lanes read a valid unit and contribute 0
+    load_xregs(F, a, act, ue, xr);
+    const Q4kLane ql = q4k_lane(ue);
+    float* part = reinterpret_cast<float*>(smem + L.part_off);
+    int* cnt = reinterpret_cast<int*>(smem + L.part_off + MAX_STAGES * R * SLICE_UNITS * 4);
+    for (long long tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
+      if (!dead && !wait_or_abort(&full[s], fphase, abort_flag)) {
+        atomicOr(a.status, ST_TIMEOUT_FULL);
+        *abort_flag = 1;
+        dead = true;
+      }
+      if (!dead && j < G) {
+        const TileDesc tr = descs[s];
+        const uint8_t* tb = smem + L.stage_off + s * L.stage_bytes + tr.misalign;
+        const int pairs = (tr.nr + 1) >> 1;
+        for (int p = j; p < pairs; p += G) {
+          const int r = 2 * p + h;
+          const bool valid = r < tr.nr;
+          float v = 0.0f;
+          row_q4k_full(tb + static_cast<size_t>(valid ? r : 0) * a.row_bytes, v, xr, ql);
+          v = unit_live ? v : 0.0f;
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+          int last = 0;
+          if ((lane & 15) == 0 && valid) {
+            volatile float* pr = part + (s * R + r) * SLICE_UNITS;
+            pr[sl] = v;
+            __threadfence_block();
+            last = atomicAdd(cnt + s * R + r, 1) == NSL - 1;
+            if (last) {
+              __threadfence_block();
+              float y = pr[0];
+              for (int q = 1; q < NSL; ++q) y += pr[q];
+              cnt[s * R + r] = 0;
+              const long long row = static_cast<long long>(tr.r0) + r;
+              if constexpr (MODE == RowOut::Store) {
+                tr.out[row] = (tr.bias != nullptr ? tr.bias[row] : 0.0f) + y;  // cpu_kernel.c:596-597
+              } else {
+                const float sc = tr.bias != nullptr ? tr.bias[row] + y : y;
+                const unsigned long long k = argmax_key(sc, static_cast<uint32_t>(a.row0 + row));
+                best = k > best ? k : best;
+              }
+            }
+          }
+        }
+      }
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == S) {
+        s = 0;
+        fphase ^= 1u;
+      }
+    }
+  } else if constexpr (EXACT) {
     // Exact mode: slot g of a tile is rows EX_ROWS*g .. EX_ROWS*g + EX_ROWS-1; slot g belongs to
     // consumer warp (it*G + g) % CONSUMER_WARPS.  Lane EX_LPR*r + c runs accumulators 2c, 2c+1 of row
     // EX_ROWS*g + r (the x86 float order).
@@ -1660,10 +1744,10 @@ __global__ void __launch_bounds__(THREADS, 1) rowstream_kernel(const RowStreamAr
   }
 }
 
-template <Fmt F, RowOut MODE, int MTOK, bool XREG = false, bool EXACT = false>
+template <Fmt F, RowOut MODE, int MTOK, bool XREG = false, bool EXACT = false, bool SLICE = false>
 cudaError_t launch_impl(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
   static int configured_smem = 0;  // per instantiation; the host API serialises its callers
-  auto kern = rowstream_kernel<F, MODE, MTOK, XREG, EXACT>;
+  auto kern = rowstream_kernel<F, MODE, MTOK, XREG, EXACT, SLICE>;
   if (L.smem_total > configured_smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L.smem_total);
     if (e != cudaSuccess) return e;
@@ -1701,6 +1785,9 @@ cudaError_t launch_mtok(const RowStreamArgs& a, const Layout& L, int grid, cudaS
   }
   if constexpr (F == Fmt::Q8_0xQ8_0 || F == Fmt::Q4_KxQ8_K) {  // activations held in registers
     if (a.m == 1 && units_per_row(F, a.K) <= 32) return launch_impl<F, MODE, 1, true>(a, L, grid, st);
+  }
+  if constexpr (F == Fmt::Q4_KxQ8_K && (MODE == RowOut::Store || MODE == RowOut::Argmax)) {
+    if (rowstream_sliced(a)) return launch_impl<F, MODE, 1, false, false, true>(a, L, grid, st);
   }
   if (a.m <= 1) return launch_impl<F, MODE, 1>(a, L, grid, st);
   if (a.m <= 2) return launch_impl<F, MODE, 2>(a, L, grid, st);

@@ -140,11 +140,27 @@ LINEAR_CASES = [
     # rows longer than a 32 KB stage -> one-row tiles: each warp owns every 15th tile and skips the
     # rest, so it can reach a stage's next fill before the previous one landed (~28 tiles per CTA)
     (TYPE_Q8_0, 4096, 16384, 1, False),
+    # Q4_K rows of more than 32 units at batch 1 (relaxed order: sliced rows): 7 full slices, a
+    # partly filled last slice (K = 7168, 11008), an odd tile height, and 15 slices (K = 30720)
+    (TYPE_Q4_K, 4096, 14336, 1, True),
+    (TYPE_Q4_K, 777, 7168, 1, False),
+    (TYPE_Q4_K, 301, 11008, 1, True),
+    (TYPE_Q4_K, 95, 30720, 1, False),
 ]
 
 
+@pytest.fixture(params=["x86", "relaxed"])
+def order(request, gpu):
+    """Both float orders of the library: the x86 order (the default) and the relaxed order, whose
+    kernels differ (sliced rows for K > 4096 at batch 1, the tensor-core GEMM for Q4_K prefill)."""
+    cuda = gpu.load_cuda()
+    assert cuda.edgexpu_cuda_set_float_order(gpu.ORDER_X86 if request.param == "x86" else gpu.ORDER_RELAXED) == 1
+    yield request.param
+    cuda.edgexpu_cuda_set_float_order(gpu.ORDER_X86)
+
+
 @pytest.mark.parametrize("wtype,n_out,n_in,m,with_bias", LINEAR_CASES)
-def test_linear_quant_batch_matches_oracle(gpu, port, wtype, n_out, n_in, m, with_bias):
+def test_linear_quant_batch_matches_oracle(gpu, port, wtype, n_out, n_in, m, with_bias, order):
     s = _synth()
     rng = np.random.default_rng(n_out * 31 + n_in + m)
     w = s.weight(rng, wtype, n_out, n_in)
