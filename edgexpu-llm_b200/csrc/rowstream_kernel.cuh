@@ -8,7 +8,7 @@
 // and three epilogues: store rows (cpu_kernel.c:545-644), greedy argmax over rows
 // (native.c:2355-2397), or per-block int32 partials (test hook for bit-exactness).
 //
-// Design (HBM-bound streaming, batch 1-8):
+// Design (HBM-bound streaming, batch 1-16):
 //   * grid = one CTA per SM (persistent); CTA c takes tiles c, c+grid, ...; a tile is R whole
 //     rows, i.e. one contiguous byte range (up to 32 KB) of the row-major GGUF tensor.
 //   * warp 0, lane 0 is the producer: it moves each tile into a ring of shared-memory stages
@@ -75,7 +75,7 @@ constexpr int BAR_BYTES = 1024;       // full[16], empty[16], abort flag, xin ba
 constexpr int DESC_OFF = 512;
 constexpr int ACT_BUDGET = 96 * 1024;
 constexpr int STAGE_SLACK = 48;       // alignment round-down (<16) + over-read of the last block
-constexpr int MAX_M = 8;              // activation rows (tokens) per launch; the host splits more
+constexpr int MAX_M = 16;             // activation rows (tokens) per launch; the host splits more
 constexpr int PROLOGUE_QUANT_MAX_M = 2;
 constexpr int PRO_BATCH = 4;          // activation blocks a consumer warp loads before quantizing them
 constexpr int SLICE_UNITS = 16;       // sliced rows: units per slice (half a warp)
@@ -1773,7 +1773,8 @@ cudaError_t launch_exact(const RowStreamArgs& a, const Layout& L, int grid, cuda
   if constexpr (MODE == RowOut::Store) {
     if (a.m <= 2) return launch_impl<F, MODE, 2, false, true>(a, L, grid, st);
     if (a.m <= 4) return launch_impl<F, MODE, 4, false, true>(a, L, grid, st);
-    return launch_impl<F, MODE, 8, false, true>(a, L, grid, st);
+    if (a.m <= 8) return launch_impl<F, MODE, 8, false, true>(a, L, grid, st);
+    return launch_impl<F, MODE, 16, false, true>(a, L, grid, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -1792,7 +1793,8 @@ cudaError_t launch_mtok(const RowStreamArgs& a, const Layout& L, int grid, cudaS
   if (a.m <= 1) return launch_impl<F, MODE, 1>(a, L, grid, st);
   if (a.m <= 2) return launch_impl<F, MODE, 2>(a, L, grid, st);
   if (a.m <= 4) return launch_impl<F, MODE, 4>(a, L, grid, st);
-  return launch_impl<F, MODE, 8>(a, L, grid, st);
+  if (a.m <= 8) return launch_impl<F, MODE, 8>(a, L, grid, st);
+  return launch_impl<F, MODE, 16>(a, L, grid, st);
 }
 
 }  // namespace
