@@ -38,6 +38,18 @@ _c_sz = ctypes.c_size_t
 _c_int = ctypes.c_int
 _c_u32 = ctypes.c_uint32
 _c_str = ctypes.c_char_p
+_c_u64 = ctypes.c_uint64
+_c_i64p = ctypes.POINTER(ctypes.c_int64)
+_c_u64p = ctypes.POINTER(ctypes.c_uint64)
+
+
+class HbmPlan(ctypes.Structure):
+    """edgexpu_cuda_hbm_plan (include/edgexpu_cuda.h)."""
+
+    _fields_ = [("weight_bytes", ctypes.c_uint64), ("kv_bytes", ctypes.c_uint64), ("scratch_bytes", ctypes.c_uint64),
+                ("total_bytes", ctypes.c_uint64), ("limit_bytes", ctypes.c_uint64), ("file_bytes", ctypes.c_uint64),
+                ("window", ctypes.c_int), ("admitted", ctypes.c_int), ("reason", ctypes.c_char * 256)]
+
 
 _CUDA_SIGS = {
     "edgexpu_cuda_abi_version": (_c_int, []),
@@ -74,9 +86,18 @@ _CUDA_SIGS = {
     "edgexpu_cuda_tp_shutdown": (_c_int, []),
     "edgexpu_cuda_linear_quant_batch_tp_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int,
                                                         _c_vp]),
+    "edgexpu_cuda_hbm_plan_native": (_c_int, [_c_u64, _c_u64, _c_u32, _c_u32, _c_int, _c_u32, _c_u32, _c_u32, _c_int,
+                                              _c_u64, ctypes.POINTER(HbmPlan)]),
+    "edgexpu_cuda_gguf_load": (_c_int, [_c_str, _c_int, ctypes.POINTER(_c_vp), ctypes.POINTER(HbmPlan), _c_str, _c_sz]),
+    "edgexpu_cuda_gguf_tensor_count": (_c_int, [_c_vp]),
+    "edgexpu_cuda_gguf_tensor_at": (_c_int, [_c_vp, _c_int, ctypes.POINTER(_c_str), ctypes.POINTER(_c_vp),
+                                             ctypes.POINTER(_c_u32), _c_i64p, _c_i64p, _c_u64p, _c_u64p]),
+    "edgexpu_cuda_gguf_find": (_c_int, [_c_vp, _c_str]),
+    "edgexpu_cuda_gguf_free": (_c_int, [_c_vp]),
 }
 
 _HOST_SIGS = {
+    "edgexpu_b200_preload": (_c_int, [_c_vp, _c_sz, _c_str, _c_int, _c_str, _c_sz]),
     "edgexpu_cpu_linear_quant": (None, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int]),
     "edgexpu_cpu_linear_quant_batch": (None, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int]),
     "edgexpu_gguf_q8_0_nbytes": (_c_sz, [_c_int]),

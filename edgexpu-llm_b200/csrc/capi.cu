@@ -871,6 +871,7 @@ int api_fail(char* error, size_t error_size, const char* fmt, ...) {
 const DeviceInfo& api_device_info() { return g.info; }
 int api_device() { return g.device; }
 bool api_exact_order() { return exact_order(); }
+cudaStream_t api_stream() { return g.stream; }
 uint32_t* api_status_word() { return g.d_status; }
 size_t api_row_bytes(uint32_t type, int n) { return row_bytes_of(type, n); }
 size_t api_act_row_bytes(uint32_t type, int n) { return act_row_bytes_of(type, n); }

@@ -65,6 +65,8 @@ int api_device();
 // True when float outputs follow the reference x86 build's order (EDGEXPU_CUDA_ORDER_X86).
 bool api_exact_order();
 uint32_t* api_status_word();
+// The library's stream (the one every synchronous entry point uses).
+cudaStream_t api_stream();
 size_t api_row_bytes(uint32_t type, int n);
 size_t api_act_row_bytes(uint32_t type, int n);
 // Device scratch of at least `bytes` (the library's activation buffer, grown outside stream capture).

@@ -59,11 +59,20 @@ typedef struct {
     uint32_t type;
     int n_out;
     int n_in;
+    int preloaded; /* part of a model loaded by edgexpu_b200_preload: freed with the model */
 } resident_entry;
 
 static resident_entry *g_res;
 static size_t g_res_cap;
 static size_t g_res_used;
+
+/* Models loaded by edgexpu_b200_preload, by the host range of their file mapping. */
+#define MAX_PRELOADED 16
+static struct {
+    const uint8_t *base;
+    size_t size;
+    void *model;
+} g_models[MAX_PRELOADED];
 
 static size_t res_slot(const uint8_t *host) {
     uint64_t h = (uint64_t)(uintptr_t)host;
@@ -96,6 +105,36 @@ static int res_grow(void) {
     }
     free(old);
     return 1;
+}
+
+/* Insert host -> dev (the table has room: callers grow it first). */
+static void res_insert(const uint8_t *host, const uint8_t *dev, size_t nbytes, uint32_t type, int n_out, int n_in,
+                       int preloaded) {
+    size_t k = res_slot(host);
+    while (g_res[k].host != NULL) {
+        k = (k + 1) & (g_res_cap - 1);
+    }
+    g_res[k].host = host;
+    g_res[k].dev = dev;
+    g_res[k].nbytes = nbytes;
+    g_res[k].type = type;
+    g_res[k].n_out = n_out;
+    g_res[k].n_in = n_in;
+    g_res[k].preloaded = preloaded;
+    g_res_used++;
+}
+
+static int res_find(const uint8_t *host) {
+    size_t k;
+    if (g_res_cap == 0) {
+        return 0;
+    }
+    for (k = res_slot(host); g_res[k].host != NULL; k = (k + 1) & (g_res_cap - 1)) {
+        if (g_res[k].host == host) {
+            return 1;
+        }
+    }
+    return 0;
 }
 
 /* Binds the library to EDGEXPU_B200_DEVICE (default 0) on first use; edgexpu_cuda_init returns 1
@@ -142,18 +181,52 @@ const uint8_t *edgexpu_b200_resident(const uint8_t *host, size_t nbytes, uint32_
     if (!edgexpu_cuda_upload_weight(host, nbytes, type, n_out, n_in, &dev, error, error_size)) {
         return NULL;
     }
-    k = res_slot(host);
-    while (g_res[k].host != NULL) {
-        k = (k + 1) & (g_res_cap - 1);
-    }
-    g_res[k].host = host;
-    g_res[k].dev = dev;
-    g_res[k].nbytes = nbytes;
-    g_res[k].type = type;
-    g_res[k].n_out = n_out;
-    g_res[k].n_in = n_in;
-    g_res_used++;
+    res_insert(host, dev, nbytes, type, n_out, n_in, 0);
     return dev;
+}
+
+int edgexpu_b200_preload(const uint8_t *file_map, size_t file_size, const char *path, int window, char *error,
+                         size_t error_size) {
+    void *model = NULL;
+    int i, n, slot = -1;
+    if (file_map == NULL || file_size == 0 || path == NULL) {
+        snprintf(error, error_size, "preload: invalid arguments");
+        return 0;
+    }
+    for (i = 0; i < MAX_PRELOADED; i++) {
+        if (g_models[i].model == NULL) {
+            slot = i;
+            break;
+        }
+    }
+    if (slot < 0) {
+        snprintf(error, error_size, "preload: more than %d models loaded", MAX_PRELOADED);
+        return 0;
+    }
+    if (!ensure_device(error, error_size) || !edgexpu_cuda_gguf_load(path, window, &model, NULL, error, error_size)) {
+        return 0;
+    }
+    n = edgexpu_cuda_gguf_tensor_count(model);
+    for (i = 0; i < n; i++) {
+        const uint8_t *dev = NULL;
+        uint32_t type = 0;
+        int64_t n_in = 0, n_out = 0;
+        uint64_t off = 0, nbytes = 0;
+        if (!edgexpu_cuda_gguf_tensor_at(model, i, NULL, &dev, &type, &n_in, &n_out, &off, &nbytes) || nbytes == 0 ||
+            off + nbytes > file_size || res_find(file_map + off)) {
+            continue;
+        }
+        if ((g_res_used + 1) * 2 > g_res_cap && !res_grow()) {
+            edgexpu_cuda_gguf_free(model);
+            snprintf(error, error_size, "preload: out of host memory");
+            return 0;
+        }
+        res_insert(file_map + off, dev, (size_t)nbytes, type, (int)n_out, (int)n_in, 1);
+    }
+    g_models[slot].base = file_map;
+    g_models[slot].size = file_size;
+    g_models[slot].model = model;
+    return 1;
 }
 
 void edgexpu_b200_release_range(const void *base, size_t size) {
@@ -161,12 +234,12 @@ void edgexpu_b200_release_range(const void *base, size_t size) {
     size_t i;
     resident_entry *old = g_res;
     size_t cap = g_res_cap;
-    if (base == NULL || size == 0 || cap == 0) {
+    if (base == NULL || size == 0) {
         return;
     }
     /* rebuild the table without the released entries (keeps the probe chains intact) */
-    g_res = (resident_entry *)calloc(cap, sizeof *g_res);
-    if (g_res == NULL) {
+    g_res = cap != 0 ? (resident_entry *)calloc(cap, sizeof *g_res) : NULL;
+    if (cap != 0 && g_res == NULL) {
         g_res = old;
         return;
     }
@@ -176,7 +249,9 @@ void edgexpu_b200_release_range(const void *base, size_t size) {
             continue;
         }
         if (old[i].host >= lo && old[i].host < lo + size) {
-            edgexpu_cuda_free_weight(old[i].dev);
+            if (!old[i].preloaded) {
+                edgexpu_cuda_free_weight(old[i].dev);
+            }
             continue;
         }
         {
@@ -189,9 +264,22 @@ void edgexpu_b200_release_range(const void *base, size_t size) {
         }
     }
     free(old);
+    for (i = 0; i < MAX_PRELOADED; i++) {
+        if (g_models[i].model != NULL && g_models[i].base >= lo && g_models[i].base < lo + size) {
+            edgexpu_cuda_gguf_free(g_models[i].model);
+            g_models[i].model = NULL;
+        }
+    }
 }
 
 void edgexpu_b200_shutdown(void) {
+    int i;
+    for (i = 0; i < MAX_PRELOADED; i++) {
+        if (g_models[i].model != NULL) {
+            edgexpu_cuda_gguf_free(g_models[i].model);
+            g_models[i].model = NULL;
+        }
+    }
     free(g_res);
     g_res = NULL;
     g_res_cap = 0;

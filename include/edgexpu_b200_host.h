@@ -73,8 +73,17 @@ void edgexpu_b200_shutdown(void);
  * and a message in `error` on failure, or when `host` was uploaded with another shape or type. */
 const uint8_t *edgexpu_b200_resident(const uint8_t *host, size_t nbytes, uint32_t type, int n_out, int n_in,
                                      char *error, size_t error_size);
-/* Frees the resident tensors whose host bytes lie in [base, base + size): the model file is being
- * unmapped (edgexpu_native_free, native.c:1203-1233), so a later mapping may reuse the addresses. */
+/* Called right after the model file is mapped (edgexpu_native_load, native.c:1282-1285): plans the
+ * HBM budget of the resident model for `window` positions (edgexpu_cuda_hbm_plan_native: 85 % of
+ * HBM, the analogue of admit_session_window native.c:79-92), streams the file's data section into
+ * HBM in one pass (edgexpu_cuda_gguf_load), and enters every tensor into the residency table under
+ * its address in the mapping [file_map, file_map + file_size), so edgexpu_b200_resident finds it
+ * without a copy.  1 on success; 0 and a message in `error` (the budget's reason on refusal). */
+int edgexpu_b200_preload(const uint8_t *file_map, size_t file_size, const char *path, int window, char *error,
+                         size_t error_size);
+/* Frees the resident tensors whose host bytes lie in [base, base + size), and the models preloaded
+ * from a mapping there: the model file is being unmapped (edgexpu_native_free, native.c:1203-1233),
+ * so a later mapping may reuse the addresses. */
 void edgexpu_b200_release_range(const void *base, size_t size);
 /* Sticky message of the first failure since the last clear ("" if none). */
 const char *edgexpu_b200_last_error(void);

@@ -216,6 +216,46 @@ int edgexpu_cuda_tp_shutdown(void);
 int edgexpu_cuda_linear_quant_batch_tp_dev(float *out, const float *x, const uint8_t *weight, uint32_t type,
                                            const float *bias, int m, int n_out, int n_in, void *stream);
 
+/* ---- device-resident model: HBM budget and a GGUF file streamed into HBM --------------------
+ * The reference maps the file (src/native.c:115-163), copies each layer into a staging buffer on
+ * every use (stage_copy_bytes, native.c:350-380) and admits a model whose working set, KV cache
+ * and scratch fit 85 % of RAM (fill_native_plan, src/scheduler.c:320-422).  Here every tensor
+ * stays resident, so the plan's weight term is every tensor byte and its limit 85 % of HBM. */
+typedef struct edgexpu_cuda_hbm_plan {
+    uint64_t weight_bytes;   /* resident tensor bytes (the GGUF data section) */
+    uint64_t kv_bytes;       /* 2 * kv_layers * kv_heads * head_dim * window * 4 (scheduler.c:353-359) */
+    uint64_t scratch_bytes;  /* min(window, 64) positions of activations (scheduler.c:360-366) */
+    uint64_t total_bytes;
+    uint64_t limit_bytes;    /* floor(HBM MB * 85 / 100) MB */
+    uint64_t file_bytes;
+    int window;
+    int admitted;
+    char reason[256];
+} edgexpu_cuda_hbm_plan;
+/* Fill `plan` (the terms of fill_native_plan, scheduler.c:320-422, with the weight term and limit
+ * above); returns plan->admitted.  Host arithmetic only.  EDGEXPU_BUDGET_DISABLE admits anything,
+ * as in the reference; so does a memory size whose 85 % rounds to 0 MB ("device memory unknown"). */
+int edgexpu_cuda_hbm_plan_native(uint64_t file_bytes, uint64_t weight_bytes, uint32_t n_kv_layers, uint32_t n_kv_heads,
+                                 int head_dim, uint32_t n_embd, uint32_t n_ff, uint32_t n_heads, int window,
+                                 uint64_t hbm_total_bytes, edgexpu_cuda_hbm_plan *plan);
+/* Parse the GGUF file at `path` (src/gguf.c:359-610), plan its HBM budget for `window` positions
+ * (dimensions from the `<arch>.*` keys), and when admitted stream its data section into one HBM
+ * arena and register every tensor of a supported type (any row of it is then a valid `weight`).
+ * *model receives an opaque handle; `plan` (nullable) the budget, also on refusal (return 0,
+ * message = plan reason). */
+int edgexpu_cuda_gguf_load(const char *path, int window, void **model, edgexpu_cuda_hbm_plan *plan, char *error,
+                           size_t error_size);
+int edgexpu_cuda_gguf_tensor_count(const void *model);
+/* Tensor `index` of a loaded model: name, device address, GGUF type, row length (n_in), rows
+ * (product of the other dimensions), absolute file offset of its first byte, and its byte size
+ * (0 when the library does not read that type, so it is not registered). */
+int edgexpu_cuda_gguf_tensor_at(const void *model, int index, const char **name, const uint8_t **dev, uint32_t *type,
+                                int64_t *n_in, int64_t *n_out, uint64_t *file_offset, uint64_t *nbytes);
+/* Index of the tensor called `name`, or -1. */
+int edgexpu_cuda_gguf_find(const void *model, const char *name);
+/* Unregister the model's tensors and free its arena. */
+int edgexpu_cuda_gguf_free(void *model);
+
 /* Token id encoded in an argmax key (0 when no row had a finite score). */
 static inline uint32_t edgexpu_cuda_argmax_key_id(uint64_t key) {
     return key == 0 ? 0u : 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFu);
