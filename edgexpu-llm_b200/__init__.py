@@ -86,6 +86,10 @@ _CUDA_SIGS = {
     "edgexpu_cuda_tp_shutdown": (_c_int, []),
     "edgexpu_cuda_linear_quant_batch_tp_dev": (_c_int, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int,
                                                         _c_vp]),
+    "edgexpu_cuda_sample_softmax": (_c_int, [_c_vp, _c_int, ctypes.c_float, _c_u64p, ctypes.POINTER(_c_u32), _c_str,
+                                             _c_sz]),
+    "edgexpu_cuda_logits_sample": (_c_int, [_c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp, ctypes.c_float, ctypes.c_float,
+                                            _c_u64p, ctypes.POINTER(_c_u32), _c_str, _c_sz]),
     "edgexpu_cuda_hbm_plan_native": (_c_int, [_c_u64, _c_u64, _c_u32, _c_u32, _c_int, _c_u32, _c_u32, _c_u32, _c_int,
                                               _c_u64, ctypes.POINTER(HbmPlan)]),
     "edgexpu_cuda_gguf_load": (_c_int, [_c_str, _c_int, ctypes.POINTER(_c_vp), ctypes.POINTER(HbmPlan), _c_str, _c_sz]),
@@ -97,6 +101,8 @@ _CUDA_SIGS = {
 }
 
 _HOST_SIGS = {
+    "edgexpu_b200_logits_sample": (_c_int, [_c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_vp, ctypes.c_float, ctypes.c_float,
+                                            _c_u64p, ctypes.POINTER(_c_u32), _c_str, _c_sz]),
     "edgexpu_b200_preload": (_c_int, [_c_vp, _c_sz, _c_str, _c_int, _c_str, _c_sz]),
     "edgexpu_cpu_linear_quant": (None, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int]),
     "edgexpu_cpu_linear_quant_batch": (None, [_c_vp, _c_vp, _c_vp, _c_u32, _c_vp, _c_int, _c_int, _c_int]),

@@ -46,7 +46,7 @@ struct Ctx {
   cudaStream_t stream = nullptr;
   ex::DeviceInfo info{};
   std::map<uintptr_t, WeightRec> weights;
-  DevBuf x, xq, out, bias, wrow;
+  DevBuf x, xq, out, bias, wrow, samp, sstat;
   HostBuf hx, hout, hbias;
   unsigned long long* d_key = nullptr;
   uint32_t* d_status = nullptr;
@@ -361,6 +361,66 @@ int run_logits_dev(const uint8_t* weight, uint32_t type, const float* hidden, in
   return 1;
 }
 
+// Every logit score of the greedy/sampling path (native.c:500-514: dot + output bias) into
+// scores[vocab]: the GEMV of run_logits_dev in Store mode.
+int run_scores_dev(const uint8_t* weight, uint32_t type, const float* hidden, int n_embd, int vocab, const float* bias,
+                   float* scores, cudaStream_t st, char* error, size_t error_size) {
+  if (weight == nullptr || hidden == nullptr || scores == nullptr || n_embd <= 0 || vocab <= 0)
+    return fail(error, error_size, "invalid arguments");
+  if (!lookup(weight, type, vocab, n_embd, error, error_size)) return 0;
+  if (is_float_type(type)) {
+    EX_CUDA(ex::launch_dot_f32(type, weight, row_bytes_of(type, n_embd), vocab, n_embd, hidden, 1, bias, scores, st),
+            error, error_size);
+    return 1;
+  }
+  ex::RowStreamArgs a{};
+  a.mode = ex::RowOut::Store;
+  a.w = weight;
+  a.n_rows = vocab;
+  a.row_bytes = static_cast<int>(row_bytes_of(type, n_embd));
+  a.K = n_embd;
+  a.m = 1;
+  a.bias = bias;
+  a.out = scores;
+  a.out_stride = vocab;
+  a.status = g.d_status;
+  a.act = hidden;
+  a.act_f32 = true;
+  a.fmt = ex::logits_fmt(type);
+  a.exact = exact_order();
+  a.act_row_bytes = ex::acts_are_q8_0(type) ? static_cast<int>(act_row_bytes_of(type, n_embd)) : n_embd * 4;
+  if (ex::rowstream_max_m(a.fmt, n_embd, g.info) < 1) return fail(error, error_size, "n_embd %d too large", n_embd);
+  EX_CUDA(ex::launch_rowstream(a, g.info, st), error, error_size);
+  return 1;
+}
+
+// The reference's xorshift64 step and draw (cpu_kernel.c:780-785, :813 / :840).
+double sample_draw(uint64_t* rng) {
+  if (*rng == 0) *rng = 0x00ED6E50ULL;
+  *rng ^= *rng << 13;
+  *rng ^= *rng >> 7;
+  *rng ^= *rng << 17;
+  return static_cast<double>(*rng & 0xFFFFFFFu) / static_cast<double>(0x10000000u);
+}
+
+int sync_and_check(cudaStream_t st, char* error, size_t error_size);
+
+// Softmax of io[n] (divided by temperature first when > 0) and the draw, on the device; the id
+// into *out.  Synchronous.
+int sample_dev(float* io, int n, float temperature, float top_p, uint64_t* rng, uint32_t* out, cudaStream_t st,
+               char* error, size_t error_size) {
+  const double u = sample_draw(rng);
+  const size_t need = ex::sample_scratch_bytes(n);
+  if (!grow_dev(g.samp, need, st, error, error_size) || !grow_dev(g.sstat, 64, st, error, error_size)) return 0;
+  uint32_t* out_dev = static_cast<uint32_t*>(g.sstat.p);
+  double* stats = reinterpret_cast<double*>(static_cast<uint8_t*>(g.sstat.p) + 32);
+  EX_CUDA(ex::launch_sample(io, n, temperature, top_p, u, g.samp.p, g.samp.cap, out_dev, stats, st), error, error_size);
+  EX_CUDA(cudaMemcpyAsync(g.h_key, out_dev, 4, cudaMemcpyDeviceToHost, st), error, error_size);
+  if (!sync_and_check(st, error, error_size)) return 0;
+  std::memcpy(out, g.h_key, 4);
+  return 1;
+}
+
 int check_status(char* error, size_t error_size) {
   // Called after the stream was synchronised and the status word copied to h_status.
   if (*g.h_status != 0) {
@@ -438,7 +498,7 @@ int edgexpu_cuda_shutdown(void) {
   for (auto& kv : g.weights)
     if (kv.second.owned) cudaFree(reinterpret_cast<void*>(kv.first));
   g.weights.clear();
-  for (DevBuf* b : {&g.x, &g.xq, &g.out, &g.bias, &g.wrow})
+  for (DevBuf* b : {&g.x, &g.xq, &g.out, &g.bias, &g.wrow, &g.samp, &g.sstat})
     if (b->p) cudaFree(b->p);
   for (HostBuf* b : {&g.hx, &g.hout, &g.hbias})
     if (b->p) cudaFreeHost(b->p);
@@ -852,6 +912,50 @@ int edgexpu_cuda_stream_sync(void* stream, char* error, size_t error_size) {
 }
 
 }  // extern "C"
+
+extern "C" int edgexpu_cuda_sample_softmax(float* logits, int n, float top_p, uint64_t* rng, uint32_t* out, char* error,
+                                           size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  if (logits == nullptr || rng == nullptr || out == nullptr || n <= 0) return fail(error, error_size, "sample_softmax: invalid arguments");
+  cudaStream_t st = g.stream;
+  const size_t b = static_cast<size_t>(n) * 4;
+  if (!grow_dev(g.out, b, st, error, error_size) || !grow_host(g.hout, b, error, error_size)) return 0;
+  std::memcpy(g.hout.p, logits, b);
+  EX_CUDA(cudaMemcpyAsync(g.out.p, g.hout.p, b, cudaMemcpyHostToDevice, st), error, error_size);
+  if (!sample_dev(static_cast<float*>(g.out.p), n, 0.0f, top_p, rng, out, st, error, error_size)) return 0;
+  // the reference leaves the probabilities in `logits` (softmax in place)
+  EX_CUDA(cudaMemcpyAsync(g.hout.p, g.out.p, b, cudaMemcpyDeviceToHost, st), error, error_size);
+  EX_CUDA(cudaStreamSynchronize(st), error, error_size);
+  std::memcpy(logits, g.hout.p, b);
+  return 1;
+}
+
+extern "C" int edgexpu_cuda_logits_sample(const uint8_t* weight, uint32_t type, const float* hidden, int n_embd, int vocab,
+                                          const float* bias, float temperature, float top_p, uint64_t* rng,
+                                          uint32_t* token_id, char* error, size_t error_size) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!need_ready(error, error_size)) return 0;
+  if (hidden == nullptr || rng == nullptr || token_id == nullptr || n_embd <= 0 || vocab <= 0 || !(temperature > 0.0f))
+    return fail(error, error_size, "logits_sample: invalid arguments");
+  cudaStream_t st = g.stream;
+  const size_t hb = static_cast<size_t>(n_embd) * 4, bb = bias != nullptr ? static_cast<size_t>(vocab) * 4 : 0;
+  if (!grow_host(g.hx, hb, error, error_size) || !grow_dev(g.x, hb, st, error, error_size) ||
+      !grow_dev(g.out, static_cast<size_t>(vocab) * 4, st, error, error_size))
+    return 0;
+  if (bb && (!grow_host(g.hbias, bb, error, error_size) || !grow_dev(g.bias, bb, st, error, error_size))) return 0;
+  std::memcpy(g.hx.p, hidden, hb);
+  EX_CUDA(cudaMemcpyAsync(g.x.p, g.hx.p, hb, cudaMemcpyHostToDevice, st), error, error_size);
+  if (bb) {
+    std::memcpy(g.hbias.p, bias, bb);
+    EX_CUDA(cudaMemcpyAsync(g.bias.p, g.hbias.p, bb, cudaMemcpyHostToDevice, st), error, error_size);
+  }
+  float* scores = static_cast<float*>(g.out.p);
+  if (!run_scores_dev(weight, type, static_cast<const float*>(g.x.p), n_embd, vocab,
+                      bb ? static_cast<const float*>(g.bias.p) : nullptr, scores, st, error, error_size))
+    return 0;
+  return sample_dev(scores, vocab, temperature, top_p, rng, token_id, st, error, error_size);
+}
 
 namespace ex {
 

@@ -24,6 +24,14 @@ cudaError_t launch_dot_f32(uint32_t type, const uint8_t* w, size_t row_bytes, in
 //   atomicMax of argmax_key(scores[i], row0 + i) over i < n into *key (the caller zeroes *key).
 cudaError_t launch_argmax_key(const float* scores, int n, long long row0, unsigned long long* key, cudaStream_t st);
 
+// Temperature sampling over n scores (sample.cu): softmax of io (divided by temperature when
+// > 0) in place, then the reference's top_p truncation and pick with the draw u in [0, 1);
+// the id into out_dev[0], the softmax denominator and the picked prefix's sum and length into
+// stats_dev[0], [2], [3].  scratch: sample_scratch_bytes(n) bytes.
+size_t sample_scratch_bytes(int n);
+cudaError_t launch_sample(float* io, int n, float temperature, float top_p, double u, void* scratch, size_t scratch_bytes,
+                          uint32_t* out_dev, double* stats_dev, cudaStream_t st);
+
 // Synchronous host-buffer calls through one mapped pinned buffer (zerocopy.cu).
 constexpr int ZC_FINISH_THREADS = 128;  // small enough to share an SM with a running GEMV CTA
 constexpr int ZC_PULL_MAX_CTAS = 16;

@@ -1,6 +1,6 @@
 // rowstream_more.cu -- row-stream GEMV instantiations for the other GGUF weight types behind the
 // same dispatch: Q4_0 and Q5_0 (Q8_0 activations), Q5_K and Q6_K (Q8_K activations, and fp32
-// activations on the greedy-logits path).  Store, Argmax and Partials epilogues; the
+// activations on the logits path).  Store, Argmax and Partials epilogues; the
 // tensor-parallel epilogue is built for Q8_0 and Q4_K only (rowstream.cu).
 #include "rowstream_kernel.cuh"
 
@@ -9,10 +9,13 @@ namespace {
 
 template <Fmt F>
 cudaError_t launch_modes(const RowStreamArgs& a, const Layout& L, int grid, cudaStream_t st) {
-  if constexpr (act_of(F) == Act::F32) {  // the logits path: one hidden state, argmax epilogue
+  if constexpr (act_of(F) == Act::F32) {  // the logits path: one hidden state; argmax, or every score
     if (a.mode == RowOut::Argmax && a.m == 1)
       return a.exact ? launch_impl<F, RowOut::Argmax, 1, false, true>(a, L, grid, st)
                      : launch_impl<F, RowOut::Argmax, 1>(a, L, grid, st);
+    if (a.mode == RowOut::Store && a.m == 1)
+      return a.exact ? launch_impl<F, RowOut::Store, 1, false, true>(a, L, grid, st)
+                     : launch_impl<F, RowOut::Store, 1>(a, L, grid, st);
   } else {
     if (a.mode == RowOut::Store) return launch_mtok<F, RowOut::Store>(a, L, grid, st);
     if (a.mode == RowOut::Argmax) return launch_mtok<F, RowOut::Argmax>(a, L, grid, st);

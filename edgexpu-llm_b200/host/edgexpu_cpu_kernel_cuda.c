@@ -409,3 +409,16 @@ int edgexpu_b200_logits_greedy(const uint8_t *weight, uint32_t type, const float
     }
     return edgexpu_cuda_logits_argmax(weight, type, hidden, n_embd, vocab, bias, token_id, NULL, error, error_size);
 }
+
+int edgexpu_b200_logits_sample(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
+                               const float *bias, float temperature, float top_p, uint64_t *rng, uint32_t *token_id,
+                               char *error, size_t error_size) {
+    if (weight == NULL || hidden == NULL || token_id == NULL || rng == NULL || vocab <= 0) {
+        if (error != NULL && error_size > 0) {
+            snprintf(error, error_size, "logits: missing weight, hidden state or vocab"); /* as native.c:2313-2315 */
+        }
+        return 0;
+    }
+    return edgexpu_cuda_logits_sample(weight, type, hidden, n_embd, vocab, bias, temperature, top_p, rng, token_id,
+                                      error, error_size);
+}

@@ -93,6 +93,12 @@ void edgexpu_b200_clear_error(void);
  * with temperature <= 1e-4.  Returns 1/0 and fills error like the reference's session calls. */
 int edgexpu_b200_logits_greedy(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
                                const float *bias, uint32_t *token_id, char *error, size_t error_size);
+/* Sampled token for temperature > 1e-4, as sample_next_token's temperature branch
+ * (native.c:2322-2353 with edgexpu_cpu_sample_softmax, cpu_kernel.c:762-849): scores / temperature,
+ * softmax, top_p and the draw from the caller's xorshift state *rng, on the device. */
+int edgexpu_b200_logits_sample(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
+                               const float *bias, float temperature, float top_p, uint64_t *rng, uint32_t *token_id,
+                               char *error, size_t error_size);
 
 #ifdef __cplusplus
 }

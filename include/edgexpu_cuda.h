@@ -216,6 +216,23 @@ int edgexpu_cuda_tp_shutdown(void);
 int edgexpu_cuda_linear_quant_batch_tp_dev(float *out, const float *x, const uint8_t *weight, uint32_t type,
                                            const float *bias, int m, int n_out, int n_in, void *stream);
 
+/* ---- temperature sampling on the device -------------------------------------------------------
+ * edgexpu_cpu_sample_softmax (src/cpu_kernel.c:762-849): softmax of logits[n] in place (the
+ * probabilities are written back), the reference's xorshift64 step of *rng (seeded with
+ * 0x00ED6E50 when 0), then for top_p in (0, 1) the shortest prefix of the ids ordered by
+ * probability (descending, ties by ascending id) whose sum reaches top_p, else all ids in order;
+ * *out = the first id of that sequence whose running sum reaches u * (its sum), u = the draw in
+ * [0, 1).  Sums in double as the reference's, in a fixed tree order; exp in double rounded to
+ * float.  1 on success. */
+int edgexpu_cuda_sample_softmax(float *logits, int n, float top_p, uint64_t *rng, uint32_t *out, char *error,
+                                size_t error_size);
+/* The temperature branch of sample_next_token (src/native.c:2322-2353): every logit score of the
+ * resident logits weight (dot + bias, the greedy path's arithmetic and float order) divided by
+ * temperature (> 0), then edgexpu_cuda_sample_softmax on the device.  *token_id = the drawn id. */
+int edgexpu_cuda_logits_sample(const uint8_t *weight, uint32_t type, const float *hidden, int n_embd, int vocab,
+                               const float *bias, float temperature, float top_p, uint64_t *rng, uint32_t *token_id,
+                               char *error, size_t error_size);
+
 /* ---- device-resident model: HBM budget and a GGUF file streamed into HBM --------------------
  * The reference maps the file (src/native.c:115-163), copies each layer into a staging buffer on
  * every use (stage_copy_bytes, native.c:350-380) and admits a model whose working set, KV cache

@@ -30,8 +30,22 @@ static double now_s(void) {
  * hidden (nullable, [n_new][n_embd]) the hidden state each step's logits were taken from;
  * seconds[0] / [1] the prefill and decode wall time.  Returns the number of ids generated (the
  * run stops early only at an end-of-sequence id), or -1 with a message in `error`. */
+int edgexpu_generate_run(const char *gguf_path, const uint32_t *prompt, int n_prompt, int n_new, float temperature,
+                         float top_p, uint32_t *out_ids, float *hidden, int n_embd, double *seconds, char *error,
+                         size_t error_size);
+
 int edgexpu_greedy_run(const char *gguf_path, const uint32_t *prompt, int n_prompt, int n_new, uint32_t *out_ids,
                        float *hidden, int n_embd, double *seconds, char *error, size_t error_size) {
+    return edgexpu_generate_run(gguf_path, prompt, n_prompt, n_new, 0.0f, 1.0f, out_ids, hidden, n_embd, seconds, error,
+                                error_size);
+}
+
+/* As edgexpu_greedy_run, with the sampling settings of edgexpu_native_generate_next: temperature
+ * <= 1e-4 is greedy, else softmax sampling with top_p (the session's sampler state carries over
+ * between calls in one process, as it does in the reference). */
+int edgexpu_generate_run(const char *gguf_path, const uint32_t *prompt, int n_prompt, int n_new, float temperature,
+                         float top_p, uint32_t *out_ids, float *hidden, int n_embd, double *seconds, char *error,
+                         size_t error_size) {
     edgexpu_native_session *s = (edgexpu_native_session *)calloc(1, sizeof *s);
     double t0, t1;
     int i, made = -1;
@@ -67,7 +81,7 @@ int edgexpu_greedy_run(const char *gguf_path, const uint32_t *prompt, int n_prom
         if (hidden != NULL) {
             memcpy(hidden + (size_t)i * n_embd, s->last_hidden, (size_t)n_embd * sizeof(float));
         }
-        if (!edgexpu_native_generate_next(s, 0.0f, 1.0f, &out_ids[i], NULL, 0, &stopped, error, error_size)) {
+        if (!edgexpu_native_generate_next(s, temperature, top_p, &out_ids[i], NULL, 0, &stopped, error, error_size)) {
             made = -1;
             goto done;
         }
