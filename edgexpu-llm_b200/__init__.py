@@ -97,7 +97,13 @@ _CUDA_SIGS = {
     "edgexpu_cuda_gguf_tensor_at": (_c_int, [_c_vp, _c_int, ctypes.POINTER(_c_str), ctypes.POINTER(_c_vp),
                                              ctypes.POINTER(_c_u32), _c_i64p, _c_i64p, _c_u64p, _c_u64p]),
     "edgexpu_cuda_gguf_find": (_c_int, [_c_vp, _c_str]),
+    "edgexpu_cuda_gguf_meta": (_c_int, [_c_vp, _c_str, _c_u64p, ctypes.POINTER(ctypes.c_double),
+                                        ctypes.POINTER(_c_str)]),
     "edgexpu_cuda_gguf_free": (_c_int, [_c_vp]),
+    "edgexpu_cuda_llama_open": (_c_int, [_c_str, _c_int, ctypes.POINTER(_c_vp), _c_str, _c_sz]),
+    "edgexpu_cuda_llama_forward": (_c_int, [_c_vp, _c_vp, _c_int, _c_int, ctypes.c_float, ctypes.c_float, _c_u64p,
+                                            ctypes.POINTER(_c_u32), _c_vp, _c_str, _c_sz]),
+    "edgexpu_cuda_llama_close": (_c_int, [_c_vp]),
 }
 
 _HOST_SIGS = {

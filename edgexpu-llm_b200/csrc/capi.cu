@@ -976,6 +976,14 @@ const DeviceInfo& api_device_info() { return g.info; }
 int api_device() { return g.device; }
 bool api_exact_order() { return exact_order(); }
 cudaStream_t api_stream() { return g.stream; }
+int api_logit_scores(const uint8_t* weight, uint32_t type, const float* hidden, int n_embd, int vocab, const float* bias,
+                     float* scores, cudaStream_t st, char* error, size_t error_size) {
+  return run_scores_dev(weight, type, hidden, n_embd, vocab, bias, scores, st, error, error_size);
+}
+int api_sample(float* io, int n, float temperature, float top_p, uint64_t* rng, uint32_t* out, cudaStream_t st,
+               char* error, size_t error_size) {
+  return sample_dev(io, n, temperature, top_p, rng, out, st, error, error_size);
+}
 uint32_t* api_status_word() { return g.d_status; }
 size_t api_row_bytes(uint32_t type, int n) { return row_bytes_of(type, n); }
 size_t api_act_row_bytes(uint32_t type, int n) { return act_row_bytes_of(type, n); }

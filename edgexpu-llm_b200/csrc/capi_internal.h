@@ -67,6 +67,12 @@ bool api_exact_order();
 uint32_t* api_status_word();
 // The library's stream (the one every synchronous entry point uses).
 cudaStream_t api_stream();
+// Every logit score (dot + bias, the logits path's activation handling and float order) into scores[vocab].
+int api_logit_scores(const uint8_t* weight, uint32_t type, const float* hidden, int n_embd, int vocab, const float* bias,
+                     float* scores, cudaStream_t st, char* error, size_t error_size);
+// Softmax of io[n] (divided by temperature when > 0) and the reference's draw from *rng; synchronous.
+int api_sample(float* io, int n, float temperature, float top_p, uint64_t* rng, uint32_t* out, cudaStream_t st,
+               char* error, size_t error_size);
 size_t api_row_bytes(uint32_t type, int n);
 size_t api_act_row_bytes(uint32_t type, int n);
 // Device scratch of at least `bytes` (the library's activation buffer, grown outside stream capture).

@@ -32,6 +32,21 @@ size_t sample_scratch_bytes(int n);
 cudaError_t launch_sample(float* io, int n, float temperature, float top_p, double u, void* scratch, size_t scratch_bytes,
                           uint32_t* out_dev, double* stats_dev, cudaStream_t st);
 
+struct ExpTab;  // exptab.cuh
+
+// Llama layer ops on the device (layers.cu).
+//   hidden += add (add nullable); out = rmsnorm(hidden) * w.  One CTA.
+cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, float* out, int n, float eps,
+                               cudaStream_t st);
+//   RoPE (adjacent pairs) of q in place and of k into k_slot; v copied to v_slot.
+cudaError_t launch_rope_kv(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
+                           float* k_slot, float* v_slot, cudaStream_t st);
+//   out[h][d] = sum_s softmax_s(dot(q_h, K[s][h/rep]) * scale) * V[s][h/rep][d], s = 0..pos.
+cudaError_t launch_attention(const float* q, const float* kc, const float* vc, int pos, int n_heads, int n_kv, int hd,
+                             float attn_scale, float* out, const ExpTab& et, cudaStream_t st);
+//   g = silu(g) * u.
+cudaError_t launch_swiglu(float* g, const float* u, int n, const ExpTab& et, cudaStream_t st);
+
 // Synchronous host-buffer calls through one mapped pinned buffer (zerocopy.cu).
 constexpr int ZC_FINISH_THREADS = 128;  // small enough to share an SM with a running GEMV CTA
 constexpr int ZC_PULL_MAX_CTAS = 16;

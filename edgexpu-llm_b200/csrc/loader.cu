@@ -105,8 +105,9 @@ size_t scalar_size(uint32_t t) {
   }
 }
 
-// Read a value of type t as an unsigned integer where it is one (the dimension keys); skip others.
-bool read_value(Reader& r, uint32_t t, uint64_t* as_int, std::string* as_str, int depth = 0) {
+// Read a value of type t: integers into *as_int, f32/f64 into *as_f, strings into *as_str, the
+// element count of an array into *as_int; everything else is skipped.
+bool read_value(Reader& r, uint32_t t, uint64_t* as_int, std::string* as_str, double* as_f = nullptr, int depth = 0) {
   if (t == GT_STRING) {
     std::string s = r.str();
     if (as_str != nullptr) *as_str = s;
@@ -116,8 +117,9 @@ bool read_value(Reader& r, uint32_t t, uint64_t* as_int, std::string* as_str, in
     const uint32_t et = r.get<uint32_t>();
     const uint64_t n = r.get<uint64_t>();
     if (!r.ok || depth > 2) return false;
+    if (as_int != nullptr) *as_int = n;
     if (et == GT_STRING || et == GT_ARRAY) {
-      for (uint64_t i = 0; i < n && r.ok; ++i) read_value(r, et, nullptr, nullptr, depth + 1);
+      for (uint64_t i = 0; i < n && r.ok; ++i) read_value(r, et, nullptr, nullptr, nullptr, depth + 1);
       return r.ok;
     }
     const size_t es = scalar_size(et);
@@ -127,7 +129,17 @@ bool read_value(Reader& r, uint32_t t, uint64_t* as_int, std::string* as_str, in
   if (sz == 0) return false;
   uint64_t v = 0;
   r.bytes(&v, sz);
-  if (as_int != nullptr && t != GT_F32 && t != GT_F64) *as_int = v;
+  if (t == GT_F32) {
+    float f;
+    std::memcpy(&f, &v, 4);
+    if (as_f != nullptr) *as_f = f;
+  } else if (t == GT_F64) {
+    double d;
+    std::memcpy(&d, &v, 8);
+    if (as_f != nullptr) *as_f = d;
+  } else if (as_int != nullptr) {
+    *as_int = v;
+  }
   return r.ok;
 }
 
@@ -141,10 +153,19 @@ struct Tensor {
   bool registered;
 };
 
+struct Meta {
+  std::string key;
+  uint32_t type;
+  uint64_t u;   // integers; element count of arrays
+  double f;     // f32 / f64
+  std::string s;
+};
+
 struct Model {
   uint8_t* arena = nullptr;
   uint64_t data_start = 0, data_bytes = 0;
   std::vector<Tensor> tensors;
+  std::vector<Meta> meta;
   edgexpu_cuda_hbm_plan plan{};
 };
 
@@ -226,24 +247,22 @@ int edgexpu_cuda_gguf_load(const char* path, int window, void** model, edgexpu_c
   if (!r.ok || n_tensors > (1u << 20) || n_kv > (1u << 20)) return bail("bad header counts");
   std::string arch;
   uint64_t alignment = 32;
-  std::vector<std::pair<std::string, uint64_t>> ints;
+  auto m = std::make_unique<Model>();
   for (uint64_t i = 0; i < n_kv && r.ok; ++i) {
-    const std::string key = r.str();
-    const uint32_t t = r.get<uint32_t>();
-    uint64_t v = 0;
-    std::string s;
-    if (!read_value(r, t, &v, &s)) return bail("bad metadata value");
-    if (key == "general.architecture") arch = s;
-    else if (key == "general.alignment" && v != 0) alignment = v;
-    else if (t != GT_STRING && t != GT_ARRAY) ints.emplace_back(key, v);
+    Meta e{};
+    e.key = r.str();
+    e.type = r.get<uint32_t>();
+    if (!read_value(r, e.type, &e.u, e.type == GT_STRING ? &e.s : nullptr, &e.f)) return bail("bad metadata value");
+    if (e.key == "general.architecture") arch = e.s;
+    else if (e.key == "general.alignment" && e.u != 0) alignment = e.u;
+    m->meta.push_back(std::move(e));
   }
   auto dim = [&](const char* suffix) -> uint64_t {
     const std::string k = arch + "." + suffix;
-    for (auto& kv : ints)
-      if (kv.first == k) return kv.second;
+    for (const Meta& e : m->meta)
+      if (e.key == k && e.type != GT_STRING && e.type != GT_ARRAY && e.type != GT_F32 && e.type != GT_F64) return e.u;
     return 0;
   };
-  auto m = std::make_unique<Model>();
   m->tensors.reserve(static_cast<size_t>(n_tensors));
   for (uint64_t i = 0; i < n_tensors && r.ok; ++i) {
     Tensor t{};
@@ -358,6 +377,18 @@ int edgexpu_cuda_gguf_find(const void* model, const char* name) {
   for (size_t i = 0; i < m->tensors.size(); ++i)
     if (m->tensors[i].name == name) return static_cast<int>(i);
   return -1;
+}
+
+int edgexpu_cuda_gguf_meta(const void* model, const char* key, uint64_t* as_int, double* as_float, const char** as_str) {
+  if (model == nullptr || key == nullptr) return 0;
+  for (const Meta& e : static_cast<const Model*>(model)->meta) {
+    if (e.key != key) continue;
+    if (as_int != nullptr) *as_int = e.u;
+    if (as_float != nullptr) *as_float = (e.type == GT_F32 || e.type == GT_F64) ? e.f : static_cast<double>(e.u);
+    if (as_str != nullptr) *as_str = e.type == GT_STRING ? e.s.c_str() : nullptr;
+    return static_cast<int>(e.type) + 1;
+  }
+  return 0;
 }
 
 int edgexpu_cuda_gguf_free(void* model) {

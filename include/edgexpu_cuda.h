@@ -270,8 +270,31 @@ int edgexpu_cuda_gguf_tensor_at(const void *model, int index, const char **name,
                                 int64_t *n_in, int64_t *n_out, uint64_t *file_offset, uint64_t *nbytes);
 /* Index of the tensor called `name`, or -1. */
 int edgexpu_cuda_gguf_find(const void *model, const char *name);
+/* Metadata value `key` of a loaded model: integers (and an array's element count) in *as_int,
+ * numbers in *as_float, strings in *as_str (owned by the model).  Returns GGUF type + 1, or 0 when
+ * the key is absent.  Any output may be NULL. */
+int edgexpu_cuda_gguf_meta(const void *model, const char *key, uint64_t *as_int, double *as_float, const char **as_str);
 /* Unregister the model's tensors and free its arena. */
 int edgexpu_cuda_gguf_free(void *model);
+
+/* ---- a llama decoder resident on the device ---------------------------------------------------
+ * The reference's layer loop (forward_decode_token, src/native.c:2404-2600) with every op on the
+ * device: embedding row, RMSNorm, the q|k|v, o, gate|up and down GEMVs, RoPE, attention over the
+ * session's fp32 KV cache, SwiGLU, residual adds, output norm, greedy logits or temperature
+ * sampling.  The weights are streamed into HBM by edgexpu_cuda_gguf_load (`window` KV positions
+ * planned).  Non-matrix ops restate the reference's float operations; its double sums run in a
+ * tree order and exp in double, so they can differ from the reference in the last bit where a
+ * value sits next to a float rounding boundary.  Architecture "llama" (RoPE on adjacent pairs). */
+int edgexpu_cuda_llama_open(const char *gguf_path, int window, void **session, char *error, size_t error_size);
+/* Run tokens[0 .. n_tokens) at positions pos0 .. pos0 + n_tokens - 1 (a prompt, or one decode
+ * step), then pick the next token from the output-normed hidden state of the last one: greedy for
+ * temperature <= 1e-4 (ties to the lowest id), else softmax sampling with top_p from the xorshift
+ * state *rng (edgexpu_cuda_sample_softmax).  last_hidden (nullable, host) receives that hidden
+ * state (the reference's session->last_hidden). */
+int edgexpu_cuda_llama_forward(void *session, const uint32_t *tokens, int n_tokens, int pos0, float temperature,
+                               float top_p, uint64_t *rng, uint32_t *next_token, float *last_hidden, char *error,
+                               size_t error_size);
+int edgexpu_cuda_llama_close(void *session);
 
 /* Token id encoded in an argmax key (0 when no row had a finite score). */
 static inline uint32_t edgexpu_cuda_argmax_key_id(uint64_t key) {
