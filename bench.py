@@ -26,6 +26,11 @@ Workloads (``--workload``):
   prompt ids, then ``--steps`` greedy tokens; the reference arm runs the unchanged reference runtime
   (oracle/_ref/libedgexpu_ref_runtime.so) on the same file.  The line also states whether the token
   ids of both are identical.  N > 1: independent replicas, one per GPU.
+* ``device_decode``: configurations 1 and 4 decoded whole on the device (edgexpu_cuda_llama_*: every
+  layer op, the KV cache and the greedy logits in HBM, token-identical to the reference): the
+  prompt, then ``--warmup`` untimed and ``--steps`` timed greedy tokens, one public-API call per
+  token (its id in, the next id out).  cpu_baseline: the unchanged reference runtime on a bounded
+  sample of the same decode, whose ids are compared with the device's.  N > 1: replicas.
 * ``llama3_8b_q4k_prefill``: configuration 3 -- one step = every quantized projection of the
   32 Llama-3-8B-shaped layers (``--layers`` fewer for small profiling cases) for a prompt of
   ``--batch`` tokens (default 2048), run by the tensor-core GEMM (tcgen05 kind::i8).  Metric:
@@ -1249,6 +1254,123 @@ def run_native(args):
         print(json.dumps(line), flush=True)
 
 
+def run_device_decode(args):
+    import tempfile
+
+    import numpy as np
+
+    world, rank, local = dist_env()
+    pkg = load_pkg()
+    from edgexpu_llm_b200 import gguf_synth as gs
+
+    shape = gs.SMOLLM2_135M_Q8_0 if args.model == "smollm2" else gs.LLAMA3_8B_Q4_K
+    if args.layers:
+        shape = shape.with_layers(args.layers)
+    n_prompt = args.prompt or (128 if args.model == "smollm2" else 512)
+    is_ref = args.impl == "reference"
+    if is_ref and rank != 0:
+        return
+    ref_fn = _bind_greedy(NATIVE_REF) if NATIVE_REF.exists() else None
+    with tempfile.TemporaryDirectory() as td:
+        path = gs.write_llama_gguf(pathlib.Path(td) / f"{shape.name}.gguf", shape, seed=0)
+        prompt = gs.prompt_ids(shape, n_prompt, seed=0)
+        sample_n = min(args.steps, args.ref_tokens)
+        if is_ref:
+            if ref_fn is None:
+                print(json.dumps({"impl": "reference", "unavailable": f"{NATIVE_REF} not built"}))
+                return
+            _greedy(ref_fn, path, prompt, 1)  # warm-up (thread probe, page cache)
+            ids, secs = _greedy(ref_fn, path, prompt, sample_n)
+            tok_s = sample_n / secs[1]
+            line = {"metric": f"decode tok/s ({shape.name}, batch 1)", "value": round(tok_s, 3), "unit": "tok/s",
+                    "n_gpus": 1, "steps": sample_n, "warmup": 1, "ms_per_step": round(secs[1] / sample_n * 1e3, 4),
+                    "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 layer ops, int8 dots",
+                    "data": "synthetic (seeded random-init GGUF model, uniform random prompt ids)",
+                    "config": {"workload": "device_decode", "model": shape.name, "layers": shape.n_layers,
+                               "prompt": n_prompt, "greedy_tokens": sample_n, "prefill_s": round(float(secs[0]), 4)},
+                    "impl": "reference",
+                    "cpu_baseline": {"value": round(tok_s, 3), "unit": "tok/s", "cores": host_threads(),
+                                     "kind": "reference", "sample": f"{sample_n} greedy tokens after a {n_prompt}-token "
+                                                                   "prompt (unchanged reference runtime)"},
+                    "e2e": {"value": round(tok_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+            return
+        pkg.init(local)
+        cuda = pkg.load_cuda()
+        assert cuda.edgexpu_cuda_set_float_order(pkg.ORDER_X86) == 1
+        window = n_prompt + args.warmup + args.steps + 1
+        sess = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(1024)
+        t_open = time.perf_counter()
+        if not cuda.edgexpu_cuda_llama_open(str(path).encode(), window, ctypes.byref(sess), err, 1024):
+            raise RuntimeError(err.value.decode())
+        t_open = time.perf_counter() - t_open
+        nxt = ctypes.c_uint32()
+        ids = []
+
+        def step(toks, pos):
+            if not cuda.edgexpu_cuda_llama_forward(sess, toks.ctypes.data, toks.size, pos, 0.0, 1.0, None,
+                                                   ctypes.byref(nxt), None, err, 1024):
+                raise RuntimeError(err.value.decode())
+            ids.append(nxt.value)
+            return np.array([nxt.value], np.uint32)
+
+        try:
+            t0 = time.perf_counter()
+            tok = step(prompt, 0)
+            prefill_s = time.perf_counter() - t0
+            pos = n_prompt
+            for _ in range(args.warmup):
+                tok = step(tok, pos)
+                pos += 1
+            sampler = ClockSampler(local)
+            sampler.start()
+            time.sleep(0.3)
+            t_w0 = time.time()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                tok = step(tok, pos)
+                pos += 1
+            dt = time.perf_counter() - t0
+            t_w1 = time.time()
+            clocks = sampler.stop(t_w0, t_w1)
+        finally:
+            cuda.edgexpu_cuda_llama_close(sess)
+        tok_s = args.steps / dt
+        ref_line = None
+        if rank == 0 and world == 1 and ref_fn is not None and not args.no_cpu_baseline:
+            r_ids, r_secs = _greedy(ref_fn, path, prompt, sample_n)
+            ref_line = {"value": round(sample_n / r_secs[1], 3), "unit": "tok/s", "cores": host_threads(),
+                        "kind": "reference",
+                        "sample": f"{sample_n} greedy tokens after the same {n_prompt}-token prompt through the unchanged "
+                                  f"reference runtime (oracle/_ref, AVX2 + OpenMP); prefill {r_secs[0]:.3f} s",
+                        "greedy_ids_identical": bool((np.asarray(ids[:sample_n], np.uint32) == r_ids).all())}
+    wb = shape.weight_bytes_per_token()
+    tot = torch_all_sum(tok_s, world) if world > 1 else tok_s
+    peak, peak_kind = peak_hbm()
+    per_tok = dt / args.steps
+    line = {
+        "metric": f"decode tok/s ({shape.name}, batch 1)", "value": round(tot, 3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_tok * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 layer ops, int8 x int8 -> i32 -> f32 dots",
+        "data": "synthetic (seeded random-init GGUF model, uniform random prompt ids)",
+        "config": {"workload": "device_decode", "model": shape.name, "layers": shape.n_layers, "prompt": n_prompt,
+                   "greedy_tokens": args.steps, "prefill_s": round(prefill_s, 4), "open_s": round(t_open, 3),
+                   "parallelism": f"replicas{world}" if world > 1 else "single", "float_order": "x86",
+                   "l2": "no flush: the weights of one token exceed L2 for llama3 and fit it for smollm2",
+                   "path": "edgexpu_cuda_llama_forward: one call per token, all layer ops on the B200"},
+        "e2e": {"value": round(tot, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8},
+        "roofline": {"bound": "hbm", "achieved": round(wb / per_tok / 1e9, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(wb / per_tok / 1e9 / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                     "note": "weight bytes per token / wall time per token (each token's call waits for its id)"},
+        "cpu_baseline": ref_line,
+        "gpu_launches": args.steps * (9 * shape.n_layers + 3),
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def torch_all_sum(v, world):
     import torch
     import torch.distributed as dist
@@ -1266,7 +1388,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gemv", "llama3_8b_q4k_prefill", "native_greedy"],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gemv", "llama3_8b_q4k_prefill", "native_greedy",
+                                                              "device_decode"],
                     default="llama3_8b_q4k_decode")
     ap.add_argument("--wtype", choices=["q4_k", "q8_0"], default="q4_k", help="gemv workload: weight type")
     ap.add_argument("--shape", default="14336,4096", help="gemv workload: n_out,n_in")
@@ -1278,6 +1401,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--model", choices=["smollm2", "llama3"], default="smollm2", help="native_greedy workload: model")
     ap.add_argument("--prompt", type=int, default=0, help="native_greedy workload: prompt ids (128 / 512 by model)")
+    ap.add_argument("--ref-tokens", type=int, default=16, help="device_decode workload: tokens of the CPU reference sample")
     ap.add_argument("--float-order", choices=["x86", "relaxed"], default="relaxed",
                     help="relaxed: the GEMV's own summation order, within 1e-5 * sum|w x| of the reference; x86: float "
                          "outputs bit-identical to the reference's x86 build (the library's default order, the one "
@@ -1291,6 +1415,9 @@ def main():
         args.batch = 2048 if args.workload == "llama3_8b_q4k_prefill" else 1
     if args.workload == "llama3_8b_q4k_prefill":
         (run_prefill_reference if args.impl == "reference" else run_prefill)(args)
+        return
+    if args.workload == "device_decode":
+        run_device_decode(args)
         return
     if args.workload == "native_greedy":
         if args.float_order == "relaxed" and "--float-order" not in sys.argv:
