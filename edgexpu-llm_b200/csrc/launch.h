@@ -38,12 +38,15 @@ struct ExpTab;  // exptab.cuh
 //   hidden += add (add nullable); out = rmsnorm(hidden) * w.  One CTA.
 cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, float* out, int n, float eps,
                                cudaStream_t st);
-//   RoPE (adjacent pairs) of q in place and of k into k_slot; v copied to v_slot.
+//   RoPE (adjacent pairs) of q in place and of k into the K cache at pos; v into the V cache.
+//   Cache layout per layer: [n_kv][window][hd].
 cudaError_t launch_rope_kv(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
-                           float* k_slot, float* v_slot, cudaStream_t st);
-//   out[h][d] = sum_s softmax_s(dot(q_h, K[s][h/rep]) * scale) * V[s][h/rep][d], s = 0..pos.
-cudaError_t launch_attention(const float* q, const float* kc, const float* vc, int pos, int n_heads, int n_kv, int hd,
-                             float attn_scale, float* out, const ExpTab& et, cudaStream_t st);
+                           float* kc, float* vc, int pos, int window, cudaStream_t st);
+//   out[h][d] = sum_s softmax_s(dot(q_h, K[s][h/rep]) * scale) * V[s][h/rep][d], s = 0..pos;
+//   scores: [n_heads][ld] scratch, ld > pos.
+cudaError_t launch_attention(const float* q, const float* kc, const float* vc, int pos, int window, int n_heads, int n_kv,
+                             int hd, float attn_scale, float* scores, int ld, float* out, const ExpTab& et,
+                             cudaStream_t st);
 //   g = silu(g) * u.
 cudaError_t launch_swiglu(float* g, const float* u, int n, const ExpTab& et, cudaStream_t st);
 

@@ -24,7 +24,8 @@ namespace ex {
 namespace {
 
 constexpr int NORM_THREADS = 1024;
-constexpr int ATTN_THREADS = 256;
+constexpr int V_CHUNK = 64;  // V rows staged in shared memory at a time by the softmax/V kernel
+constexpr int V_LD = V_CHUNK * 256 / 4 / 256;  // float4 loads per thread per chunk (head_dim <= 256, 256 threads)
 
 __device__ __forceinline__ double cta_sum_d(double v, double* red) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -83,10 +84,11 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float* hidden
   for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(hidden[i], scale), w[i]);
 }
 
-// Pairs (2j, 2j+1) of every q head rotated in place, of every k head rotated into the K cache
-// slot; v copied into the V cache slot.  rope[2j] = cos, rope[2j+1] = sin of pair j at this position.
+// Pairs (2j, 2j+1) of every q head rotated in place, of every k head rotated into the K cache;
+// v copied into the V cache.  rope[2j] = cos, rope[2j+1] = sin of pair j at this position.  Cache
+// layout per layer: [kv head][window][hd] (one head's rows contiguous).
 __global__ void rope_kv_kernel(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
-                               float* k_slot, float* v_slot) {
+                               float* kc, float* vc, int pos, int window) {
   const int half = hd / 2;
   const int nq = n_heads * half, nk = n_kv * half;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nq + nk; i += gridDim.x * blockDim.x) {
@@ -99,41 +101,60 @@ __global__ void rope_kv_kernel(float* q, const float* k, const float* v, const f
     const float x0 = src[off], x1 = src[off + 1];
     const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
     const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-    float* dst = isq ? q : k_slot;
-    dst[off] = y0;
-    dst[off + 1] = y1;
+    float* dst = isq ? q + off : kc + (static_cast<size_t>(head) * window + pos) * hd + 2 * pr;
+    dst[0] = y0;
+    dst[1] = y1;
   }
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_kv * hd; i += gridDim.x * blockDim.x) v_slot[i] = v[i];
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_kv * hd; i += gridDim.x * blockDim.x) {
+    const int head = i / hd;
+    vc[(static_cast<size_t>(head) * window + pos) * hd + (i - head * hd)] = v[i];
+  }
 }
 
-// One CTA per query head, for the query at position pos: scores over positions 0..pos of the
-// head's KV group, softmax, and the weighted sum of the V rows.  Cache rows: [pos][n_kv][hd].
-__global__ void __launch_bounds__(ATTN_THREADS) attention_kernel(const float* q, const float* kc, const float* vc, int pos,
-                                                                int n_heads, int n_kv, int hd, float attn_scale,
-                                                                float* out, ExpTab et) {
-  extern __shared__ float sm[];
-  float* qh = sm;        // [hd]
-  float* p = sm + hd;    // [pos + 1]
+// Attention scores of the query at position pos: score[h][s] = dot(q_h, K[s][h/rep]) * scale for
+// s = 0..pos.  Eight lanes share a position: lane l runs the AVX2 dot's FMA lane l (elements l,
+// l+8, ...), and the eight lanes are combined in that dot's order.  grid = (n_heads, ceil((pos+1)/32)).
+__global__ void __launch_bounds__(256) attn_scores_kernel(const float* q, const float* kc, int pos, int window, int n_heads,
+                                                          int n_kv, int hd, float attn_scale, float* scores, int ld) {
+  const int h = blockIdx.x, kvh = h / (n_heads / n_kv);
+  const int l = threadIdx.x & 7;
+  const int s = blockIdx.y * 32 + (threadIdx.x >> 3);
+  const int n8 = hd / 8 * 8;
+  const float* qh = q + static_cast<size_t>(h) * hd;
+  const bool live = s <= pos;
+  const float* kr = kc + (static_cast<size_t>(kvh) * window + (live ? s : 0)) * hd;
+  float a = 0.0f;
+  for (int i = l; i < n8; i += 8) a = fmaf(qh[i], kr[i], a);
+  // ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7)) within each group of eight lanes
+  const float a4 = __shfl_down_sync(0xFFFFFFFFu, a, 4, 8);
+  const float b = __fadd_rn(a, a4);              // lane l < 4: a_l + a_{l+4}
+  const float b1 = __shfl_down_sync(0xFFFFFFFFu, b, 1, 8);
+  const float c = __fadd_rn(b, b1);              // lane 0: b0 + b1, lane 2: b2 + b3
+  const float c2 = __shfl_down_sync(0xFFFFFFFFu, c, 2, 8);
+  if (l == 0 && live) {
+    float d = __fadd_rn(c, c2);
+    for (int i = n8; i < hd; ++i) d = __fadd_rn(d, __fmul_rn(qh[i], kr[i]));
+    scores[static_cast<size_t>(h) * ld + s] = __fmul_rn(d, attn_scale);
+  }
+}
+
+// Softmax of score[h][0..pos] and out[h][d] = sum_s p_s * V[s][h/rep][d] (the saxpy's FMAs in s
+// order).  One CTA per head; the V rows come through shared memory V_CHUNK at a time, loaded by
+// every thread, and one thread per output element d runs its FMA chain over them.
+__global__ void __launch_bounds__(256) attn_softmax_v_kernel(const float* scores, int ld, const float* vc, int pos,
+                                                             int window, int n_heads, int n_kv, int hd, float* out,
+                                                             ExpTab et) {
+  extern __shared__ float p[];  // [pos + 1], then V_CHUNK rows of hd at vs
+  float* vs = p + ((pos + 1 + 3) & ~3);
   __shared__ double dred[33];
   __shared__ float fred[33];
   const int h = blockIdx.x, kvh = h / (n_heads / n_kv);
-  for (int i = threadIdx.x; i < hd; i += blockDim.x) qh[i] = q[h * hd + i];
-  __syncthreads();
-  const int n8 = hd / 8 * 8;
+  const float* sc = scores + static_cast<size_t>(h) * ld;
   float m = -INFINITY;
   for (int s = threadIdx.x; s <= pos; s += blockDim.x) {
-    const float* kr = kc + (static_cast<size_t>(s) * n_kv + kvh) * hd;
-    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int i = 0; i < n8; i += 8) {
-#pragma unroll
-      for (int l = 0; l < 8; ++l) a[l] = fmaf(qh[i + l], kr[i + l], a[l]);
-    }
-    float d = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[4]), __fadd_rn(a[1], a[5])),
-                        __fadd_rn(__fadd_rn(a[2], a[6]), __fadd_rn(a[3], a[7])));
-    for (int i = n8; i < hd; ++i) d = __fadd_rn(d, __fmul_rn(qh[i], kr[i]));
-    const float sc = __fmul_rn(d, attn_scale);
-    p[s] = sc;
-    m = fmaxf(m, sc);
+    const float v = sc[s];
+    p[s] = v;
+    m = fmaxf(m, v);
   }
   m = cta_max_f(m, fred);
   double sum = 0.0;
@@ -146,18 +167,42 @@ __global__ void __launch_bounds__(ATTN_THREADS) attention_kernel(const float* q,
   if (sum > 0.0) {
     for (int s = threadIdx.x; s <= pos; s += blockDim.x) p[s] = static_cast<float>(static_cast<double>(p[s]) / sum);
   }
-  __syncthreads();
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float acc = 0.0f;
-    const float* vr = vc + static_cast<size_t>(kvh) * hd + d;
-    const size_t stride = static_cast<size_t>(n_kv) * hd;
-    if (d < n8) {
-      for (int s = 0; s <= pos; ++s) acc = fmaf(p[s], vr[s * stride], acc);
-    } else {
-      for (int s = 0; s <= pos; ++s) acc = __fadd_rn(acc, __fmul_rn(p[s], vr[s * stride]));
+  const int n8 = hd / 8 * 8;
+  // this head's V rows are contiguous: chunk c is V_CHUNK * hd floats at vbase + c * V_CHUNK * hd;
+  // each thread holds up to V_LD float4 of the next chunk in registers while the current one is
+  // used (hd % 4 == 0).
+  const float4* vbase = reinterpret_cast<const float4*>(vc + static_cast<size_t>(kvh) * window * hd);
+  float4* vs4 = reinterpret_cast<float4*>(vs);
+  const int d = threadIdx.x;  // blockDim.x >= hd
+  float acc = 0.0f;
+  float4 nxt[V_LD];
+  auto fetch = [&](int s0) {
+    const int n4 = min(V_CHUNK, pos + 1 - s0) * hd / 4;
+    const float4* src = vbase + static_cast<size_t>(s0) * hd / 4;
+#pragma unroll
+    for (int u = 0; u < V_LD; ++u) {
+      const int i = threadIdx.x + u * static_cast<int>(blockDim.x);
+      if (i < n4) nxt[u] = src[i];
     }
-    out[h * hd + d] = acc;
+  };
+  fetch(0);
+  for (int s0 = 0; s0 <= pos; s0 += V_CHUNK) {
+    const int n = min(V_CHUNK, pos + 1 - s0);
+    __syncthreads();  // the previous chunk has been used (and p is complete on the first pass)
+#pragma unroll
+    for (int u = 0; u < V_LD; ++u) {
+      const int i = threadIdx.x + u * static_cast<int>(blockDim.x);
+      if (i < n * hd / 4) vs4[i] = nxt[u];
+    }
+    __syncthreads();
+    if (s0 + V_CHUNK <= pos) fetch(s0 + V_CHUNK);
+    if (d < n8) {
+      for (int r = 0; r < n; ++r) acc = fmaf(p[s0 + r], vs[r * hd + d], acc);
+    } else if (d < hd) {
+      for (int r = 0; r < n; ++r) acc = __fadd_rn(acc, __fmul_rn(p[s0 + r], vs[r * hd + d]));
+    }
   }
+  if (d < hd) out[h * hd + d] = acc;
 }
 
 __global__ void swiglu_kernel(float* g, const float* u, int n, ExpTab et) {
@@ -177,21 +222,28 @@ cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, 
 }
 
 cudaError_t launch_rope_kv(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
-                           float* k_slot, float* v_slot, cudaStream_t st) {
+                           float* kc, float* vc, int pos, int window, cudaStream_t st) {
   const int work = (n_heads + n_kv) * hd / 2;
-  rope_kv_kernel<<<(work + 255) / 256, 256, 0, st>>>(q, k, v, rope, n_heads, n_kv, hd, k_slot, v_slot);
+  rope_kv_kernel<<<(work + 255) / 256, 256, 0, st>>>(q, k, v, rope, n_heads, n_kv, hd, kc, vc, pos, window);
   return cudaGetLastError();
 }
 
-cudaError_t launch_attention(const float* q, const float* kc, const float* vc, int pos, int n_heads, int n_kv, int hd,
-                             float attn_scale, float* out, const ExpTab& et, cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(hd + pos + 1) * 4;
+cudaError_t launch_attention(const float* q, const float* kc, const float* vc, int pos, int window, int n_heads, int n_kv,
+                             int hd, float attn_scale, float* scores, int ld, float* out, const ExpTab& et,
+                             cudaStream_t st) {
+  if (pos + 1 > ld || pos >= window || hd % 4 != 0) return cudaErrorInvalidValue;
+  attn_scores_kernel<<<dim3(n_heads, (pos + 1 + 31) / 32), 256, 0, st>>>(q, kc, pos, window, n_heads, n_kv, hd, attn_scale,
+                                                                         scores, ld);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (hd > 256) return cudaErrorInvalidValue;
+  const size_t smem = (static_cast<size_t>((pos + 1 + 3) & ~3) + static_cast<size_t>(V_CHUNK) * hd) * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    e = cudaFuncSetAttribute(attn_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
   }
-  attention_kernel<<<n_heads, ATTN_THREADS, smem, st>>>(q, kc, vc, pos, n_heads, n_kv, hd, attn_scale, out, et);
+  attn_softmax_v_kernel<<<n_heads, 256, smem, st>>>(scores, ld, vc, pos, window, n_heads, n_kv, hd, out, et);
   return cudaGetLastError();
 }
 

@@ -51,9 +51,10 @@ struct Session {
   const float* out_norm = nullptr;
   float* buf = nullptr;  // device: hidden, normed, q, k, v, attn, proj, gate, up, down, last, scores
   float *hidden, *normed, *q, *k, *v, *attn, *proj, *gate, *up, *down, *last, *scores;
-  float* kc = nullptr;   // [layers][window][n_kv * hd]
+  float* kc = nullptr;   // [layers][n_kv][window][hd]
   float* vc = nullptr;
   float* rope = nullptr;  // [window][hd]: cos, sin of each pair
+  float* att = nullptr;   // [n_heads][window]: attention scores
   int32_t* tok_dev = nullptr;
   uint64_t* key_dev = nullptr;
   ex::ExpTab et{};
@@ -94,6 +95,7 @@ void release(Session* s) {
   cudaFree(s->kc);
   cudaFree(s->vc);
   cudaFree(s->rope);
+  cudaFree(s->att);
   cudaFree(s->tok_dev);
   cudaFree(s->key_dev);
   cudaFreeHost(s->tok_host);
@@ -131,13 +133,12 @@ int forward_token(Session* s, const int32_t* tok_dev, int pos, cudaStream_t st, 
         if (!edgexpu_cuda_linear_quant_batch_dev(o3[i], s->normed, w3[i]->p, w3[i]->type, nullptr, 1, w3[i]->n_out, s->n_embd, st))
           return ex::api_fail(error, error_size, "layer %d q/k/v: %s", l, edgexpu_cuda_last_error());
     }
-    float* kslot = s->kc + (static_cast<size_t>(l) * s->window + pos) * kv_row;
-    float* vslot = s->vc + (static_cast<size_t>(l) * s->window + pos) * kv_row;
-    SX(ex::launch_rope_kv(s->q, s->k, s->v, s->rope + static_cast<size_t>(pos) * s->hd, s->n_heads, s->n_kv, s->hd, kslot,
-                          vslot, st));
-    SX(ex::launch_attention(s->q, s->kc + static_cast<size_t>(l) * s->window * kv_row,
-                            s->vc + static_cast<size_t>(l) * s->window * kv_row, pos, s->n_heads, s->n_kv, s->hd,
-                            s->attn_scale, s->attn, s->et, st));
+    float* kl = s->kc + static_cast<size_t>(l) * s->window * kv_row;  // [n_kv][window][hd]
+    float* vl = s->vc + static_cast<size_t>(l) * s->window * kv_row;
+    SX(ex::launch_rope_kv(s->q, s->k, s->v, s->rope + static_cast<size_t>(pos) * s->hd, s->n_heads, s->n_kv, s->hd, kl, vl,
+                          pos, s->window, st));
+    SX(ex::launch_attention(s->q, kl, vl, pos, s->window, s->n_heads, s->n_kv, s->hd, s->attn_scale, s->att, s->window,
+                            s->attn, s->et, st));
     if (!edgexpu_cuda_linear_quant_batch_dev(s->proj, s->attn, L.o.p, L.o.type, nullptr, 1, L.o.n_out, L.o.n_in, st))
       return ex::api_fail(error, error_size, "layer %d o: %s", l, edgexpu_cuda_last_error());
     SX(ex::launch_add_rmsnorm(s->hidden, s->proj, L.ffn_norm, s->normed, s->n_embd, s->eps, st));
@@ -192,7 +193,9 @@ int edgexpu_cuda_llama_open(const char* gguf_path, int window, void** session, c
   s->window = window;
   uint64_t n_tok = 0;
   edgexpu_cuda_gguf_meta(s->model, "tokenizer.ggml.tokens", &n_tok, nullptr, nullptr);
-  if (s->hd % 2 != 0 || s->hd > 512) return ex::api_fail(error, error_size, "llama_open: head_dim %d unsupported", s->hd);
+  if (s->hd % 4 != 0 || s->hd > 256) return ex::api_fail(error, error_size, "llama_open: head_dim %d unsupported", s->hd);
+  if ((static_cast<size_t>(window) + 4 + 64u * s->hd) * 4 > 200u * 1024)  // the attention kernel's shared memory
+    return ex::api_fail(error, error_size, "llama_open: window %d too long for head_dim %d", window, s->hd);
   if (!find(s->model, "token_embd.weight", &s->embd, error, error_size)) return 0;
   if (!find(s->model, "output.weight", &s->out, error, error_size, false)) return 0;
   if (s->out.p == nullptr) s->out = s->embd;  // tied embeddings (native.c:415-426)
@@ -252,6 +255,7 @@ int edgexpu_cuda_llama_open(const char* gguf_path, int window, void** session, c
     }
   }
   SX(cudaMalloc(&s->rope, rope.size() * 4));
+  SX(cudaMalloc(&s->att, static_cast<size_t>(s->n_heads) * window * 4));
   SX(cudaMemcpy(s->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice));
   if (!ex::exptab_acquire(&s->et, error, error_size)) return 0;
   s->et_held = true;
