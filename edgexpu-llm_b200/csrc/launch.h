@@ -40,13 +40,19 @@ cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, 
                                cudaStream_t st);
 //   RoPE (adjacent pairs) of q in place and of k into the K cache at pos; v into the V cache.
 //   Cache layout per layer: [n_kv][window][hd].
+//   The position is step[1] (device); rope: [window][hd] table.
 cudaError_t launch_rope_kv(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
-                           float* kc, float* vc, int pos, int window, cudaStream_t st);
+                           float* kc, float* vc, const int* step, int window, cudaStream_t st);
+//   step[0] = token, step[1] = pos (one thread).
+cudaError_t launch_set_step(int* step, int token, int pos, cudaStream_t st);
 //   out[h][d] = sum_s softmax_s(dot(q_h, K[s][h/rep]) * scale) * V[s][h/rep][d], s = 0..pos;
 //   scores: [n_heads][ld] scratch, ld > pos.
-cudaError_t launch_attention(const float* q, const float* kc, const float* vc, int pos, int window, int n_heads, int n_kv,
-                             int hd, float attn_scale, float* scores, int ld, float* out, const ExpTab& et,
+//   pos = step[1] (device); prepare_attention(window, hd) once before the first launch.
+cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int* step, int window, int n_heads,
+                             int n_kv, int hd, float attn_scale, float* scores, int ld, float* out, const ExpTab& et,
                              cudaStream_t st);
+cudaError_t prepare_attention(int window, int hd);
+size_t attention_smem_bytes(int window, int hd);
 //   g = silu(g) * u.
 cudaError_t launch_swiglu(float* g, const float* u, int n, const ExpTab& et, cudaStream_t st);
 

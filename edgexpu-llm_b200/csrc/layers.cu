@@ -85,10 +85,13 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float* hidden
 }
 
 // Pairs (2j, 2j+1) of every q head rotated in place, of every k head rotated into the K cache;
-// v copied into the V cache.  rope[2j] = cos, rope[2j+1] = sin of pair j at this position.  Cache
-// layout per layer: [kv head][window][hd] (one head's rows contiguous).
-__global__ void rope_kv_kernel(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
-                               float* kc, float* vc, int pos, int window) {
+// v copied into the V cache.  The position is step[1] (device memory, so a captured graph serves
+// every position); rope[pos*hd + 2j] = cos, [.. + 2j+1] = sin of pair j.  Cache layout per layer:
+// [kv head][window][hd] (one head's rows contiguous).
+__global__ void rope_kv_kernel(float* q, const float* k, const float* v, const float* rope_all, int n_heads, int n_kv,
+                               int hd, float* kc, float* vc, const int* step, int window) {
+  const int pos = step[1];
+  const float* rope = rope_all + static_cast<size_t>(pos) * hd;
   const int half = hd / 2;
   const int nq = n_heads * half, nk = n_kv * half;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nq + nk; i += gridDim.x * blockDim.x) {
@@ -111,11 +114,15 @@ __global__ void rope_kv_kernel(float* q, const float* k, const float* v, const f
   }
 }
 
-// Attention scores of the query at position pos: score[h][s] = dot(q_h, K[s][h/rep]) * scale for
-// s = 0..pos.  Eight lanes share a position: lane l runs the AVX2 dot's FMA lane l (elements l,
-// l+8, ...), and the eight lanes are combined in that dot's order.  grid = (n_heads, ceil((pos+1)/32)).
-__global__ void __launch_bounds__(256) attn_scores_kernel(const float* q, const float* kc, int pos, int window, int n_heads,
-                                                          int n_kv, int hd, float attn_scale, float* scores, int ld) {
+// Attention scores of the query at position pos = step[1]: score[h][s] = dot(q_h, K[s][h/rep]) *
+// scale for s = 0..pos.  Eight lanes share a position: lane l runs the AVX2 dot's FMA lane l
+// (elements l, l+8, ...), and the eight lanes are combined in that dot's order.
+// grid = (n_heads, ceil(window/32)); blocks past pos return at once.
+__global__ void __launch_bounds__(256) attn_scores_kernel(const float* q, const float* kc, const int* step, int window,
+                                                          int n_heads, int n_kv, int hd, float attn_scale, float* scores,
+                                                          int ld) {
+  const int pos = step[1];
+  if (static_cast<int>(blockIdx.y) * 32 > pos) return;
   const int h = blockIdx.x, kvh = h / (n_heads / n_kv);
   const int l = threadIdx.x & 7;
   const int s = blockIdx.y * 32 + (threadIdx.x >> 3);
@@ -141,11 +148,12 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const float* q, const 
 // Softmax of score[h][0..pos] and out[h][d] = sum_s p_s * V[s][h/rep][d] (the saxpy's FMAs in s
 // order).  One CTA per head; the V rows come through shared memory V_CHUNK at a time, loaded by
 // every thread, and one thread per output element d runs its FMA chain over them.
-__global__ void __launch_bounds__(256) attn_softmax_v_kernel(const float* scores, int ld, const float* vc, int pos,
+__global__ void __launch_bounds__(256) attn_softmax_v_kernel(const float* scores, int ld, const float* vc, const int* step,
                                                              int window, int n_heads, int n_kv, int hd, float* out,
                                                              ExpTab et) {
-  extern __shared__ float p[];  // [pos + 1], then V_CHUNK rows of hd at vs
-  float* vs = p + ((pos + 1 + 3) & ~3);
+  extern __shared__ float p[];  // [window], then V_CHUNK rows of hd at vs
+  const int pos = step[1];
+  float* vs = p + ((window + 3) & ~3);
   __shared__ double dred[33];
   __shared__ float fred[33];
   const int h = blockIdx.x, kvh = h / (n_heads / n_kv);
@@ -213,6 +221,12 @@ __global__ void swiglu_kernel(float* g, const float* u, int n, ExpTab et) {
   }
 }
 
+// The token id and position of the next forward step, for the kernels that read them.
+__global__ void set_step_kernel(int* step, int token, int pos) {
+  step[0] = token;
+  step[1] = pos;
+}
+
 }  // namespace
 
 cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, float* out, int n, float eps,
@@ -221,30 +235,40 @@ cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, 
   return cudaGetLastError();
 }
 
-cudaError_t launch_rope_kv(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
-                           float* kc, float* vc, int pos, int window, cudaStream_t st) {
-  const int work = (n_heads + n_kv) * hd / 2;
-  rope_kv_kernel<<<(work + 255) / 256, 256, 0, st>>>(q, k, v, rope, n_heads, n_kv, hd, kc, vc, pos, window);
+cudaError_t launch_set_step(int* step, int token, int pos, cudaStream_t st) {
+  set_step_kernel<<<1, 1, 0, st>>>(step, token, pos);
   return cudaGetLastError();
 }
 
-cudaError_t launch_attention(const float* q, const float* kc, const float* vc, int pos, int window, int n_heads, int n_kv,
-                             int hd, float attn_scale, float* scores, int ld, float* out, const ExpTab& et,
+cudaError_t launch_rope_kv(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
+                           float* kc, float* vc, const int* step, int window, cudaStream_t st) {
+  const int work = (n_heads + n_kv) * hd / 2;
+  rope_kv_kernel<<<(work + 255) / 256, 256, 0, st>>>(q, k, v, rope, n_heads, n_kv, hd, kc, vc, step, window);
+  return cudaGetLastError();
+}
+
+size_t attention_smem_bytes(int window, int hd) {
+  return (static_cast<size_t>((window + 3) & ~3) + static_cast<size_t>(V_CHUNK) * hd) * 4;
+}
+
+cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int* step, int window, int n_heads,
+                             int n_kv, int hd, float attn_scale, float* scores, int ld, float* out, const ExpTab& et,
                              cudaStream_t st) {
-  if (pos + 1 > ld || pos >= window || hd % 4 != 0) return cudaErrorInvalidValue;
-  attn_scores_kernel<<<dim3(n_heads, (pos + 1 + 31) / 32), 256, 0, st>>>(q, kc, pos, window, n_heads, n_kv, hd, attn_scale,
-                                                                         scores, ld);
+  if (window > ld || hd % 4 != 0) return cudaErrorInvalidValue;
+  attn_scores_kernel<<<dim3(n_heads, (window + 31) / 32), 256, 0, st>>>(q, kc, step, window, n_heads, n_kv, hd, attn_scale,
+                                                                        scores, ld);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (hd > 256) return cudaErrorInvalidValue;
-  const size_t smem = (static_cast<size_t>((pos + 1 + 3) & ~3) + static_cast<size_t>(V_CHUNK) * hd) * 4;
+  const size_t smem = attention_smem_bytes(window, hd);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  if (smem > 48 * 1024) {
-    e = cudaFuncSetAttribute(attn_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-  }
-  attn_softmax_v_kernel<<<n_heads, 256, smem, st>>>(scores, ld, vc, pos, window, n_heads, n_kv, hd, out, et);
+  attn_softmax_v_kernel<<<n_heads, 256, smem, st>>>(scores, ld, vc, step, window, n_heads, n_kv, hd, out, et);
   return cudaGetLastError();
+}
+
+cudaError_t prepare_attention(int window, int hd) {
+  return cudaFuncSetAttribute(attn_softmax_v_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(attention_smem_bytes(window, hd)));
 }
 
 cudaError_t launch_swiglu(float* g, const float* u, int n, const ExpTab& et, cudaStream_t st) {

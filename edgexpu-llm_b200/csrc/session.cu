@@ -55,12 +55,13 @@ struct Session {
   float* vc = nullptr;
   float* rope = nullptr;  // [window][hd]: cos, sin of each pair
   float* att = nullptr;   // [n_heads][window]: attention scores
-  int32_t* tok_dev = nullptr;
+  int32_t* step = nullptr;  // device: {token, position} of the step being run
   uint64_t* key_dev = nullptr;
   ex::ExpTab et{};
   bool et_held = false;
-  int32_t* tok_host = nullptr;
   uint64_t* key_host = nullptr;
+  int eager_steps = 0;      // single-token steps run without the graph (the first one instantiates every kernel)
+  cudaGraphExec_t graph = nullptr;  // the layers of one token, for any position
 };
 
 int find(void* model, const std::string& name, W* w, char* error, size_t error_size, bool required = true) {
@@ -96,9 +97,9 @@ void release(Session* s) {
   cudaFree(s->vc);
   cudaFree(s->rope);
   cudaFree(s->att);
-  cudaFree(s->tok_dev);
+  if (s->graph != nullptr) cudaGraphExecDestroy(s->graph);
+  cudaFree(s->step);
   cudaFree(s->key_dev);
-  cudaFreeHost(s->tok_host);
   cudaFreeHost(s->key_host);
   if (s->model != nullptr) edgexpu_cuda_gguf_free(s->model);
   if (s->et_held) ex::exptab_release();
@@ -111,10 +112,10 @@ void release(Session* s) {
     if (e_ != cudaSuccess) return ex::api_fail(error, error_size, "%s: %s", #call, cudaGetErrorString(e_)); \
   } while (0)
 
-// The token at tok_dev[0] at position pos through every layer; leaves the output-normed hidden state
-// in s->last.
-int forward_token(Session* s, const int32_t* tok_dev, int pos, cudaStream_t st, char* error, size_t error_size) {
-  SX(ex::launch_dequant_rows(s->embd.type, s->embd.p, ex::api_row_bytes(s->embd.type, s->n_embd), s->embd.n_out, tok_dev,
+// The token and position in s->step through every layer; leaves the output-normed hidden state
+// in s->last.  Every launch reads the position from s->step, so one captured graph serves all.
+int forward_layers(Session* s, cudaStream_t st, char* error, size_t error_size) {
+  SX(ex::launch_dequant_rows(s->embd.type, s->embd.p, ex::api_row_bytes(s->embd.type, s->n_embd), s->embd.n_out, s->step,
                              1, s->n_embd, s->hidden, ex::api_status_word(), st));
   const size_t kv_row = static_cast<size_t>(s->n_kv) * s->hd;
   for (int l = 0; l < s->n_layers; ++l) {
@@ -135,9 +136,8 @@ int forward_token(Session* s, const int32_t* tok_dev, int pos, cudaStream_t st, 
     }
     float* kl = s->kc + static_cast<size_t>(l) * s->window * kv_row;  // [n_kv][window][hd]
     float* vl = s->vc + static_cast<size_t>(l) * s->window * kv_row;
-    SX(ex::launch_rope_kv(s->q, s->k, s->v, s->rope + static_cast<size_t>(pos) * s->hd, s->n_heads, s->n_kv, s->hd, kl, vl,
-                          pos, s->window, st));
-    SX(ex::launch_attention(s->q, kl, vl, pos, s->window, s->n_heads, s->n_kv, s->hd, s->attn_scale, s->att, s->window,
+    SX(ex::launch_rope_kv(s->q, s->k, s->v, s->rope, s->n_heads, s->n_kv, s->hd, kl, vl, s->step, s->window, st));
+    SX(ex::launch_attention(s->q, kl, vl, s->step, s->window, s->n_heads, s->n_kv, s->hd, s->attn_scale, s->att, s->window,
                             s->attn, s->et, st));
     if (!edgexpu_cuda_linear_quant_batch_dev(s->proj, s->attn, L.o.p, L.o.type, nullptr, 1, L.o.n_out, L.o.n_in, st))
       return ex::api_fail(error, error_size, "layer %d o: %s", l, edgexpu_cuda_last_error());
@@ -157,6 +157,26 @@ int forward_token(Session* s, const int32_t* tok_dev, int pos, cudaStream_t st, 
       return ex::api_fail(error, error_size, "layer %d down: %s", l, edgexpu_cuda_last_error());
   }
   SX(ex::launch_add_rmsnorm(s->hidden, s->down, s->out_norm, s->last, s->n_embd, s->eps, st));
+  return 1;
+}
+
+// Capture forward_layers into s->graph (after eager steps have instantiated and configured every
+// kernel, so the capture makes no other CUDA calls).
+int capture(Session* s, cudaStream_t st, char* error, size_t error_size) {
+  SX(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  const int ok = forward_layers(s, st, error, error_size);
+  cudaGraph_t g = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(st, &g);
+  if (!ok || e != cudaSuccess) {
+    if (g != nullptr) cudaGraphDestroy(g);
+    return ok ? ex::api_fail(error, error_size, "capturing the decode step: %s", cudaGetErrorString(e)) : 0;
+  }
+  const cudaError_t ie = cudaGraphInstantiate(&s->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) {
+    s->graph = nullptr;
+    return ex::api_fail(error, error_size, "instantiating the decode step: %s", cudaGetErrorString(ie));
+  }
   return 1;
 }
 
@@ -194,7 +214,7 @@ int edgexpu_cuda_llama_open(const char* gguf_path, int window, void** session, c
   uint64_t n_tok = 0;
   edgexpu_cuda_gguf_meta(s->model, "tokenizer.ggml.tokens", &n_tok, nullptr, nullptr);
   if (s->hd % 4 != 0 || s->hd > 256) return ex::api_fail(error, error_size, "llama_open: head_dim %d unsupported", s->hd);
-  if ((static_cast<size_t>(window) + 4 + 64u * s->hd) * 4 > 200u * 1024)  // the attention kernel's shared memory
+  if (ex::attention_smem_bytes(window, s->hd) > 200u * 1024)  // the attention kernel's shared memory
     return ex::api_fail(error, error_size, "llama_open: window %d too long for head_dim %d", window, s->hd);
   if (!find(s->model, "token_embd.weight", &s->embd, error, error_size)) return 0;
   if (!find(s->model, "output.weight", &s->out, error, error_size, false)) return 0;
@@ -259,9 +279,9 @@ int edgexpu_cuda_llama_open(const char* gguf_path, int window, void** session, c
   SX(cudaMemcpy(s->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice));
   if (!ex::exptab_acquire(&s->et, error, error_size)) return 0;
   s->et_held = true;
-  SX(cudaMalloc(&s->tok_dev, static_cast<size_t>(window) * 4));
+  SX(ex::prepare_attention(window, s->hd));
+  SX(cudaMalloc(&s->step, 16));
   SX(cudaMalloc(&s->key_dev, 16));
-  SX(cudaHostAlloc(reinterpret_cast<void**>(&s->tok_host), static_cast<size_t>(window) * 4, cudaHostAllocDefault));
   SX(cudaHostAlloc(reinterpret_cast<void**>(&s->key_host), 16, cudaHostAllocDefault));
   *session = s.release();
   return 1;
@@ -281,12 +301,16 @@ int edgexpu_cuda_llama_forward(void* session, const uint32_t* tokens, int n_toke
   const bool sample = temperature > 1e-4f;
   if (sample && rng == nullptr) return ex::api_fail(error, error_size, "llama_forward: sampling needs an rng state");
   cudaStream_t st = ex::api_stream();
-  // all ids in one copy; the pinned staging is rewritten only once the stream has read it
-  SX(cudaStreamSynchronize(st));
-  std::memcpy(s->tok_host, tokens, static_cast<size_t>(n_tokens) * 4);
-  SX(cudaMemcpyAsync(s->tok_dev, s->tok_host, static_cast<size_t>(n_tokens) * 4, cudaMemcpyHostToDevice, st));
-  for (int t = 0; t < n_tokens; ++t)
-    if (!forward_token(s, s->tok_dev + t, pos0 + t, st, error, error_size)) return 0;
+  for (int t = 0; t < n_tokens; ++t) {
+    SX(ex::launch_set_step(s->step, static_cast<int>(tokens[t]), pos0 + t, st));
+    if (n_tokens == 1 && s->eager_steps >= 1 && s->graph == nullptr && !capture(s, st, error, error_size)) return 0;
+    if (n_tokens == 1 && s->graph != nullptr) {
+      SX(cudaGraphLaunch(s->graph, st));
+    } else {
+      if (!forward_layers(s, st, error, error_size)) return 0;
+      if (n_tokens == 1) ++s->eager_steps;
+    }
+  }
   if (last_hidden != nullptr)
     SX(cudaMemcpyAsync(last_hidden, s->last, static_cast<size_t>(s->n_embd) * 4, cudaMemcpyDeviceToHost, st));
   if (sample) {
