@@ -960,6 +960,9 @@ def run_prefill(args):
     pkg = load_pkg()
     from edgexpu_llm_b200 import synth
 
+    WT = TYPE_Q8_0 if args.wtype == "q8_0" else TYPE_Q4_K
+    tname = "Q8_0" if WT == TYPE_Q8_0 else "Q4_K"
+
     cuda = pkg.load_cuda()
     host = pkg.load_host()
     pkg.init(local)
@@ -977,8 +980,8 @@ def run_prefill(args):
     for _ in range(L):
         lay = []
         for label, n_out, n_in, _k in shapes:
-            buf = synth.torch_weight(TYPE_Q4_K, n_out, n_in, gen, dev)
-            lay.append((label, n_out, n_in, buf, pkg.register_weight(buf, TYPE_Q4_K, n_out, n_in)))
+            buf = synth.torch_weight(WT, n_out, n_in, gen, dev)
+            lay.append((label, n_out, n_in, buf, pkg.register_weight(buf, WT, n_out, n_in)))
         layers.append(lay)
     ins = {n_in: torch.randn((m, n_in), generator=gen, device=dev) for _, _, n_in, _k in shapes}
     outs = {label: torch.empty((m, n_out), device=dev) for label, n_out, _, _k in shapes}
@@ -998,10 +1001,10 @@ def run_prefill(args):
         st = torch.cuda.current_stream().cuda_stream
         for n_t, o_arr, w_arr, n_arr, n_in in calls:
             if n_t == 1:
-                ok = cuda.edgexpu_cuda_linear_quant_batch_dev(o_arr[0], ins[n_in].data_ptr(), w_arr[0], TYPE_Q4_K, None,
+                ok = cuda.edgexpu_cuda_linear_quant_batch_dev(o_arr[0], ins[n_in].data_ptr(), w_arr[0], WT, None,
                                                               m, n_arr[0], n_in, st)
             else:
-                ok = cuda.edgexpu_cuda_linear_quant_multi_dev(n_t, o_arr, w_arr, n_arr, None, TYPE_Q4_K,
+                ok = cuda.edgexpu_cuda_linear_quant_multi_dev(n_t, o_arr, w_arr, n_arr, None, WT,
                                                               ins[n_in].data_ptr(), m, n_in, st)
             if not ok:
                 raise RuntimeError(cuda.edgexpu_cuda_last_error().decode())
@@ -1061,13 +1064,13 @@ def run_prefill(args):
     for i, (label, n_out, n_in, _k) in enumerate(shapes):
         o = outs[label]
         for _ in range(2):
-            cuda.edgexpu_cuda_linear_quant_batch_dev(o.data_ptr(), ins[n_in].data_ptr(), layers[0][i][4], TYPE_Q4_K,
+            cuda.edgexpu_cuda_linear_quant_batch_dev(o.data_ptr(), ins[n_in].data_ptr(), layers[0][i][4], WT,
                                                      None, m, n_out, n_in, st)
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         reps = 5
         a0.record()
         for j in range(reps):
-            cuda.edgexpu_cuda_linear_quant_batch_dev(o.data_ptr(), ins[n_in].data_ptr(), layers[j % L][i][4], TYPE_Q4_K,
+            cuda.edgexpu_cuda_linear_quant_batch_dev(o.data_ptr(), ins[n_in].data_ptr(), layers[j % L][i][4], WT,
                                                      None, m, n_out, n_in, st)
         a1.record()
         torch.cuda.synchronize()
@@ -1085,7 +1088,7 @@ def run_prefill(args):
     def e2e_step():
         for lay in layers:
             for label, n_out, n_in, _b, h in lay:
-                host.edgexpu_cpu_linear_quant_batch(hout[label].ctypes.data, hx[n_in].ctypes.data, h, TYPE_Q4_K, None,
+                host.edgexpu_cpu_linear_quant_batch(hout[label].ctypes.data, hx[n_in].ctypes.data, h, WT, None,
                                                     m, n_out, n_in)
         err = host.edgexpu_b200_last_error()
         if err:
@@ -1105,7 +1108,7 @@ def run_prefill(args):
     e2e_tops = ops * world * e_steps / float(e2e_s.item()) / 1e12
 
     cpu_baseline = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and WT == TYPE_Q4_K:
         try:
             ct, csec, threads = cpu_prefill(64, 10.0, 3)
             cpu_baseline = {"value": round(ct, 4), "unit": "TOPS", "cores": threads, "kind": "reference",
@@ -1115,19 +1118,19 @@ def run_prefill(args):
             cpu_baseline = {"value": None, "unit": "TOPS", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
 
     line = {
-        "metric": f"Q4_K prefill GEMM useful int8 TOPS (llama3_8b_q4k_prefill, M {m})",
+        "metric": f"{tname} prefill GEMM useful int8 TOPS (llama3_8b_q4k_prefill, M {m})",
         "value": round(tops, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_max / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u4/i8 x i8 -> i32 -> f32",
+        "vs_baseline": None, "dtype": "i8 x i8 -> i32 -> f32" if WT == TYPE_Q8_0 else "u4/i8 x i8 -> i32 -> f32",
         "data": "synthetic (seeded random-init GGUF blocks generated in HBM)",
-        "config": {"workload": "llama3_8b_q4k_prefill", "batch": m, "layers": L,
+        "config": {"workload": "llama3_8b_q4k_prefill", "weight_type": tname, "batch": m, "layers": L,
                    "parallelism": f"replicas{world}" if world > 1 else "single", "ops_per_step": ops,
                    "prompt_tokens_per_s": round(m * world * args.steps / (ms_max / 1e3) * L / PREFILL["layers"], 1),
                    "graph": True, "l2": "weights larger than L2, streamed once per step", "per_projection": per_proj,
                    "spec_frac": round(tops / world / TENSOR_I8_SPEC_TOPS, 4)},
         "roofline": {"bound": "tensor", "achieved": round(tops / world, 1), "peak": round(peak, 1), "unit": "TOP/s",
                      "frac": round(tops / world / peak, 4), "traffic": None,
-                     "kernel": "gemm_q4k_tc (tcgen05 kind::i8) incl. its activation packing",
+                     "kernel": ("gemm_q8_tc" if WT == TYPE_Q8_0 else "gemm_q4k_tc") + " (tcgen05 kind::i8) incl. its activation packing",
                      "peak_source": peak_src,
                      "note": "exact integer path runs 2 int8 MMA passes per useful MAC (sc*q4 needs 10 bits)"},
         "cpu_baseline": cpu_baseline,

@@ -40,8 +40,16 @@ struct HostBuf {
   size_t cap = 0;
 };
 
+// A Q8_0 weight (rows [w, w + n_out) of width n_in) repacked for the tensor-core GEMM (gemm_q8_tc.cu).
+struct Q8Pack {
+  void* p = nullptr;
+  int n_out = 0;
+  int n_in = 0;
+};
+
 struct Ctx {
   bool ready = false;
+  std::map<uintptr_t, Q8Pack> q8packs;
   int device = -1;
   cudaStream_t stream = nullptr;
   ex::DeviceInfo info{};
@@ -265,6 +273,61 @@ bool use_tc_partials(uint32_t type, int m, int n_in) {
   return type == ex::TYPE_Q4_K && m >= ex::TC_MIN_M && n_in % ex::QK_K == 0;
 }
 bool use_tc(uint32_t type, int m, int n_in) { return !exact_order() && use_tc_partials(type, m, n_in); }
+// Prefill-sized Q8_0 batches in the relaxed order run as the Q8_0 tensor-core GEMM.
+bool use_tc_q8(uint32_t type, int m, int n_in) {
+  return !exact_order() && type == ex::TYPE_Q8_0 && m >= ex::TC_MIN_M && n_in % ex::QK8_0 == 0;
+}
+
+// The repacked form of rows [weight, weight + n_out) (made on first use, kept until the tensor
+// is freed).
+const uint8_t* q8_pack_of(const uint8_t* weight, int n_out, int n_in, cudaStream_t st, char* error, size_t error_size) {
+  const uintptr_t key = reinterpret_cast<uintptr_t>(weight);
+  auto it = g.q8packs.find(key);
+  if (it != g.q8packs.end() && it->second.n_out == n_out && it->second.n_in == n_in)
+    return static_cast<const uint8_t*>(it->second.p);
+  if (it != g.q8packs.end()) {
+    cudaStreamSynchronize(st);
+    cudaFree(it->second.p);
+    g.q8packs.erase(it);
+  }
+  if (capturing(st)) {
+    fail(error, error_size, "the Q8_0 GEMM's weight repack cannot be made during stream capture");
+    return nullptr;
+  }
+  void* p = nullptr;
+  if (cudaMalloc(&p, ex::q8_weight_pack_bytes(n_out, n_in)) != cudaSuccess) {
+    fail(error, error_size, "cudaMalloc of a Q8_0 repack failed");
+    return nullptr;
+  }
+  if (ex::launch_q8_repack_weight(weight, n_out, n_in, static_cast<uint8_t*>(p), st) != cudaSuccess) {
+    cudaFree(p);
+    fail(error, error_size, "Q8_0 repack launch failed");
+    return nullptr;
+  }
+  g.q8packs[key] = Q8Pack{p, n_out, n_in};
+  return static_cast<const uint8_t*>(p);
+}
+
+// Drop the repacks of rows inside [base, base + bytes).
+void q8_unpack_range(uintptr_t base, size_t bytes) {
+  for (auto it = g.q8packs.lower_bound(base); it != g.q8packs.end() && it->first < base + bytes;) {
+    cudaFree(it->second.p);
+    it = g.q8packs.erase(it);
+  }
+}
+
+// out = x . W^T (+ bias) for a Q8_0 prefill batch on the tensor cores; x fp32 rows, or
+// pre-quantized Q8_0 rows xq.
+int tc_q8_linear(float* out, const float* x, const uint8_t* xq, const uint8_t* weight, const float* bias, int m,
+                 int n_out, int n_in, cudaStream_t st, char* error, size_t error_size) {
+  const uint8_t* wp = q8_pack_of(weight, n_out, n_in, st, error, error_size);
+  if (wp == nullptr) return 0;
+  if (!grow_dev(g.xq, ex::q8_act_pack_bytes(m, n_in) + 64, st, error, error_size)) return 0;
+  uint8_t* ap = static_cast<uint8_t*>(g.xq.p);
+  EX_CUDA(ex::launch_q8_pack_act(x, xq, m, n_in, ap, st), error, error_size);
+  EX_CUDA(ex::launch_q8_gemm(wp, n_out, ap, m, n_in, bias, out, n_out, g.d_status, g.info, st), error, error_size);
+  return 1;
+}
 
 // Pack m activation rows (fp32 x, or Q8_K rows xq) into the GEMM's tile layout in g.xq.
 int tc_pack(const float* x, const uint8_t* xq, int m, int n_in, cudaStream_t st, char* error, size_t error_size) {
@@ -305,6 +368,7 @@ int run_linear_dev(float* out, const float* x, const uint8_t* weight, uint32_t t
   if (use_tc(type, m, n_in))
     return tc_pack(x, nullptr, m, n_in, st, error, error_size) &&
            tc_gemm(out, nullptr, weight, bias, m, n_out, n_in, st, error, error_size);
+  if (use_tc_q8(type, m, n_in)) return tc_q8_linear(out, x, nullptr, weight, bias, m, n_out, n_in, st, error, error_size);
   const ex::Fmt fmt = ex::fmt_q8(type);
   // cpu_kernel.c:577-631: every activation row is quantized once, then each weight row is dotted
   // against every quantized row.  Small batches quantize inside the GEMV launch itself.
@@ -498,6 +562,8 @@ int edgexpu_cuda_shutdown(void) {
   for (auto& kv : g.weights)
     if (kv.second.owned) cudaFree(reinterpret_cast<void*>(kv.first));
   g.weights.clear();
+  for (auto& kv : g.q8packs) cudaFree(kv.second.p);
+  g.q8packs.clear();
   for (DevBuf* b : {&g.x, &g.xq, &g.out, &g.bias, &g.wrow, &g.samp, &g.sstat})
     if (b->p) cudaFree(b->p);
   for (HostBuf* b : {&g.hx, &g.hout, &g.hbias})
@@ -556,10 +622,9 @@ int edgexpu_cuda_free_weight(const void* handle) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   auto it = g.weights.find(reinterpret_cast<uintptr_t>(handle));
   if (it == g.weights.end()) return fail(nullptr, 0, "free_weight: %p is not a registered handle", handle);
-  if (it->second.owned) {
-    cudaDeviceSynchronize();
-    cudaFree(const_cast<void*>(handle));
-  }
+  cudaDeviceSynchronize();
+  q8_unpack_range(it->first, it->second.capacity);
+  if (it->second.owned) cudaFree(const_cast<void*>(handle));
   g.weights.erase(it);
   return 1;
 }
@@ -816,6 +881,13 @@ int edgexpu_cuda_linear_quant_multi_dev(int n, float* const* outs, const uint8_t
         return 0;
     return 1;
   }
+  if (use_tc_q8(type, m, n_in)) {  // one GEMM per tensor (each packs the activations)
+    for (int i = 0; i < n; ++i)
+      if (!tc_q8_linear(outs[i], x, nullptr, weights[i], biases != nullptr ? biases[i] : nullptr, m, n_outs[i], n_in, st,
+                        nullptr, 0))
+        return 0;
+    return 1;
+  }
   const ex::Fmt fmt = ex::fmt_q8(type);
   const size_t qb = act_row_bytes_of(type, n_in);
   const bool fused = ex::rowstream_quantizes_itself(fmt, m);
@@ -859,6 +931,7 @@ int edgexpu_cuda_dot_quant_q8_dev(float* out, const uint8_t* xq, const uint8_t* 
   if (use_tc(type, m, n_in))
     return tc_pack(nullptr, xq, m, n_in, pick(stream), nullptr, 0) &&
            tc_gemm(out, nullptr, weight, bias, m, n_out, n_in, pick(stream), nullptr, 0);
+  if (use_tc_q8(type, m, n_in)) return tc_q8_linear(out, nullptr, xq, weight, bias, m, n_out, n_in, pick(stream), nullptr, 0);
   return run_rows_dev(out, xq, false, weight, type, bias, m, n_out, n_in, pick(stream), nullptr, 0);
 }
 

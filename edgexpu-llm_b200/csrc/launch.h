@@ -156,6 +156,17 @@ struct DeviceInfo {
   int max_smem_optin;
 };
 
+// Q8_0 x Q8_0 tensor-core GEMM for prefill batches (gemm_q8_tc.cu).  The weight rows are repacked
+// once into q8_weight_pack_bytes(n_rows, K) bytes; the activations into q8_act_pack_bytes(m, K).
+size_t q8_weight_pack_bytes(int n_rows, int K);
+size_t q8_act_pack_bytes(int m, int K);
+cudaError_t launch_q8_repack_weight(const uint8_t* w, int n_rows, int K, uint8_t* pack, cudaStream_t st);
+//   From fp32 rows x, or (x == nullptr) from Q8_0 rows xq.
+cudaError_t launch_q8_pack_act(const float* x, const uint8_t* xq, int m, int K, uint8_t* pack, cudaStream_t st);
+//   out[t*out_stride + r] = bias[r] + sum_b d_w[r][b] d_x[t][b] ip[t][r][b]
+cudaError_t launch_q8_gemm(const uint8_t* wpack, int n_rows, const uint8_t* apack, int m, int K, const float* bias,
+                           float* out, long long out_stride, uint32_t* status, const DeviceInfo& dev, cudaStream_t st);
+
 // Largest number of activation rows one row-stream launch keeps in shared memory for this K.
 int rowstream_max_m(Fmt fmt, int K, const DeviceInfo& dev);
 

@@ -192,3 +192,69 @@ def test_gemm_grouped_launch_and_determinism(gpu, port):
     finally:
         for h in hs:
             gpu.free_weight(h)
+
+
+# ---- the Q8_0 GEMM (gemm_q8_tc.cu) ------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("n_out,n_in,m,with_bias", [
+    (1536, 576, 128, False),     # config 1's gate/up at its 128-token prompt (K tail: 18 blocks)
+    (576, 1536, 200, True),      # down, ragged token tile
+    (192, 576, 64, False),       # k/v, one token tile
+    (1001, 4096, 77, True),      # ragged rows and tokens
+    (130, 32, 64, False),        # one block: a chunk of one valid block
+])
+def test_q8_gemm_linear_matches_oracle(gpu, port, n_out, n_in, m, with_bias):
+    from _oracle import TYPE_Q8_0
+
+    s = _synth()
+    rng = np.random.default_rng(n_out + 7 * n_in + m)
+    w = s.q8_0_weight(rng, n_out, n_in)
+    x = s.activations(rng, m, n_in)
+    bias = rng.standard_normal(n_out).astype(np.float32) if with_bias else None
+    h = gpu.upload_weight(w, TYPE_Q8_0, n_out, n_in)
+    try:
+        got = gpu.linear_quant_batch(x, h, TYPE_Q8_0, n_out, bias)
+        again = gpu.linear_quant_batch(x, h, TYPE_Q8_0, n_out, bias)  # the cached repack
+    finally:
+        gpu.free_weight(h)
+    want = port.linear(x, w, TYPE_Q8_0, n_out, bias)
+    bound = port.linear_bound(x, w, TYPE_Q8_0, n_out)
+    assert_close(got, want, bound, 0.0 if bias is None else 1e-7 * np.abs(bias)[None, :] + 1e-6)
+    np.testing.assert_array_equal(got, again)
+
+
+def test_q8_gemm_prequantized_and_grouped(gpu, port):
+    """Pre-quantized Q8_0 rows (edgexpu_cuda_dot_quant_q8_dev) and a grouped q|k|v launch give the
+    fp32 GEMM the same bits as the separate fp32 calls."""
+    from _oracle import TYPE_Q8_0
+
+    torch = _torch()
+    s = _synth()
+    rng = np.random.default_rng(99)
+    n_in, m = 576, 96
+    shapes = [576, 192, 192]
+    ws = [s.q8_0_weight(rng, n, n_in) for n in shapes]
+    x = s.activations(rng, m, n_in)
+    hs = [gpu.upload_weight(w, TYPE_Q8_0, n, n_in) for w, n in zip(ws, shapes)]
+    cuda = gpu.load_cuda()
+    try:
+        sep = [gpu.linear_quant_batch(x, h, TYPE_Q8_0, n) for h, n in zip(hs, shapes)]
+        xd = torch.from_numpy(x).cuda()
+        outs = [torch.full((m, n), float("nan"), device="cuda") for n in shapes]
+        arr_o = (ctypes.c_void_p * 3)(*[o.data_ptr() for o in outs])
+        arr_w = (ctypes.c_void_p * 3)(*hs)
+        arr_n = (ctypes.c_int * 3)(*shapes)
+        assert cuda.edgexpu_cuda_linear_quant_multi_dev(3, arr_o, arr_w, arr_n, None, TYPE_Q8_0, xd.data_ptr(), m, n_in,
+                                                        _stream())
+        xq = torch.from_numpy(port.quantize(x, TYPE_Q8_0)).cuda()
+        pre = torch.full((m, shapes[0]), float("nan"), device="cuda")
+        assert cuda.edgexpu_cuda_dot_quant_q8_dev(pre.data_ptr(), xq.data_ptr(), hs[0], TYPE_Q8_0, None, m, shapes[0],
+                                                  n_in, _stream())
+        _sync(gpu)
+        for o, r in zip(outs, sep):
+            np.testing.assert_array_equal(o.cpu().numpy(), r)
+        np.testing.assert_array_equal(pre.cpu().numpy(), sep[0])
+    finally:
+        for h in hs:
+            gpu.free_weight(h)
