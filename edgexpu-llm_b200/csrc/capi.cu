@@ -14,6 +14,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <tuple>
 
 #include "../../include/edgexpu_cuda.h"
 #include "capi_internal.h"
@@ -47,6 +48,26 @@ struct Q8Pack {
   int n_in = 0;
 };
 
+// A synchronous host-buffer call's three launches (pull, product, finish) recorded once per call
+// shape and replayed as one CUDA graph.
+struct ZcKey {
+  int kind;  // 0: linear, 1: greedy logits
+  uintptr_t weight;
+  uint32_t type;
+  int m, n_out, n_in;
+  int has_bias;
+  int order;
+  bool operator<(const ZcKey& o) const {
+    return std::tie(kind, weight, type, m, n_out, n_in, has_bias, order) <
+           std::tie(o.kind, o.weight, o.type, o.m, o.n_out, o.n_in, o.has_bias, o.order);
+  }
+};
+struct ZcGraph {
+  cudaGraphExec_t exec = nullptr;  // null: recording was refused, the call launches directly
+  uint64_t gen = 0;                // buffer generation the graph's pointers belong to
+};
+constexpr size_t ZC_MAX_GRAPHS = 4096;
+
 struct Ctx {
   bool ready = false;
   std::map<uintptr_t, Q8Pack> q8packs;
@@ -66,6 +87,8 @@ struct Ctx {
   uint8_t* zc_d = nullptr;  // the same buffer's device address
   size_t zc_cap = 0;
   uint32_t zc_seq = 0;
+  std::map<ZcKey, ZcGraph> zc_graphs;
+  uint64_t buf_gen = 1;  // advances whenever a scratch or mapped buffer moves, or a weight is freed
 };
 
 Ctx g;
@@ -143,6 +166,7 @@ int grow_dev(DevBuf& b, size_t need, cudaStream_t st, char* error, size_t error_
   if (b.p != nullptr) cudaFree(b.p);
   b.p = nullptr;
   b.cap = 0;
+  ++g.buf_gen;
   EX_CUDA(cudaMalloc(&b.p, cap), error, error_size);
   b.cap = cap;
   return 1;
@@ -175,6 +199,7 @@ int grow_zc(size_t need, char* error, size_t error_size) {
   }
   g.zc_h = g.zc_d = nullptr;
   g.zc_cap = 0;
+  ++g.buf_gen;
   EX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&g.zc_h), cap, cudaHostAllocMapped), error, error_size);
   EX_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&g.zc_d), g.zc_h, 0), error, error_size);
   std::memset(g.zc_h, 0, 256);
@@ -184,15 +209,60 @@ int grow_zc(size_t need, char* error, size_t error_size) {
 
 int check_status(char* error, size_t error_size);
 
-// Launch the finish kernel for the call's outputs (n floats at src -> offset `off` of the mapped
-// buffer) and wait until its sequence number arrives.  The wait is bounded: the stream is
-// polled for errors every ~1000 spins, and after 60 s the call fails.
-int zc_finish_and_wait(const float* src, int n, size_t off, cudaStream_t st, char* error, size_t error_size) {
+void zc_graphs_clear() {
+  for (auto& kv : g.zc_graphs)
+    if (kv.second.exec != nullptr) cudaGraphExecDestroy(kv.second.exec);
+  g.zc_graphs.clear();
+}
+
+// The next call's sequence number, written into the mapped buffer at `off` (after the call's
+// inputs, inside the range its pull kernel copies to the device).
+uint32_t zc_stage_seq(size_t off) {
   if (++g.zc_seq == 0) g.zc_seq = 1;
-  const uint32_t seq = g.zc_seq;
-  EX_CUDA(ex::launch_zc_finish(src, reinterpret_cast<float*>(g.zc_d + off), n, g.d_status,
-                               reinterpret_cast<uint32_t*>(g.zc_d), seq, st),
-          error, error_size);
+  *reinterpret_cast<volatile uint32_t*>(g.zc_h + off) = g.zc_seq;
+  std::atomic_thread_fence(std::memory_order_release);
+  return g.zc_seq;
+}
+
+// Run a synchronous call's launches: `enqueue(error, error_size)` puts pull, product and finish on
+// st.  The first call of a shape launches them directly (sizing any scratch) and then records them
+// into a CUDA graph; later calls of that shape replay the graph, one launch instead of three.  A
+// graph belongs to one buffer generation: once a buffer moved it is recorded again.
+template <class F>
+int zc_run(const ZcKey& key, cudaStream_t st, F&& enqueue, char* error, size_t error_size) {
+  auto it = g.zc_graphs.find(key);
+  if (it != g.zc_graphs.end() && it->second.gen == g.buf_gen) {
+    if (it->second.exec == nullptr) return enqueue(error, error_size);
+    EX_CUDA(cudaGraphLaunch(it->second.exec, st), error, error_size);
+    return 1;
+  }
+  const uint64_t gen = g.buf_gen;
+  if (!enqueue(error, error_size)) return 0;
+  if (g.buf_gen != gen) return 1;  // a buffer moved during the call: record on a later one
+  if (g.zc_graphs.size() >= ZC_MAX_GRAPHS) zc_graphs_clear();
+  ZcGraph zg;
+  zg.gen = gen;
+  char saved[sizeof g_err];
+  std::memcpy(saved, g_err, sizeof g_err);
+  cudaGraph_t graph = nullptr;
+  if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+    const int ok = enqueue(nullptr, 0);
+    const cudaError_t e = cudaStreamEndCapture(st, &graph);
+    if (ok && e == cudaSuccess && graph != nullptr && cudaGraphInstantiate(&zg.exec, graph, 0) != cudaSuccess)
+      zg.exec = nullptr;
+    if (graph != nullptr) cudaGraphDestroy(graph);
+  }
+  (void)cudaGetLastError();  // a refused recording is not the call's error
+  std::memcpy(g_err, saved, sizeof g_err);
+  ZcGraph& slot = g.zc_graphs[key];
+  if (slot.exec != nullptr) cudaGraphExecDestroy(slot.exec);
+  slot = zg;
+  return 1;
+}
+
+// Wait until the call's finish kernel has published sequence number `seq`.  The wait is bounded:
+// the stream is polled for errors every ~1000 spins, and after 60 s the call fails.
+int zc_wait(uint32_t seq, cudaStream_t st, char* error, size_t error_size) {
   volatile uint32_t* ctrl = reinterpret_cast<volatile uint32_t*>(g.zc_h);
   const auto t0 = std::chrono::steady_clock::now();
   for (unsigned it = 1;; ++it) {
@@ -559,6 +629,7 @@ int edgexpu_cuda_shutdown(void) {
   cudaSetDevice(g.device);
   cudaDeviceSynchronize();
   ex::tp_release();
+  zc_graphs_clear();
   for (auto& kv : g.weights)
     if (kv.second.owned) cudaFree(reinterpret_cast<void*>(kv.first));
   g.weights.clear();
@@ -623,6 +694,7 @@ int edgexpu_cuda_free_weight(const void* handle) {
   auto it = g.weights.find(reinterpret_cast<uintptr_t>(handle));
   if (it == g.weights.end()) return fail(nullptr, 0, "free_weight: %p is not a registered handle", handle);
   cudaDeviceSynchronize();
+  zc_graphs_clear();  // recorded calls may name this tensor
   q8_unpack_range(it->first, it->second.capacity);
   if (it->second.owned) cudaFree(const_cast<void*>(handle));
   g.weights.erase(it);
@@ -670,20 +742,29 @@ int edgexpu_cuda_linear_quant_batch(float* out, const float* x, const uint8_t* w
   const size_t xb = static_cast<size_t>(m) * n_in * 4, ob = static_cast<size_t>(m) * n_out * 4;
   const size_t bb = bias != nullptr ? static_cast<size_t>(n_out) * 4 : 0;
   if (al256(xb) + bb <= ex::ZC_MAX_BYTES && ob <= ex::ZC_MAX_BYTES) {
-    // Decode-sized call: inputs pulled from and outputs pushed to the mapped buffer by kernels.
-    const size_t xoff = 256, ooff = xoff + al256(al256(xb) + bb);
-    if (!grow_zc(ooff + al256(ob), error, error_size) || !grow_dev(g.x, al256(xb) + bb + 64, st, error, error_size) ||
+    // Decode-sized call: inputs pulled from and outputs pushed to the mapped buffer by kernels;
+    // the call's sequence number sits after the inputs.
+    const size_t xoff = 256, soff = al256(al256(xb) + bb), ooff = xoff + soff + 256;
+    if (!grow_zc(ooff + al256(ob), error, error_size) || !grow_dev(g.x, soff + 16 + 64, st, error, error_size) ||
         !grow_dev(g.out, ob, st, error, error_size))
       return 0;
     std::memcpy(g.zc_h + xoff, x, xb);
     if (bb) std::memcpy(g.zc_h + xoff + al256(xb), bias, bb);
+    const uint32_t seq = zc_stage_seq(xoff + soff);
     float* xd = static_cast<float*>(g.x.p);
-    EX_CUDA(ex::launch_zc_pull(reinterpret_cast<const float*>(g.zc_d + xoff), xd, static_cast<int>((al256(xb) + bb) / 4), st),
-            error, error_size);
-    if (!run_linear_dev(static_cast<float*>(g.out.p), xd, weight, type, bb ? xd + al256(xb) / 4 : nullptr, m, n_out,
-                        n_in, st, error, error_size))
-      return 0;
-    if (!zc_finish_and_wait(static_cast<const float*>(g.out.p), m * n_out, ooff, st, error, error_size)) return 0;
+    float* od = static_cast<float*>(g.out.p);
+    const uint32_t* seq_dev = reinterpret_cast<const uint32_t*>(static_cast<uint8_t*>(g.x.p) + soff);
+    auto enqueue = [&](char* e, size_t es) -> int {
+      EX_CUDA(ex::launch_zc_pull(reinterpret_cast<const float*>(g.zc_d + xoff), xd, static_cast<int>((soff + 16) / 4), st),
+              e, es);
+      if (!run_linear_dev(od, xd, weight, type, bb ? xd + al256(xb) / 4 : nullptr, m, n_out, n_in, st, e, es)) return 0;
+      EX_CUDA(ex::launch_zc_finish(od, reinterpret_cast<float*>(g.zc_d + ooff), m * n_out, g.d_status,
+                                   reinterpret_cast<uint32_t*>(g.zc_d), seq_dev, st),
+              e, es);
+      return 1;
+    };
+    const ZcKey key{0, reinterpret_cast<uintptr_t>(weight), type, m, n_out, n_in, bb != 0, g_order};
+    if (!zc_run(key, st, enqueue, error, error_size) || !zc_wait(seq, st, error, error_size)) return 0;
     std::memcpy(out, g.zc_h + ooff, ob);
     return 1;
   }
@@ -716,17 +797,25 @@ int edgexpu_cuda_logits_argmax(const uint8_t* weight, uint32_t type, const float
   const size_t hb = static_cast<size_t>(n_embd) * 4, bb = bias != nullptr ? static_cast<size_t>(vocab) * 4 : 0;
   unsigned long long key = 0;
   if (al256(hb) + bb <= ex::ZC_MAX_BYTES) {  // through the mapped buffer (zerocopy.cu)
-    const size_t xoff = 256, koff = xoff + al256(al256(hb) + bb);
-    if (!grow_zc(koff + 256, error, error_size) || !grow_dev(g.x, al256(hb) + bb + 64, st, error, error_size)) return 0;
+    const size_t xoff = 256, soff = al256(al256(hb) + bb), koff = xoff + soff + 256;
+    if (!grow_zc(koff + 256, error, error_size) || !grow_dev(g.x, soff + 16 + 64, st, error, error_size)) return 0;
     std::memcpy(g.zc_h + xoff, hidden, hb);
     if (bb) std::memcpy(g.zc_h + xoff + al256(hb), bias, bb);
+    const uint32_t seq = zc_stage_seq(xoff + soff);
     float* xd = static_cast<float*>(g.x.p);
-    EX_CUDA(ex::launch_zc_pull(reinterpret_cast<const float*>(g.zc_d + xoff), xd, static_cast<int>((al256(hb) + bb) / 4), st),
-            error, error_size);
-    if (!run_logits_dev(weight, type, xd, n_embd, vocab, bb ? xd + al256(hb) / 4 : nullptr, 0, g.d_key, st, error,
-                        error_size))
-      return 0;
-    if (!zc_finish_and_wait(reinterpret_cast<const float*>(g.d_key), 2, koff, st, error, error_size)) return 0;
+    const uint32_t* seq_dev = reinterpret_cast<const uint32_t*>(static_cast<uint8_t*>(g.x.p) + soff);
+    auto enqueue = [&](char* e, size_t es) -> int {
+      EX_CUDA(ex::launch_zc_pull(reinterpret_cast<const float*>(g.zc_d + xoff), xd, static_cast<int>((soff + 16) / 4), st),
+              e, es);
+      if (!run_logits_dev(weight, type, xd, n_embd, vocab, bb ? xd + al256(hb) / 4 : nullptr, 0, g.d_key, st, e, es))
+        return 0;
+      EX_CUDA(ex::launch_zc_finish(reinterpret_cast<const float*>(g.d_key), reinterpret_cast<float*>(g.zc_d + koff), 2,
+                                   g.d_status, reinterpret_cast<uint32_t*>(g.zc_d), seq_dev, st),
+              e, es);
+      return 1;
+    };
+    const ZcKey zk{1, reinterpret_cast<uintptr_t>(weight), type, 1, vocab, n_embd, bb != 0, g_order};
+    if (!zc_run(zk, st, enqueue, error, error_size) || !zc_wait(seq, st, error, error_size)) return 0;
     std::memcpy(&key, g.zc_h + koff, 8);
   } else {
     if (!grow_host(g.hx, hb, error, error_size) || !grow_dev(g.x, hb, st, error, error_size)) return 0;

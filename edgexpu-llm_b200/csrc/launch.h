@@ -63,9 +63,10 @@ constexpr size_t ZC_MAX_BYTES = 256 * 1024;  // per direction; larger calls use 
 //   dst[0 .. n) = src[0 .. n): src in mapped host memory, both 16-byte aligned.
 cudaError_t launch_zc_pull(const float* src, float* dst, int n, cudaStream_t st);
 //   After the previous grid completes: dst[0 .. n) = src[0 .. n) (dst in mapped host memory),
-//   ctrl[1] = *d_status (and *d_status = 0), then ctrl[0] = seq.
-cudaError_t launch_zc_finish(const float* src, float* dst, int n, uint32_t* d_status, uint32_t* ctrl, uint32_t seq,
-                             cudaStream_t st);
+//   ctrl[1] = *d_status (and *d_status = 0), then ctrl[0] = *seq_dev (device memory, written by the
+//   call's pull).
+cudaError_t launch_zc_finish(const float* src, float* dst, int n, uint32_t* d_status, uint32_t* ctrl,
+                             const uint32_t* seq_dev, cudaStream_t st);
 
 // What the row-stream kernel does with each finished row.
 enum class RowOut : int {

@@ -8,8 +8,10 @@
 //     bus into device scratch; it lets the GEMV launch behind it at once (programmatic dependent
 //     launch), and the GEMV reads the scratch only after its dependency wait;
 //   * zc_finish_kernel, launched after the GEMV and waiting for it, writes the outputs and the
-//     device status word back into the buffer and then a sequence number; the host spins on that
-//     number instead of synchronising the stream.
+//     device status word back into the buffer and then the call's sequence number; the host spins
+//     on that number instead of synchronising the stream.  The number travels in with the inputs
+//     (the host writes it after them, the pull kernel copies it), so the three launches take no
+//     per-call argument and the host can replay them as one CUDA graph per call shape.
 // Writers order their stores to host memory with a system-scope fence before the block barrier
 // that precedes the sequence-number store, so a host that sees the number sees the data.
 #include <cuda_runtime.h>
@@ -31,8 +33,9 @@ __global__ void __launch_bounds__(256) zc_pull_kernel(const float* __restrict__ 
 }
 
 __global__ void __launch_bounds__(ZC_FINISH_THREADS) zc_finish_kernel(const float* __restrict__ src, float* dst, int n,
-                                                                      uint32_t* d_status, uint32_t* ctrl, uint32_t seq) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // the producing grid has completed
+                                                                      uint32_t* d_status, uint32_t* ctrl,
+                                                                      const uint32_t* seq_dev) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the producing grid (and the pull before it) has completed
   const int n4 = n >> 2;
   const float4* s4 = reinterpret_cast<const float4*>(src);
   float4* d4 = reinterpret_cast<float4*>(dst);
@@ -47,7 +50,7 @@ __global__ void __launch_bounds__(ZC_FINISH_THREADS) zc_finish_kernel(const floa
     volatile uint32_t* c = ctrl;
     c[1] = s;
     __threadfence_system();
-    c[0] = seq;
+    c[0] = *seq_dev;
   }
 }
 
@@ -61,8 +64,8 @@ cudaError_t launch_zc_pull(const float* src, float* dst, int n, cudaStream_t st)
   return cudaGetLastError();
 }
 
-cudaError_t launch_zc_finish(const float* src, float* dst, int n, uint32_t* d_status, uint32_t* ctrl, uint32_t seq,
-                             cudaStream_t st) {
+cudaError_t launch_zc_finish(const float* src, float* dst, int n, uint32_t* d_status, uint32_t* ctrl,
+                             const uint32_t* seq_dev, cudaStream_t st) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(ZC_FINISH_THREADS);
@@ -72,7 +75,7 @@ cudaError_t launch_zc_finish(const float* src, float* dst, int n, uint32_t* d_st
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, zc_finish_kernel, src, dst, n, d_status, ctrl, seq);
+  return cudaLaunchKernelEx(&cfg, zc_finish_kernel, src, dst, n, d_status, ctrl, seq_dev);
 }
 
 }  // namespace ex
