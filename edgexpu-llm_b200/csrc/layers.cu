@@ -23,6 +23,31 @@ namespace ex {
 
 namespace {
 
+// Every kernel here is launched as a programmatic dependent of the kernel before it (the decode
+// step is one chain of them): it lets its own dependent launch at once, so that kernel's CTAs are
+// placed (and a following GEMV starts streaming its weights) while this one runs, and then waits
+// until the previous grid has completed before touching memory.  Every block passes the wait
+// before it can exit, so this grid's completion implies its predecessors'.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 constexpr int NORM_THREADS = 1024;
 constexpr int V_CHUNK = 64;  // V rows staged in shared memory at a time by the softmax/V kernel
 constexpr int V_LD = V_CHUNK * 256 / 4 / 256;  // float4 loads per thread per chunk (head_dim <= 256, 256 threads)
@@ -68,6 +93,7 @@ __device__ __forceinline__ float cta_max_f(float v, float* red) {
 // One CTA.  hidden += add (when add != nullptr), then out = rmsnorm(hidden) * w.
 __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float* hidden, const float* add, const float* w,
                                                                   float* out, int n, float eps) {
+  pdl_enter();
   __shared__ double red[33];
   double ss = 0.0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -90,6 +116,7 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float* hidden
 // [kv head][window][hd] (one head's rows contiguous).
 __global__ void rope_kv_kernel(float* q, const float* k, const float* v, const float* rope_all, int n_heads, int n_kv,
                                int hd, float* kc, float* vc, const int* step, int window) {
+  pdl_enter();
   const int pos = step[1];
   const float* rope = rope_all + static_cast<size_t>(pos) * hd;
   const int half = hd / 2;
@@ -121,6 +148,7 @@ __global__ void rope_kv_kernel(float* q, const float* k, const float* v, const f
 __global__ void __launch_bounds__(256) attn_scores_kernel(const float* q, const float* kc, const int* step, int window,
                                                           int n_heads, int n_kv, int hd, float attn_scale, float* scores,
                                                           int ld) {
+  pdl_enter();
   const int pos = step[1];
   if (static_cast<int>(blockIdx.y) * 32 > pos) return;
   const int h = blockIdx.x, kvh = h / (n_heads / n_kv);
@@ -151,6 +179,7 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const float* q, const 
 __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const float* scores, int ld, const float* vc, const int* step,
                                                              int window, int n_heads, int n_kv, int hd, float* out,
                                                              ExpTab et) {
+  pdl_enter();
   extern __shared__ float p[];  // [window], then V_CHUNK rows of hd at vs
   const int pos = step[1];
   float* vs = p + ((window + 3) & ~3);
@@ -214,6 +243,7 @@ __global__ void __launch_bounds__(256) attn_softmax_v_kernel(const float* scores
 }
 
 __global__ void swiglu_kernel(float* g, const float* u, int n, ExpTab et) {
+  pdl_enter();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const float x = g[i];
     const float s = __fdiv_rn(x, __fadd_rn(1.0f, exp_lookup(et, -x)));
@@ -231,8 +261,7 @@ __global__ void set_step_kernel(int* step, int token, int pos) {
 
 cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, float* out, int n, float eps,
                                cudaStream_t st) {
-  add_rmsnorm_kernel<<<1, NORM_THREADS, 0, st>>>(hidden, add, w, out, n, eps);
-  return cudaGetLastError();
+  return launch_pdl(add_rmsnorm_kernel, dim3(1), dim3(NORM_THREADS), 0, st, hidden, add, w, out, n, eps);
 }
 
 cudaError_t launch_set_step(int* step, int token, int pos, cudaStream_t st) {
@@ -243,8 +272,8 @@ cudaError_t launch_set_step(int* step, int token, int pos, cudaStream_t st) {
 cudaError_t launch_rope_kv(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
                            float* kc, float* vc, const int* step, int window, cudaStream_t st) {
   const int work = (n_heads + n_kv) * hd / 2;
-  rope_kv_kernel<<<(work + 255) / 256, 256, 0, st>>>(q, k, v, rope, n_heads, n_kv, hd, kc, vc, step, window);
-  return cudaGetLastError();
+  return launch_pdl(rope_kv_kernel, dim3((work + 255) / 256), dim3(256), 0, st, q, k, v, rope, n_heads, n_kv, hd, kc, vc,
+                    step, window);
 }
 
 size_t attention_smem_bytes(int window, int hd) {
@@ -255,15 +284,14 @@ cudaError_t launch_attention(const float* q, const float* kc, const float* vc, c
                              int n_kv, int hd, float attn_scale, float* scores, int ld, float* out, const ExpTab& et,
                              cudaStream_t st) {
   if (window > ld || hd % 4 != 0) return cudaErrorInvalidValue;
-  attn_scores_kernel<<<dim3(n_heads, (window + 31) / 32), 256, 0, st>>>(q, kc, step, window, n_heads, n_kv, hd, attn_scale,
-                                                                        scores, ld);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(attn_scores_kernel, dim3(n_heads, (window + 31) / 32), dim3(256), 0, st, q, kc, step, window,
+                             n_heads, n_kv, hd, attn_scale, scores, ld);
   if (e != cudaSuccess) return e;
   if (hd > 256) return cudaErrorInvalidValue;
   const size_t smem = attention_smem_bytes(window, hd);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  attn_softmax_v_kernel<<<n_heads, 256, smem, st>>>(scores, ld, vc, step, window, n_heads, n_kv, hd, out, et);
-  return cudaGetLastError();
+  return launch_pdl(attn_softmax_v_kernel, dim3(n_heads), dim3(256), smem, st, scores, ld, vc, step, window, n_heads, n_kv,
+                    hd, out, et);
 }
 
 cudaError_t prepare_attention(int window, int hd) {
@@ -272,8 +300,7 @@ cudaError_t prepare_attention(int window, int hd) {
 }
 
 cudaError_t launch_swiglu(float* g, const float* u, int n, const ExpTab& et, cudaStream_t st) {
-  swiglu_kernel<<<(n + 255) / 256 < 296 ? (n + 255) / 256 : 296, 256, 0, st>>>(g, u, n, et);
-  return cudaGetLastError();
+  return launch_pdl(swiglu_kernel, dim3((n + 255) / 256 < 296 ? (n + 255) / 256 : 296), dim3(256), 0, st, g, u, n, et);
 }
 
 }  // namespace ex
