@@ -1251,8 +1251,9 @@ def run_native(args):
                             "peak_source": f"{peak_kind} hbm_gbs"}
         line["config"]["l2"] = "no flush: the weights of one token exceed L2 for llama3 and fit it for smollm2"
         line["cpu_baseline"] = ref_line
-        # one fused quantize+GEMV launch per projection (7 per layer at batch 1) and one logits launch
-        line["gpu_launches"] = n_new * (7 * shape.n_layers + 1)
+        # per synchronous call (7 projections per layer at batch 1, then the logits): the input pull, the
+        # GEMV (it quantizes its own activations) and the finish kernel
+        line["gpu_launches"] = n_new * (7 * shape.n_layers + 1) * 3
     if rank == 0:
         print(json.dumps(line), flush=True)
 
