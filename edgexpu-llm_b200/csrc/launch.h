@@ -35,7 +35,8 @@ cudaError_t launch_sample(float* io, int n, float temperature, float top_p, doub
 struct ExpTab;  // exptab.cuh
 
 // Llama layer ops on the device (layers.cu).
-//   hidden += add (add nullable); out = rmsnorm(hidden) * w.  One CTA.
+//   hidden += add (add nullable); out = rmsnorm(hidden) * w.  One CTA; n <= NORM_MAX_N.
+constexpr int NORM_MAX_N = 8192;
 cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, float* out, int n, float eps,
                                cudaStream_t st);
 //   RoPE (adjacent pairs) of q in place and of k into the K cache at pos; v into the V cache.

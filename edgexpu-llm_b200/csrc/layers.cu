@@ -49,6 +49,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 }
 
 constexpr int NORM_THREADS = 1024;
+constexpr int NORM_PER_THREAD = NORM_MAX_N / NORM_THREADS;
 constexpr int V_CHUNK = 64;  // V rows staged in shared memory at a time by the softmax/V kernel
 constexpr int V_LD = V_CHUNK * 256 / 4 / 256;  // float4 loads per thread per chunk (head_dim <= 256, 256 threads)
 
@@ -90,24 +91,42 @@ __device__ __forceinline__ float cta_max_f(float v, float* red) {
   return r;
 }
 
-// One CTA.  hidden += add (when add != nullptr), then out = rmsnorm(hidden) * w.
+// One CTA.  hidden += add (when add != nullptr), then out = rmsnorm(hidden) * w.  Thread t holds
+// elements t, t + blockDim, ... (at most NORM_PER_THREAD) in registers for both passes; its
+// partial sum of squares runs over them in that order.
 __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float* hidden, const float* add, const float* w,
                                                                   float* out, int n, float eps) {
   pdl_enter();
   __shared__ double red[33];
-  double ss = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float x = hidden[i];
-    if (add != nullptr) {
-      x = __fadd_rn(x, add[i]);
-      hidden[i] = x;
+  float xv[NORM_PER_THREAD], wv[NORM_PER_THREAD];
+#pragma unroll
+  for (int k = 0; k < NORM_PER_THREAD; ++k) {  // every load of the kernel issued up front
+    const int i = threadIdx.x + k * NORM_THREADS;
+    xv[k] = 0.0f;
+    wv[k] = 0.0f;
+    if (i < n) {
+      xv[k] = hidden[i];
+      wv[k] = w[i];
+      if (add != nullptr) xv[k] = __fadd_rn(xv[k], add[i]);
     }
-    ss += static_cast<double>(x) * static_cast<double>(x);
+  }
+  double ss = 0.0;
+#pragma unroll
+  for (int k = 0; k < NORM_PER_THREAD; ++k) {
+    const int i = threadIdx.x + k * NORM_THREADS;
+    if (i < n) {
+      if (add != nullptr) hidden[i] = xv[k];
+      ss += static_cast<double>(xv[k]) * static_cast<double>(xv[k]);
+    }
   }
   ss = cta_sum_d(ss, red);
   const float mean = static_cast<float>(ss / static_cast<double>(n));
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(hidden[i], scale), w[i]);
+#pragma unroll
+  for (int k = 0; k < NORM_PER_THREAD; ++k) {
+    const int i = threadIdx.x + k * NORM_THREADS;
+    if (i < n) out[i] = __fmul_rn(__fmul_rn(xv[k], scale), wv[k]);
+  }
 }
 
 // Pairs (2j, 2j+1) of every q head rotated in place, of every k head rotated into the K cache;
@@ -261,6 +280,7 @@ __global__ void set_step_kernel(int* step, int token, int pos) {
 
 cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, float* out, int n, float eps,
                                cudaStream_t st) {
+  if (n > NORM_THREADS * NORM_PER_THREAD) return cudaErrorInvalidValue;
   return launch_pdl(add_rmsnorm_kernel, dim3(1), dim3(NORM_THREADS), 0, st, hidden, add, w, out, n, eps);
 }
 

@@ -214,6 +214,8 @@ int edgexpu_cuda_llama_open(const char* gguf_path, int window, void** session, c
   uint64_t n_tok = 0;
   edgexpu_cuda_gguf_meta(s->model, "tokenizer.ggml.tokens", &n_tok, nullptr, nullptr);
   if (s->hd % 4 != 0 || s->hd > 256) return ex::api_fail(error, error_size, "llama_open: head_dim %d unsupported", s->hd);
+  if (s->n_embd > ex::NORM_MAX_N)
+    return ex::api_fail(error, error_size, "llama_open: n_embd %d unsupported (at most %d)", s->n_embd, ex::NORM_MAX_N);
   if (ex::attention_smem_bytes(window, s->hd) > 200u * 1024)  // the attention kernel's shared memory
     return ex::api_fail(error, error_size, "llama_open: window %d too long for head_dim %d", window, s->hd);
   if (!find(s->model, "token_embd.weight", &s->embd, error, error_size)) return 0;
