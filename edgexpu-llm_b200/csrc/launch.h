@@ -39,19 +39,15 @@ struct ExpTab;  // exptab.cuh
 constexpr int NORM_MAX_N = 8192;
 cudaError_t launch_add_rmsnorm(float* hidden, const float* add, const float* w, float* out, int n, float eps,
                                cudaStream_t st);
-//   RoPE (adjacent pairs) of q in place and of k into the K cache at pos; v into the V cache.
-//   Cache layout per layer: [n_kv][window][hd].
-//   The position is step[1] (device); rope: [window][hd] table.
-cudaError_t launch_rope_kv(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
-                           float* kc, float* vc, const int* step, int window, cudaStream_t st);
 //   step[0] = token, step[1] = pos (one thread).
 cudaError_t launch_set_step(int* step, int token, int pos, cudaStream_t st);
-//   out[h][d] = sum_s softmax_s(dot(q_h, K[s][h/rep]) * scale) * V[s][h/rep][d], s = 0..pos;
-//   scores: [n_heads][ld] scratch, ld > pos.
-//   pos = step[1] (device); prepare_attention(window, hd) once before the first launch.
-cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int* step, int window, int n_heads,
-                             int n_kv, int hd, float attn_scale, float* scores, int ld, float* out, const ExpTab& et,
-                             cudaStream_t st);
+//   RoPE (adjacent pairs) of q and k at pos = step[1] (device; rope: [window][hd] cos/sin table), k
+//   and v into the caches at pos, then out[h][d] = sum_s softmax_s(dot(rot(q_h), K[s][h/rep]) * scale) *
+//   V[s][h/rep][d], s = 0..pos.  Cache layout per layer: [n_kv][window][hd]; scores: [n_heads][ld]
+//   scratch, ld > pos.  prepare_attention(window, hd) once before the first launch.
+cudaError_t launch_attention(const float* q, const float* k, const float* v, const float* rope, float* kc, float* vc,
+                             const int* step, int window, int n_heads, int n_kv, int hd, float attn_scale, float* scores,
+                             int ld, float* out, const ExpTab& et, cudaStream_t st);
 cudaError_t prepare_attention(int window, int hd);
 size_t attention_smem_bytes(int window, int hd);
 //   g = silu(g) * u.

@@ -129,56 +129,50 @@ __global__ void __launch_bounds__(NORM_THREADS) add_rmsnorm_kernel(float* hidden
   }
 }
 
-// Pairs (2j, 2j+1) of every q head rotated in place, of every k head rotated into the K cache;
-// v copied into the V cache.  The position is step[1] (device memory, so a captured graph serves
-// every position); rope[pos*hd + 2j] = cos, [.. + 2j+1] = sin of pair j.  Cache layout per layer:
-// [kv head][window][hd] (one head's rows contiguous).
-__global__ void rope_kv_kernel(float* q, const float* k, const float* v, const float* rope_all, int n_heads, int n_kv,
-                               int hd, float* kc, float* vc, const int* step, int window) {
-  pdl_enter();
-  const int pos = step[1];
-  const float* rope = rope_all + static_cast<size_t>(pos) * hd;
-  const int half = hd / 2;
-  const int nq = n_heads * half, nk = n_kv * half;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nq + nk; i += gridDim.x * blockDim.x) {
-    const bool isq = i < nq;
-    const int j = isq ? i : i - nq;
-    const int head = j / half, pr = j - head * half;
-    const float c = rope[2 * pr], s = rope[2 * pr + 1];
-    const float* src = isq ? q : k;
-    const int off = head * hd + 2 * pr;
-    const float x0 = src[off], x1 = src[off + 1];
-    const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-    float* dst = isq ? q + off : kc + (static_cast<size_t>(head) * window + pos) * hd + 2 * pr;
-    dst[0] = y0;
-    dst[1] = y1;
-  }
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_kv * hd; i += gridDim.x * blockDim.x) {
-    const int head = i / hd;
-    vc[(static_cast<size_t>(head) * window + pos) * hd + (i - head * hd)] = v[i];
-  }
-}
-
-// Attention scores of the query at position pos = step[1]: score[h][s] = dot(q_h, K[s][h/rep]) *
-// scale for s = 0..pos.  Eight lanes share a position: lane l runs the AVX2 dot's FMA lane l
+// RoPE and attention scores of the query at position pos = step[1] (rope_all[pos*hd + 2j] = cos,
+// [.. + 2j+1] = sin of pair j): score[h][s] = dot(rot(q_h), K[s][h/rep]) * scale for s = 0..pos.
+// Each block rotates its head's q pairs (x0*c - x1*s, x0*s + x1*c, unfused) into shared memory; a
+// block that covers pos rotates k of its kv head the same way and uses it for s = pos, and the
+// first head of each kv group writes that row and v into the caches (the softmax/V kernel reads
+// them after this grid).  Eight lanes share a position: lane l runs the AVX2 dot's FMA lane l
 // (elements l, l+8, ...), and the eight lanes are combined in that dot's order.
-// grid = (n_heads, ceil(window/32)); blocks past pos return at once.
-__global__ void __launch_bounds__(256) attn_scores_kernel(const float* q, const float* kc, const int* step, int window,
-                                                          int n_heads, int n_kv, int hd, float attn_scale, float* scores,
-                                                          int ld) {
+// grid = (n_heads, ceil(window/32)); blocks past pos return at once.  Cache layout per layer:
+// [kv head][window][hd].
+__global__ void __launch_bounds__(256) attn_scores_kernel(const float* q, const float* k, const float* v,
+                                                          const float* rope_all, float* kc, float* vc, const int* step,
+                                                          int window, int n_heads, int n_kv, int hd, float attn_scale,
+                                                          float* scores, int ld) {
   pdl_enter();
+  __shared__ float qr[256], kp[256];  // hd <= 256
   const int pos = step[1];
   if (static_cast<int>(blockIdx.y) * 32 > pos) return;
-  const int h = blockIdx.x, kvh = h / (n_heads / n_kv);
+  const int h = blockIdx.x, rep = n_heads / n_kv, kvh = h / rep;
+  const bool covers_pos = static_cast<int>(blockIdx.y) == pos / 32;
+  const float* rope = rope_all + static_cast<size_t>(pos) * hd;
+  for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+    const int j2 = e & ~1;
+    const float c = rope[j2], sn = rope[j2 + 1];
+    const float x0 = q[static_cast<size_t>(h) * hd + j2], x1 = q[static_cast<size_t>(h) * hd + j2 + 1];
+    qr[e] = (e & 1) ? __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c)) : __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+    if (covers_pos) {
+      const float y0 = k[static_cast<size_t>(kvh) * hd + j2], y1 = k[static_cast<size_t>(kvh) * hd + j2 + 1];
+      const float kr = (e & 1) ? __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, c)) : __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
+      kp[e] = kr;
+      if (h % rep == 0) {
+        const size_t row = (static_cast<size_t>(kvh) * window + pos) * hd + e;
+        kc[row] = kr;
+        vc[row] = v[static_cast<size_t>(kvh) * hd + e];
+      }
+    }
+  }
+  __syncthreads();
   const int l = threadIdx.x & 7;
   const int s = blockIdx.y * 32 + (threadIdx.x >> 3);
   const int n8 = hd / 8 * 8;
-  const float* qh = q + static_cast<size_t>(h) * hd;
   const bool live = s <= pos;
-  const float* kr = kc + (static_cast<size_t>(kvh) * window + (live ? s : 0)) * hd;
+  const float* kr = s == pos ? kp : kc + (static_cast<size_t>(kvh) * window + (live ? s : 0)) * hd;
   float a = 0.0f;
-  for (int i = l; i < n8; i += 8) a = fmaf(qh[i], kr[i], a);
+  for (int i = l; i < n8; i += 8) a = fmaf(qr[i], kr[i], a);
   // ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7)) within each group of eight lanes
   const float a4 = __shfl_down_sync(0xFFFFFFFFu, a, 4, 8);
   const float b = __fadd_rn(a, a4);              // lane l < 4: a_l + a_{l+4}
@@ -187,7 +181,7 @@ __global__ void __launch_bounds__(256) attn_scores_kernel(const float* q, const 
   const float c2 = __shfl_down_sync(0xFFFFFFFFu, c, 2, 8);
   if (l == 0 && live) {
     float d = __fadd_rn(c, c2);
-    for (int i = n8; i < hd; ++i) d = __fadd_rn(d, __fmul_rn(qh[i], kr[i]));
+    for (int i = n8; i < hd; ++i) d = __fadd_rn(d, __fmul_rn(qr[i], kr[i]));
     scores[static_cast<size_t>(h) * ld + s] = __fmul_rn(d, attn_scale);
   }
 }
@@ -289,23 +283,16 @@ cudaError_t launch_set_step(int* step, int token, int pos, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_rope_kv(float* q, const float* k, const float* v, const float* rope, int n_heads, int n_kv, int hd,
-                           float* kc, float* vc, const int* step, int window, cudaStream_t st) {
-  const int work = (n_heads + n_kv) * hd / 2;
-  return launch_pdl(rope_kv_kernel, dim3((work + 255) / 256), dim3(256), 0, st, q, k, v, rope, n_heads, n_kv, hd, kc, vc,
-                    step, window);
-}
-
 size_t attention_smem_bytes(int window, int hd) {
   return (static_cast<size_t>((window + 3) & ~3) + static_cast<size_t>(V_CHUNK) * hd) * 4;
 }
 
-cudaError_t launch_attention(const float* q, const float* kc, const float* vc, const int* step, int window, int n_heads,
-                             int n_kv, int hd, float attn_scale, float* scores, int ld, float* out, const ExpTab& et,
-                             cudaStream_t st) {
-  if (window > ld || hd % 4 != 0) return cudaErrorInvalidValue;
-  cudaError_t e = launch_pdl(attn_scores_kernel, dim3(n_heads, (window + 31) / 32), dim3(256), 0, st, q, kc, step, window,
-                             n_heads, n_kv, hd, attn_scale, scores, ld);
+cudaError_t launch_attention(const float* q, const float* k, const float* v, const float* rope, float* kc, float* vc,
+                             const int* step, int window, int n_heads, int n_kv, int hd, float attn_scale, float* scores,
+                             int ld, float* out, const ExpTab& et, cudaStream_t st) {
+  if (window > ld || hd % 4 != 0 || hd > 256) return cudaErrorInvalidValue;
+  cudaError_t e = launch_pdl(attn_scores_kernel, dim3(n_heads, (window + 31) / 32), dim3(256), 0, st, q, k, v, rope, kc, vc,
+                             step, window, n_heads, n_kv, hd, attn_scale, scores, ld);
   if (e != cudaSuccess) return e;
   if (hd > 256) return cudaErrorInvalidValue;
   const size_t smem = attention_smem_bytes(window, hd);

@@ -136,9 +136,8 @@ int forward_layers(Session* s, cudaStream_t st, char* error, size_t error_size) 
     }
     float* kl = s->kc + static_cast<size_t>(l) * s->window * kv_row;  // [n_kv][window][hd]
     float* vl = s->vc + static_cast<size_t>(l) * s->window * kv_row;
-    SX(ex::launch_rope_kv(s->q, s->k, s->v, s->rope, s->n_heads, s->n_kv, s->hd, kl, vl, s->step, s->window, st));
-    SX(ex::launch_attention(s->q, kl, vl, s->step, s->window, s->n_heads, s->n_kv, s->hd, s->attn_scale, s->att, s->window,
-                            s->attn, s->et, st));
+    SX(ex::launch_attention(s->q, s->k, s->v, s->rope, kl, vl, s->step, s->window, s->n_heads, s->n_kv, s->hd,
+                            s->attn_scale, s->att, s->window, s->attn, s->et, st));
     if (!edgexpu_cuda_linear_quant_batch_dev(s->proj, s->attn, L.o.p, L.o.type, nullptr, 1, L.o.n_out, L.o.n_in, st))
       return ex::api_fail(error, error_size, "layer %d o: %s", l, edgexpu_cuda_last_error());
     SX(ex::launch_add_rmsnorm(s->hidden, s->proj, L.ffn_norm, s->normed, s->n_embd, s->eps, st));
