@@ -1376,7 +1376,9 @@ def run_device_decode(args):
                      "frac": round(wb / per_tok / 1e9 / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                      "note": "weight bytes per token / wall time per token (each token's call waits for its id)"},
         "cpu_baseline": ref_line,
-        "gpu_launches": args.steps * (9 * shape.n_layers + 3),
+        # per token: the step word, the embedding row, per layer 2 norms + 4 GEMVs + RoPE/scores + softmax/V +
+        # SwiGLU, the output norm, and the greedy logits GEMV
+        "gpu_launches": args.steps * (9 * shape.n_layers + 4),
         "clocks": clocks,
     }
     if rank == 0:
