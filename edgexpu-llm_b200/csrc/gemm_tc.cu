@@ -11,8 +11,8 @@
 //    contractions over the super-block accumulate L = sum l*q8 and H = sum h*q8 in int32, so
 //    sumi = L + 256*H exactly.
 //  * summ on the CUDA cores.  It has only 8 terms per super-block: m_j (6-bit, unsigned) times
-//    the 32-element activation sums S_j (13-bit, signed).  The packing kernel splits every S_j
-//    into 7-bit digits S = 128*Sh + Sl, and four dp4a give summ exactly.
+//    the 32-element activation sums S_j (13-bit, signed).  The packing kernel stores the S_j as
+//    16-bit pairs, and four dp2a (two 16-bit x 8-bit products each) give summ exactly.
 //
 // Float conversion without I2F.  The L and H accumulators start at the bit pattern 0x4B400000
 // (1.5 * 2^23 as a float) instead of 0; the MMA adds exact int32 products to it, and since
@@ -62,7 +62,7 @@ constexpr int A_TILE = TC_BM * KH_BYTES;         // 16 KB, one part (L or H) of 
 constexpr int B_TILE = TC_BN * KH_BYTES;         // 16 KB
 constexpr int RAW_BYTES = TC_BM * Q4_K_BYTES;    // one super-block of 128 rows: 18432
 constexpr int AUX_DX = TC_BN * 4;                // d of 128 tokens
-constexpr int AUX_BYTES = AUX_DX + TC_BN * 16;   // + 16 bytes of sub-block-sum digits per token
+constexpr int AUX_BYTES = AUX_DX + TC_BN * 16;   // + the eight 16-bit sub-block sums of each token
 constexpr int N_STAGES = 3;
 constexpr int NR_STAGES = 2;
 constexpr int NX_STAGES = 4;
@@ -108,7 +108,7 @@ struct TcKernelArgs {
   int n_rows, row_bytes, nb, m, n_tt, n_rt;
   const uint8_t* w;       // Q4_K rows (header of each super-block for the epilogue)
   const uint8_t* bt;      // activation tiles [n_tt][nb][2][16 KB]
-  const uint8_t* aux;     // [n_tt][nb][AUX_BYTES]: d[128] floats, digits[128][4] words
+  const uint8_t* aux;     // [n_tt][nb][AUX_BYTES]: d[128] floats, sums[128][4] words of two int16
   const float* bias;
   float* out;
   long long out_stride;
@@ -193,18 +193,11 @@ __host__ __device__ __forceinline__ int sw128_chunk(int r, int c) {
   return (r >> 3) * 1024 + (r & 7) * 128 + (((c ^ r) & 7) << 4);
 }
 
-// Unsigned bytes of a times signed bytes of b, accumulated into c.
-__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
-  int d;
-  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
 // ---- activation packing -------------------------------------------------------------------------
 // One warp per (token, super-block): Q8_K-quantize 256 values (bit-exact with
 // edgexpu_gguf_quantize_q8_k) or take them from a Q8_K row, scatter the int8 values into the two
-// swizzled K-half tiles, and store d and the 7-bit digits of the eight 32-element sums
-// (S_j = bsum_2j + bsum_2j+1 = 128*Sh_j + Sl_j).  Rows past m are written as zeros.
+// swizzled K-half tiles, and store d and the eight 32-element sums S_j = bsum_2j + bsum_2j+1 as
+// int16 pairs (|S_j| <= 32 * 127).  Rows past m are written as zeros.
 template <bool FROM_F32>
 __global__ void __launch_bounds__(256) tc_pack_kernel(const float* __restrict__ x, const uint8_t* __restrict__ xq,
                                                       int m, int K, uint8_t* __restrict__ bt,
@@ -249,14 +242,12 @@ __global__ void __launch_bounds__(256) tc_pack_kernel(const float* __restrict__ 
   // 32-element sums: lanes 4j..4j+3 hold sub-block j
   int s32 = s8 + __shfl_xor_sync(0xFFFFFFFFu, s8, 1);
   s32 += __shfl_xor_sync(0xFFFFFFFFu, s32, 2);
-  const uint32_t lo = static_cast<uint32_t>(s32 & 127), hi = static_cast<uint32_t>((s32 >> 7) & 0xFF);
-  // digits of a token: words [Sl0..3][Sl4..7][Sh0..3][Sh4..7]
+  // sums of a token: words [S0|S1][S2|S3][S4|S5][S6|S7], S_2w in the low half
   uint32_t dig[4] = {0, 0, 0, 0};
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const uint32_t l = __shfl_sync(0xFFFFFFFFu, lo, 4 * j), h = __shfl_sync(0xFFFFFFFFu, hi, 4 * j);
-    dig[j >> 2] |= l << (8 * (j & 3));
-    dig[2 + (j >> 2)] |= h << (8 * (j & 3));
+    const uint32_t v = static_cast<uint32_t>(__shfl_sync(0xFFFFFFFFu, s32, 4 * j)) & 0xFFFFu;
+    dig[j >> 1] |= v << (16 * (j & 1));
   }
   if (lane == 0) {
     uint8_t* xa = aux + ((size_t)tt * nb + sb) * AUX_BYTES;
@@ -588,10 +579,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < EG; ++e) {
             const uint32_t Le = Lb[c][e], He = Hb[c][e];
-            const uint4 dg = dgs[EG * h + e];  // Sl0..3, Sl4..7, Sh0..3, Sh4..7
-            // summ = sum_j m_j * (128*Sh_j + Sl_j), carried with the float bias
-            int sm = dp4a_us(m47, dg.w, dp4a_us(m03, dg.z, 0));
-            sm = dp4a_us(m47, dg.y, dp4a_us(m03, dg.x, sm * 128 + (int)ACC_BIAS));
+            const uint4 dg = dgs[EG * h + e];  // S0|S1, S2|S3, S4|S5, S6|S7
+            // summ = sum_j m_j * S_j (m_j <= 63 reads the same as a signed byte), carried with the float bias
+            int sm = __dp2a_lo(static_cast<int>(dg.x), static_cast<int>(m03), static_cast<int>(ACC_BIAS));
+            sm = __dp2a_hi(static_cast<int>(dg.y), static_cast<int>(m03), sm);
+            sm = __dp2a_lo(static_cast<int>(dg.z), static_cast<int>(m47), sm);
+            sm = __dp2a_hi(static_cast<int>(dg.w), static_cast<int>(m47), sm);
             if constexpr (PARTIALS) {
               const int t = t0 + EG * h + e;
               if (valid && t < a.m) {
