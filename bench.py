@@ -686,7 +686,11 @@ def run_ours(args, wl):
         except FileNotFoundError as e:
             cpu_baseline = {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
 
-    launches_per_step = wl["layers"] * len(groups) + m  # one GEMV launch per group + the logits kernel
+    # one GEMV launch per group + the logits kernel; Q4_K batches of 9..63 in the relaxed order run the
+    # tensor-core GEMM instead: one activation packing per group, then a K-split GEMM and the reduction of
+    # its partial sums per tensor
+    tc_small = t == TYPE_Q4_K and args.float_order == "relaxed" and 9 <= m < 64
+    launches_per_step = wl["layers"] * sum((1 + 2 * len(grp)) if tc_small else 1 for grp in groups) + m
     line = {
         "metric": f"{'Q4_K' if t == TYPE_Q4_K else 'Q8_0'} GEMV HBM GB/s ({args.workload}, batch {m})",
         "value": round(value_gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -703,7 +707,9 @@ def run_ours(args, wl):
                                   if p2p else ("NCCL all-reduce after o/down, NCCL argmax" if tp else "none"))},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "rowstream GEMV (Q4_K x Q8_K)" if t == TYPE_Q4_K else "rowstream GEMV (Q8_0 x Q8_0)",
+                     "kernel": ("gemm_q4k_tc, 16-token tiles with split K (+ activation packing, split reduction)"
+                                if tc_small else "rowstream GEMV (Q4_K x Q8_K)" if t == TYPE_Q4_K
+                                else "rowstream GEMV (Q8_0 x Q8_0)"),
                      "launches": kern_launches, "avg_launch_us": round(kern_s / kern_launches * 1e6, 3),
                      "peak_source": f"{peak_kind} hbm_gbs"},
         "cpu_baseline": cpu_baseline,

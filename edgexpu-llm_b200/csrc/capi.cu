@@ -75,7 +75,7 @@ struct Ctx {
   cudaStream_t stream = nullptr;
   ex::DeviceInfo info{};
   std::map<uintptr_t, WeightRec> weights;
-  DevBuf x, xq, out, bias, wrow, samp, sstat;
+  DevBuf x, xq, out, bias, wrow, samp, sstat, tcpart;
   HostBuf hx, hout, hbias;
   unsigned long long* d_key = nullptr;
   uint32_t* d_status = nullptr;
@@ -336,11 +336,11 @@ int run_rows_dev(float* out, const void* act, bool act_f32, const uint8_t* weigh
   return 1;
 }
 
-// Prefill-sized Q4_K batches run as a tensor-core GEMM (gemm_tc.cu): always for the integer partials
-// (bit-exact either way), for float outputs only in the relaxed order (its epilogue sums the
-// super-blocks in its own order).
+// Q4_K batches of TC_SMALL_MIN_M rows and more run as a tensor-core GEMM (gemm_tc.cu; 16-token
+// tiles below TC_MIN_M): always for the integer partials (bit-exact either way), for float outputs
+// only in the relaxed order (its epilogue sums the super-blocks in its own order).
 bool use_tc_partials(uint32_t type, int m, int n_in) {
-  return type == ex::TYPE_Q4_K && m >= ex::TC_MIN_M && n_in % ex::QK_K == 0;
+  return type == ex::TYPE_Q4_K && m >= ex::TC_SMALL_MIN_M && n_in % ex::QK_K == 0;
 }
 bool use_tc(uint32_t type, int m, int n_in) { return !exact_order() && use_tc_partials(type, m, n_in); }
 // Prefill-sized Q8_0 batches in the relaxed order run as the Q8_0 tensor-core GEMM.
@@ -421,6 +421,9 @@ int tc_gemm(float* out, int32_t* partials, const uint8_t* weight, const float* b
   a.out_stride = n_out;
   a.partials = partials;
   a.status = g.d_status;
+  const size_t pb = partials == nullptr ? ex::tc_split_bytes(m, n_out, n_in, g.info) : 0;
+  if (pb != 0 && !grow_dev(g.tcpart, pb, st, error, error_size)) return 0;
+  a.part = pb != 0 ? static_cast<float*>(g.tcpart.p) : nullptr;
   EX_CUDA(ex::launch_tc_gemm(a, g.info, st), error, error_size);
   return 1;
 }
@@ -635,7 +638,7 @@ int edgexpu_cuda_shutdown(void) {
   g.weights.clear();
   for (auto& kv : g.q8packs) cudaFree(kv.second.p);
   g.q8packs.clear();
-  for (DevBuf* b : {&g.x, &g.xq, &g.out, &g.bias, &g.wrow, &g.samp, &g.sstat})
+  for (DevBuf* b : {&g.x, &g.xq, &g.out, &g.bias, &g.wrow, &g.samp, &g.sstat, &g.tcpart})
     if (b->p) cudaFree(b->p);
   for (HostBuf* b : {&g.hx, &g.hout, &g.hbias})
     if (b->p) cudaFreeHost(b->p);

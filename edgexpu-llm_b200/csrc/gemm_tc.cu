@@ -56,13 +56,9 @@ namespace ex {
 namespace {
 
 constexpr int TC_BM = 128;                       // weight rows per tile (MMA M)
-constexpr int TC_BN = 128;                       // tokens per tile (MMA N)
 constexpr int KH_BYTES = 128;                    // K elements (int8 bytes) per stage
 constexpr int A_TILE = TC_BM * KH_BYTES;         // 16 KB, one part (L or H) of a stage
-constexpr int B_TILE = TC_BN * KH_BYTES;         // 16 KB
 constexpr int RAW_BYTES = TC_BM * Q4_K_BYTES;    // one super-block of 128 rows: 18432
-constexpr int AUX_DX = TC_BN * 4;                // d of 128 tokens
-constexpr int AUX_BYTES = AUX_DX + TC_BN * 16;   // + the eight 16-bit sub-block sums of each token
 constexpr int N_STAGES = 3;
 constexpr int NR_STAGES = 2;
 constexpr int NX_STAGES = 4;
@@ -70,51 +66,84 @@ constexpr int N_CONV_WARPS = 4;
 #ifndef EX_TC_EPI_PER_Q
 #define EX_TC_EPI_PER_Q 4
 #endif
-constexpr int EPI_PER_Q = EX_TC_EPI_PER_Q;       // epilogue warps per 32-lane quadrant
-constexpr int N_EPI_WARPS = 4 * EPI_PER_Q;
-constexpr int EPI_TOK = TC_BN / EPI_PER_Q;       // tokens per epilogue warp
 constexpr int EG = 8;                            // tokens per tensor-memory load group
 constexpr int WARP_PROD = 0;
 constexpr int WARP_MMA = 1;
 constexpr int WARP_CONV0 = 2;
 constexpr int WARP_EPI0 = WARP_CONV0 + N_CONV_WARPS;
-constexpr int TC_THREADS = 32 * (WARP_EPI0 + N_EPI_WARPS);
 
-constexpr uint32_t ACC_COLS = 2 * TC_BN;         // L and H of one buffer
-constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t ACC_BIAS = 0x4B400000u;
 constexpr float ACC_BIAS_F = 12582912.0f;
 
-// kind::i8 instruction descriptor: D int32 (c_format 2 at bit 4), A and B signed int8
-// (formats 1 at bits 7 and 10), both K-major, N>>3 at bit 17, M>>4 at bit 24.
-constexpr uint32_t IDESC_I8 = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(TC_BN >> 3) << 17) |
-                              (uint32_t(TC_BM >> 4) << 24);
-
-struct SmemLayout {
+// Everything that depends on the token tile BN (MMA N): 128 for prefill batches, 16 for batches
+// of 9..63 tokens (the decode batches of the configurations), where a 128-token tile would leave
+// most of every MMA and of the epilogue idle.
+template <int BN>
+struct Cfg {
+  static_assert(BN == 16 || BN == 128, "token tiles of 16 or 128");
+  static constexpr int B_TILE = BN * KH_BYTES;               // 16 KB / 2 KB
+  static constexpr int AUX_DX = BN * 4;                      // d of the tile's tokens
+  static constexpr int AUX_BYTES = AUX_DX + BN * 16;         // + the eight 16-bit sub-block sums of each token
+  static constexpr int EPI_PER_Q = BN == 128 ? EX_TC_EPI_PER_Q : 1;  // epilogue warps per 32-lane quadrant
+  static constexpr int N_EPI_WARPS = 4 * EPI_PER_Q;
+  static constexpr int EPI_TOK = BN / EPI_PER_Q;             // tokens per epilogue warp
+  static constexpr int THREADS = 32 * (WARP_EPI0 + N_EPI_WARPS);
+  static constexpr uint32_t ACC_COLS = 2 * BN;               // L and H of one buffer
+  static constexpr uint32_t TMEM_COLS = BN == 128 ? 512 : 64; // two buffers, a power of two >= 32
+  // kind::i8 instruction descriptor: D int32 (c_format 2 at bit 4), A and B signed int8
+  // (formats 1 at bits 7 and 10), both K-major, N>>3 at bit 17, M>>4 at bit 24.
+  static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
+                                    (uint32_t(TC_BM >> 4) << 24);
+  // shared memory
   static constexpr int A_OFF = 0;                                  // [stage][L, H] 32 KB
-  static constexpr int B_OFF = A_OFF + N_STAGES * 2 * A_TILE;      // [stage] 16 KB
+  static constexpr int B_OFF = A_OFF + N_STAGES * 2 * A_TILE;      // [stage] B_TILE
   static constexpr int R_OFF = B_OFF + N_STAGES * B_TILE;          // [raw stage] 18 KB
-  static constexpr int X_OFF = R_OFF + NR_STAGES * RAW_BYTES;      // [aux stage] 2.5 KB
+  static constexpr int X_OFF = R_OFF + NR_STAGES * RAW_BYTES;      // [aux stage]
   static constexpr int BAR_OFF = X_OFF + NX_STAGES * AUX_BYTES;
   static constexpr int N_BARS = 3 * N_STAGES + 2 * NR_STAGES + 2 * NX_STAGES + 4 + 1;
   static constexpr int MISC_OFF = BAR_OFF + 8 * N_BARS;
   static constexpr int BYTES = MISC_OFF + 16;
   static constexpr int ALLOC = BYTES + 1024;  // base rounded up to 1024 for the swizzled tiles
+  static_assert(ALLOC > 116 * 1024, "one CTA per SM keeps the tensor-memory allocation uncontended");
+  static_assert(ALLOC <= 227 * 1024, "shared memory per CTA");
+  static_assert(R_OFF % 1024 == 0 && B_TILE % 1024 == 0 && AUX_BYTES % 16 == 0 && BAR_OFF % 8 == 0, "alignment");
 };
-static_assert(SmemLayout::ALLOC > 116 * 1024, "one CTA per SM keeps the tensor-memory allocation uncontended");
-static_assert(SmemLayout::ALLOC <= 227 * 1024, "shared memory per CTA");
 
+// Work item = (row tile, token tile, K range): with n_ks > 1 the super-blocks of a row tile are
+// split over several CTAs (sb_per each), which write fp32 partial sums for tc_split_reduce_kernel.
 struct TcKernelArgs {
-  int n_rows, row_bytes, nb, m, n_tt, n_rt;
+  int n_rows, row_bytes, nb, m, n_tt, n_rt, n_ks, sb_per;
   const uint8_t* w;       // Q4_K rows (header of each super-block for the epilogue)
-  const uint8_t* bt;      // activation tiles [n_tt][nb][2][16 KB]
-  const uint8_t* aux;     // [n_tt][nb][AUX_BYTES]: d[128] floats, sums[128][4] words of two int16
+  const uint8_t* bt;      // activation tiles [n_tt][nb][2][B_TILE]
+  const uint8_t* aux;     // [n_tt][nb][AUX_BYTES]: d[BN] floats, sums[BN][4] words of two int16
   const float* bias;
   float* out;
   long long out_stride;
+  float* part;            // n_ks > 1: partial sums [n_ks][m][n_rows]
   int32_t* partials;      // non-null: write (sumi, summ) per (token, row, super-block) instead of out
   uint32_t* status;
 };
+
+// Row tile, token tile and super-block range of work item `tile` (128-token tiles are never split).
+template <int BN>
+__device__ __forceinline__ void tc_item(const TcKernelArgs& a, long long tile, int& rt, int& tt, int& ks, int& sb0,
+                                        int& sb1) {
+  if constexpr (BN == 128) {
+    rt = (int)(tile / a.n_tt);
+    tt = (int)(tile - (long long)rt * a.n_tt);
+    ks = 0;
+    sb0 = 0;
+    sb1 = a.nb;
+    return;
+  }
+  const long long per_rt = (long long)a.n_tt * a.n_ks;
+  rt = (int)(tile / per_rt);
+  const int rem = (int)(tile - (long long)rt * per_rt);
+  tt = rem / a.n_ks;
+  ks = rem - tt * a.n_ks;
+  sb0 = ks * a.sb_per;
+  sb1 = min(a.nb, sb0 + a.sb_per);
+}
 
 // ---- tcgen05 / TMA wrappers -------------------------------------------------------------------
 
@@ -133,12 +162,12 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t addr, uint32_t ncols) {
 }
 
 // D[tmem] += A[smem descriptor] x B[smem descriptor]
-__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc) {
+__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, 1, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(IDESC_I8)
+      "l"(a_desc), "l"(b_desc), "r"(idesc)
       : "memory");
 }
 
@@ -198,17 +227,17 @@ __host__ __device__ __forceinline__ int sw128_chunk(int r, int c) {
 // edgexpu_gguf_quantize_q8_k) or take them from a Q8_K row, scatter the int8 values into the two
 // swizzled K-half tiles, and store d and the eight 32-element sums S_j = bsum_2j + bsum_2j+1 as
 // int16 pairs (|S_j| <= 32 * 127).  Rows past m are written as zeros.
-template <bool FROM_F32>
+template <bool FROM_F32, int BN>
 __global__ void __launch_bounds__(256) tc_pack_kernel(const float* __restrict__ x, const uint8_t* __restrict__ xq,
                                                       int m, int K, uint8_t* __restrict__ bt,
                                                       uint8_t* __restrict__ aux) {
   const int nb = K / QK_K;
   const int lane = threadIdx.x & 31;
   const long long gw = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int n_tt = (m + TC_BN - 1) / TC_BN;
-  if (gw >= (long long)n_tt * TC_BN * nb) return;
+  const int n_tt = (m + BN - 1) / BN;
+  if (gw >= (long long)n_tt * BN * nb) return;
   const int t = (int)(gw / nb), sb = (int)(gw % nb);
-  const int tt = t / TC_BN, r = t % TC_BN;
+  const int tt = t / BN, r = t % BN;
   uint32_t w0 = 0, w1 = 0;
   float d = 0.0f;
   int s8 = 0;  // this lane's share of its 32-element sum
@@ -237,7 +266,7 @@ __global__ void __launch_bounds__(256) tc_pack_kernel(const float* __restrict__ 
     }
   }
   const int kh = lane >> 4, kb = (lane & 15) * 8;
-  uint8_t* tile = bt + (((size_t)tt * nb + sb) * 2 + kh) * B_TILE;
+  uint8_t* tile = bt + (((size_t)tt * nb + sb) * 2 + kh) * Cfg<BN>::B_TILE;
   *reinterpret_cast<uint2*>(tile + sw128_chunk(r, kb >> 4) + (kb & 15)) = make_uint2(w0, w1);
   // 32-element sums: lanes 4j..4j+3 hold sub-block j
   int s32 = s8 + __shfl_xor_sync(0xFFFFFFFFu, s8, 1);
@@ -250,9 +279,9 @@ __global__ void __launch_bounds__(256) tc_pack_kernel(const float* __restrict__ 
     dig[j >> 1] |= v << (16 * (j & 1));
   }
   if (lane == 0) {
-    uint8_t* xa = aux + ((size_t)tt * nb + sb) * AUX_BYTES;
+    uint8_t* xa = aux + ((size_t)tt * nb + sb) * Cfg<BN>::AUX_BYTES;
     reinterpret_cast<float*>(xa)[r] = d;
-    *reinterpret_cast<uint4*>(xa + AUX_DX + r * 16) = make_uint4(dig[0], dig[1], dig[2], dig[3]);
+    *reinterpret_cast<uint4*>(xa + Cfg<BN>::AUX_DX + r * 16) = make_uint4(dig[0], dig[1], dig[2], dig[3]);
   }
 }
 
@@ -297,16 +326,17 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, uint32_t* 
 }
 
 // PARTIALS: write the exact (sumi, summ) per block instead of the fp32 outputs (test hook).
-template <bool PARTIALS>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+template <bool PARTIALS, int BN>
+__global__ void __launch_bounds__(Cfg<BN>::THREADS, 1)
     gemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap wmap, const TcKernelArgs a) {
+  using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ast = smem + SmemLayout::A_OFF;
-  uint8_t* bst = smem + SmemLayout::B_OFF;
-  uint8_t* rst = smem + SmemLayout::R_OFF;
-  uint8_t* xst = smem + SmemLayout::X_OFF;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::BAR_OFF);
+  uint8_t* ast = smem + C::A_OFF;
+  uint8_t* bst = smem + C::B_OFF;
+  uint8_t* rst = smem + C::R_OFF;
+  uint8_t* xst = smem + C::X_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* a_full = bars;                // A tiles of a stage written (4 converter warps)
   uint64_t* b_full = a_full + N_STAGES;   // B tile of a stage landed (producer, tx bytes)
   uint64_t* empty = b_full + N_STAGES;    // the MMAs of a stage completed
@@ -317,8 +347,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* acc_full = x_empty + NX_STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* fin = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SmemLayout::MISC_OFF);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::MISC_OFF + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -333,18 +363,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < NX_STAGES; ++i) {
       mbar_init(&x_full[i], 1);
-      mbar_init(&x_empty[i], N_EPI_WARPS);
+      mbar_init(&x_empty[i], C::N_EPI_WARPS);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], N_EPI_WARPS);
+      mbar_init(&acc_empty[i], C::N_EPI_WARPS);
     }
     mbar_init(fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == WARP_MMA) {  // warp 1 has not diverged: the warp-collective allocation is converged
-    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -353,7 +383,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   const int nb = a.nb, n_tt = a.n_tt;
-  const long long n_tiles = (long long)a.n_rt * n_tt;
+  const long long n_tiles = (long long)a.n_rt * n_tt * (BN == 128 ? 1 : a.n_ks);
 
   if (warp == WARP_PROD) {
     if (lane == 0) {
@@ -362,8 +392,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       long long b_issued = 0, r_issued = 0, x_issued = 0;
       bool ok = true;
       for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-        const int rt = (int)(tile / n_tt), tt = (int)(tile % n_tt);
-        for (int sb = 0; ok && sb < nb; ++sb) {
+        int rt, tt, ks, sb0, sb1;
+        tc_item<BN>(a, tile, rt, tt, ks, sb0, sb1);
+        for (int sb = sb0; ok && sb < sb1; ++sb) {
           if (!wait_or_abort(&r_empty[rs], rph ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -379,8 +410,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&x_full[xs], AUX_BYTES);
-          bulk_g2s(xst + xs * AUX_BYTES, a.aux + ((size_t)tt * nb + sb) * AUX_BYTES, AUX_BYTES, &x_full[xs], pol);
+          mbar_arrive_expect_tx(&x_full[xs], C::AUX_BYTES);
+          bulk_g2s(xst + xs * C::AUX_BYTES, a.aux + ((size_t)tt * nb + sb) * C::AUX_BYTES, C::AUX_BYTES, &x_full[xs], pol);
           ++x_issued;
           if (++xs == NX_STAGES) {
             xs = 0;
@@ -391,8 +422,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&b_full[s], B_TILE);
-            bulk_g2s(bst + s * B_TILE, a.bt + (((size_t)tt * nb + sb) * 2 + kh) * B_TILE, B_TILE, &b_full[s], pol);
+            mbar_arrive_expect_tx(&b_full[s], C::B_TILE);
+            bulk_g2s(bst + s * C::B_TILE, a.bt + (((size_t)tt * nb + sb) * 2 + kh) * C::B_TILE, C::B_TILE, &b_full[s], pol);
             ++b_issued;
             if (++s == N_STAGES) {
               s = 0;
@@ -417,13 +448,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t s = 0, ph = 0, accb = 0;
       bool ok = true;
       for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-        for (int sb = 0; ok && sb < nb; ++sb) {
+        int rt, tt, ks, sb0, sb1;
+        tc_item<BN>(a, tile, rt, tt, ks, sb0, sb1);
+        for (int sb = sb0; ok && sb < sb1; ++sb) {
           const uint32_t ab = accb & 1u;
           if (!spin_wait(&acc_empty[ab], (accb >> 1) & 1u, abort_flag)) {
             ok = false;
             break;
           }
-          const uint32_t d_l = tmem + ab * ACC_COLS, d_h = d_l + TC_BN;
+          const uint32_t d_l = tmem + ab * C::ACC_COLS, d_h = d_l + BN;
           for (int kh = 0; kh < 2; ++kh) {
             if (!spin_wait(&b_full[s], ph, abort_flag) || !spin_wait(&a_full[s], ph, abort_flag)) {
               ok = false;
@@ -432,12 +465,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tc_fence_after();
             const uint64_t al = sw128_desc(smem_u32(ast + s * 2 * A_TILE));
             const uint64_t ah = sw128_desc(smem_u32(ast + s * 2 * A_TILE + A_TILE));
-            const uint64_t bd = sw128_desc(smem_u32(bst + s * B_TILE));
+            const uint64_t bd = sw128_desc(smem_u32(bst + s * C::B_TILE));
 #pragma unroll
             for (int ks = 0; ks < KH_BYTES / 32; ++ks) {
               const uint64_t k = (uint64_t)((ks * 32) >> 4);
-              mma_i8_ss(d_l, al + k, bd + k);
-              mma_i8_ss(d_h, ah + k, bd + k);
+              mma_i8_ss(d_l, al + k, bd + k, C::IDESC);
+              mma_i8_ss(d_h, ah + k, bd + k, C::IDESC);
             }
             tc_commit(&empty[s]);
             if (++s == N_STAGES) {
@@ -462,7 +495,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint32_t s = 0, ph = 0, rs = 0, rph = 0;
     bool ok = true;
     for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-      for (int sb = 0; ok && sb < nb; ++sb) {
+      int rt, tt, ks, sb0, sb1;
+      tc_item<BN>(a, tile, rt, tt, ks, sb0, sb1);
+      for (int sb = sb0; ok && sb < sb1; ++sb) {
         if (!warp_wait(&r_full[rs], rph, abort_flag)) {
           ok = false;
           break;
@@ -516,7 +551,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else {
     // Epilogue: quadrant q (rows 32q + lane), token half j (tokens 64j..64j+63 of the tile).
     const int q = warp & 3, j = (warp - WARP_EPI0) >> 2;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(EPI_TOK * j);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(C::EPI_TOK * j);
     uint32_t bias8[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) bias8[k] = ACC_BIAS;
@@ -525,7 +560,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
       for (int p = 0; p < 2; ++p)
 #pragma unroll
-        for (int h = 0; h < EPI_TOK / 8; ++h) tmem_st8(lane_base + b * ACC_COLS + p * TC_BN + 8 * h, bias8);
+        for (int h = 0; h < C::EPI_TOK / 8; ++h) tmem_st8(lane_base + b * C::ACC_COLS + p * BN + 8 * h, bias8);
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
@@ -536,45 +571,46 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint32_t accb = 0, xs = 0, xph = 0;
     bool ok = true;
     for (long long tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-      const int rt = (int)(tile / n_tt), tt = (int)(tile % n_tt);
+      int rt, tt, ks, sb0, sb1;
+      tc_item<BN>(a, tile, rt, tt, ks, sb0, sb1);
       const int n = rt * TC_BM + 32 * q + lane;
       const bool valid = n < a.n_rows;
       const uint8_t* rowp = a.w + (size_t)(valid ? n : 0) * a.row_bytes;
-      const int t0 = tt * TC_BN + EPI_TOK * j;
-      float acc[EPI_TOK];
+      const int t0 = tt * BN + C::EPI_TOK * j;
+      float acc[C::EPI_TOK];
 #pragma unroll
-      for (int e = 0; e < EPI_TOK; ++e) acc[e] = 0.0f;
-      uint4 hdr = __ldg(reinterpret_cast<const uint4*>(rowp));
-      for (int sb = 0; sb < nb; ++sb) {
+      for (int e = 0; e < C::EPI_TOK; ++e) acc[e] = 0.0f;
+      uint4 hdr = __ldg(reinterpret_cast<const uint4*>(rowp + sb0 * Q4_K_BYTES));
+      for (int sb = sb0; sb < sb1; ++sb) {
         const float dw = fp16_bits_to_float(hdr.x), dmw = fp16_bits_to_float(hdr.x >> 16);
         uint32_t sc4, m03, m47;
         q4k_scales_half(hdr.y, hdr.z, hdr.w, 0, sc4, m03);
         q4k_scales_half(hdr.y, hdr.z, hdr.w, 1, sc4, m47);
-        if (sb + 1 < nb) hdr = __ldg(reinterpret_cast<const uint4*>(rowp + (sb + 1) * Q4_K_BYTES));
+        if (sb + 1 < sb1) hdr = __ldg(reinterpret_cast<const uint4*>(rowp + (sb + 1) * Q4_K_BYTES));
         const uint32_t ab = accb & 1u;
         if (!warp_wait(&x_full[xs], xph, abort_flag) || !warp_wait(&acc_full[ab], (accb >> 1) & 1u, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float* dxs = reinterpret_cast<const float*>(xst + xs * AUX_BYTES) + EPI_TOK * j;
-        const uint4* dgs = reinterpret_cast<const uint4*>(xst + xs * AUX_BYTES + AUX_DX) + EPI_TOK * j;
-        const uint32_t col = lane_base + ab * ACC_COLS;
+        const float* dxs = reinterpret_cast<const float*>(xst + xs * C::AUX_BYTES) + C::EPI_TOK * j;
+        const uint4* dgs = reinterpret_cast<const uint4*>(xst + xs * C::AUX_BYTES + C::AUX_DX) + C::EPI_TOK * j;
+        const uint32_t col = lane_base + ab * C::ACC_COLS;
         // One group = EG tokens.  The loads of group h + 1 are issued right after the wait for
         // group h, so their latency overlaps the arithmetic of group h.
         uint32_t Lb[2][EG], Hb[2][EG];
         tmem_ld8(col, Lb[0]);
-        tmem_ld8(col + TC_BN, Hb[0]);
+        tmem_ld8(col + BN, Hb[0]);
 #pragma unroll
-        for (int h = 0; h < EPI_TOK / EG; ++h) {
+        for (int h = 0; h < C::EPI_TOK / EG; ++h) {
           const int c = h & 1;
           __syncwarp();  // tcgen05.ld/st are warp-collective; the partials stores below diverge
           tmem_wait_ld();
           tmem_st8(col + EG * h, bias8);
-          tmem_st8(col + TC_BN + EG * h, bias8);
-          if (h + 1 < EPI_TOK / EG) {
+          tmem_st8(col + BN + EG * h, bias8);
+          if (h + 1 < C::EPI_TOK / EG) {
             tmem_ld8(col + EG * (h + 1), Lb[c ^ 1]);
-            tmem_ld8(col + TC_BN + EG * (h + 1), Hb[c ^ 1]);
+            tmem_ld8(col + BN + EG * (h + 1), Hb[c ^ 1]);
           }
 #pragma unroll
           for (int e = 0; e < EG; ++e) {
@@ -617,11 +653,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       if (!ok) break;
       if (!PARTIALS && valid) {
-        const float bv = a.bias != nullptr ? a.bias[n] : 0.0f;
+        if (BN == 128 || a.n_ks == 1) {
+          const float bv = a.bias != nullptr ? a.bias[n] : 0.0f;
 #pragma unroll
-        for (int e = 0; e < EPI_TOK; ++e) {
-          const int t = t0 + e;
-          if (t < a.m) a.out[(size_t)t * a.out_stride + n] = acc[e] + bv;
+          for (int e = 0; e < C::EPI_TOK; ++e) {
+            const int t = t0 + e;
+            if (t < a.m) a.out[(size_t)t * a.out_stride + n] = acc[e] + bv;
+          }
+        } else if constexpr (BN == 16) {  // this K range's sum, for tc_split_reduce_kernel
+#pragma unroll
+          for (int e = 0; e < C::EPI_TOK; ++e) {
+            const int t = t0 + e;
+            if (t < a.m) a.part[((size_t)ks * a.m + t) * a.n_rows + n] = acc[e];
+          }
         }
       }
     }
@@ -633,7 +677,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   if (warp == WARP_MMA) {
     __syncwarp();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// out[t][n] = bias[n] + sum over the K ranges of part[ks][t][n], in K-range order (deterministic).
+__global__ void tc_split_reduce_kernel(const float* __restrict__ part, int n_ks, int m, int n_rows,
+                                       const float* __restrict__ bias, float* __restrict__ out, long long out_stride) {
+  const long long total = (long long)m * n_rows;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(i / n_rows), n = (int)(i - (long long)t * n_rows);
+    float acc = part[i];
+    for (int k = 1; k < n_ks; ++k) acc += part[(size_t)k * total + i];
+    out[(size_t)t * out_stride + n] = acc + (bias != nullptr ? bias[n] : 0.0f);
   }
 }
 
@@ -657,24 +713,58 @@ EncodeTiledFn encode_tiled() {
 
 }  // namespace
 
+// Token tile of a batch of m tokens: 16 below the prefill threshold, else 128.
+static int tc_bn(int m) { return m < TC_MIN_M ? 16 : 128; }
+
 size_t tc_act_bytes(int m, int K) {
-  const size_t n_tt = (size_t)(m + TC_BN - 1) / TC_BN, nb = (size_t)K / QK_K;
-  return n_tt * nb * (2 * B_TILE + AUX_BYTES);
+  const int bn = tc_bn(m);
+  const size_t n_tt = (size_t)(m + bn - 1) / bn, nb = (size_t)K / QK_K;
+  return bn == 16 ? n_tt * nb * (2 * Cfg<16>::B_TILE + Cfg<16>::AUX_BYTES)
+                  : n_tt * nb * (2 * Cfg<128>::B_TILE + Cfg<128>::AUX_BYTES);
+}
+
+// K split of a launch: with 16-token tiles the row tiles alone leave most SMs idle, so the
+// super-blocks of each row tile are split (at least 2 per range) until there are about two work
+// items per SM.  128-token tiles are not split.
+static void tc_split(int m, int n_rows, int K, const DeviceInfo& dev, int& n_ks, int& sb_per) {
+  const int nb = K / QK_K, bn = tc_bn(m);
+  const long long base = (long long)((n_rows + TC_BM - 1) / TC_BM) * ((m + bn - 1) / bn);
+  n_ks = 1;
+  if (bn == 16 && base < 2LL * dev.sm_count) {
+    long long want = (2LL * dev.sm_count + base - 1) / base;
+    if (want > nb / 2) want = nb / 2;
+    n_ks = want < 1 ? 1 : (int)want;
+  }
+  sb_per = (nb + n_ks - 1) / n_ks;
+  n_ks = (nb + sb_per - 1) / sb_per;
+}
+
+size_t tc_split_bytes(int m, int n_rows, int K, const DeviceInfo& dev) {
+  int n_ks, sb_per;
+  tc_split(m, n_rows, K, dev, n_ks, sb_per);
+  return n_ks > 1 ? (size_t)n_ks * m * n_rows * sizeof(float) : 0;
+}
+
+template <int BN>
+static cudaError_t launch_pack_bn(bool from_f32, const float* x, const uint8_t* xq, int m, int K, uint8_t* act,
+                                  cudaStream_t st) {
+  const int n_tt = (m + BN - 1) / BN, nb = K / QK_K;
+  uint8_t* bt = act;
+  uint8_t* aux = act + (size_t)n_tt * nb * 2 * Cfg<BN>::B_TILE;
+  const long long warps = (long long)n_tt * BN * nb;
+  const unsigned grid = (unsigned)((warps + 7) / 8);
+  if (from_f32)
+    tc_pack_kernel<true, BN><<<grid, 256, 0, st>>>(x, nullptr, m, K, bt, aux);
+  else
+    tc_pack_kernel<false, BN><<<grid, 256, 0, st>>>(nullptr, xq, m, K, bt, aux);
+  return cudaGetLastError();
 }
 
 static cudaError_t launch_pack(bool from_f32, const float* x, const uint8_t* xq, int m, int K, uint8_t* act,
                                cudaStream_t st) {
   if (m <= 0 || K <= 0 || K % QK_K != 0) return cudaErrorInvalidValue;
-  const int n_tt = (m + TC_BN - 1) / TC_BN, nb = K / QK_K;
-  uint8_t* bt = act;
-  uint8_t* aux = act + (size_t)n_tt * nb * 2 * B_TILE;
-  const long long warps = (long long)n_tt * TC_BN * nb;
-  const unsigned grid = (unsigned)((warps + 7) / 8);
-  if (from_f32)
-    tc_pack_kernel<true><<<grid, 256, 0, st>>>(x, nullptr, m, K, bt, aux);
-  else
-    tc_pack_kernel<false><<<grid, 256, 0, st>>>(nullptr, xq, m, K, bt, aux);
-  return cudaGetLastError();
+  return tc_bn(m) == 16 ? launch_pack_bn<16>(from_f32, x, xq, m, K, act, st)
+                        : launch_pack_bn<128>(from_f32, x, xq, m, K, act, st);
 }
 
 cudaError_t launch_tc_pack_f32(const float* x, int m, int K, uint8_t* act, cudaStream_t st) {
@@ -685,12 +775,31 @@ cudaError_t launch_tc_pack_q8k(const uint8_t* xq, int m, int K, uint8_t* act, cu
   return launch_pack(false, nullptr, xq, m, K, act, st);
 }
 
+template <int BN>
+static cudaError_t launch_gemm_bn(const CUtensorMap& map, const TcKernelArgs& k, int grid, cudaStream_t st) {
+  static bool attr_set = false;  // per instantiation; the host API serialises its callers
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc_kernel<false, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg<BN>::ALLOC);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_q4k_tc_kernel<true, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Cfg<BN>::ALLOC);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  if (k.partials != nullptr)
+    gemm_q4k_tc_kernel<true, BN><<<grid, Cfg<BN>::THREADS, Cfg<BN>::ALLOC, st>>>(map, k);
+  else
+    gemm_q4k_tc_kernel<false, BN><<<grid, Cfg<BN>::THREADS, Cfg<BN>::ALLOC, st>>>(map, k);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_tc_gemm(const TcGemmArgs& g, const DeviceInfo& dev, cudaStream_t st) {
   if (g.n_rows <= 0 || g.m <= 0 || g.K <= 0 || g.K % QK_K != 0) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(g.w) & 15u) != 0) return cudaErrorMisalignedAddress;
   EncodeTiledFn enc = encode_tiled();
   if (enc == nullptr) return cudaErrorNotSupported;
-  const int nb = g.K / QK_K, row_bytes = nb * Q4_K_BYTES;
+  const int nb = g.K / QK_K, row_bytes = nb * Q4_K_BYTES, bn = tc_bn(g.m);
   // The weight as a 2-D byte array [n_rows][row_bytes]; one box = one super-block of 128 rows.
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
@@ -708,33 +817,28 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& g, const DeviceInfo& dev, cudaStrea
   k.row_bytes = row_bytes;
   k.nb = nb;
   k.m = g.m;
-  k.n_tt = (g.m + TC_BN - 1) / TC_BN;
+  k.n_tt = (g.m + bn - 1) / bn;
   k.n_rt = (g.n_rows + TC_BM - 1) / TC_BM;
+  tc_split(g.m, g.n_rows, g.K, dev, k.n_ks, k.sb_per);
+  // (the exact partials are written per super-block, so a split needs no partial sums there)
+  if (g.partials == nullptr && k.n_ks > 1 && g.part == nullptr) return cudaErrorInvalidValue;
   k.w = g.w;
   k.bt = g.act;
-  k.aux = g.act + (size_t)k.n_tt * nb * 2 * B_TILE;
+  k.aux = g.act + (size_t)k.n_tt * nb * 2 * (bn == 16 ? Cfg<16>::B_TILE : Cfg<128>::B_TILE);
   k.bias = g.bias;
   k.out = g.out;
   k.out_stride = g.out_stride;
+  k.part = g.part;
   k.partials = g.partials;
   k.status = g.status;
 
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_q4k_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SmemLayout::ALLOC);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemm_q4k_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               SmemLayout::ALLOC);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
-  const long long tiles = (long long)k.n_tt * k.n_rt;
+  const long long tiles = (long long)k.n_tt * k.n_rt * k.n_ks;
   const int grid = (int)(tiles < dev.sm_count ? tiles : dev.sm_count);
-  if (k.partials != nullptr)
-    gemm_q4k_tc_kernel<true><<<grid, TC_THREADS, SmemLayout::ALLOC, st>>>(map, k);
-  else
-    gemm_q4k_tc_kernel<false><<<grid, TC_THREADS, SmemLayout::ALLOC, st>>>(map, k);
+  cudaError_t e = bn == 16 ? launch_gemm_bn<16>(map, k, grid, st) : launch_gemm_bn<128>(map, k, grid, st);
+  if (e != cudaSuccess || g.partials != nullptr || k.n_ks == 1) return e;
+  const long long total = (long long)g.m * g.n_rows;
+  const int rgrid = (int)((total + 255) / 256 < 4LL * dev.sm_count ? (total + 255) / 256 : 4LL * dev.sm_count);
+  tc_split_reduce_kernel<<<rgrid, 256, 0, st>>>(g.part, k.n_ks, g.m, g.n_rows, g.bias, g.out, g.out_stride);
   return cudaGetLastError();
 }
 

@@ -177,6 +177,9 @@ cudaError_t launch_rowstream(const RowStreamArgs& a, const DeviceInfo& dev, cuda
 
 // Smallest batch routed to the tensor-core GEMM instead of the row-stream GEMV.
 constexpr int TC_MIN_M = 64;
+// Smallest batch routed to the tensor-core GEMM's 16-token tiles (batches below TC_MIN_M; the K
+// range of a row tile is split over several CTAs whose partial sums a second kernel adds).
+constexpr int TC_SMALL_MIN_M = 9;
 
 // Bytes of the packed activations of m rows of length K (swizzled int8 tiles + per-block d).
 size_t tc_act_bytes(int m, int K);
@@ -197,7 +200,11 @@ struct TcGemmArgs {
   long long out_stride;
   int32_t* partials;     // non-null: (sumi, summ) per [t][row][super-block] instead of out
   uint32_t* status;      // device status word
+  float* part;           // tc_split_bytes(m, n_rows, K) bytes of scratch (when nonzero) for K-split sums
 };
+
+// Scratch for the partial sums of a K-split launch (0: the launch is not split).
+size_t tc_split_bytes(int m, int n_rows, int K, const DeviceInfo& dev);
 
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, const DeviceInfo& dev, cudaStream_t st);
 

@@ -66,6 +66,11 @@ def _partials(gpu, h, xq, m, n_out, n_in):
     (300, 1024, 64),    # ragged row tile
     (200, 512, 100),    # ragged token tile
     (257, 4096, 130),   # both ragged, 16 super-blocks, 3 token tiles
+    # 16-token tiles (batches of 9..63), K split over CTAs where the row tiles alone leave SMs idle
+    (128, 256, 63),     # one super-block: no split, 4 token tiles
+    (300, 1024, 9),     # ragged row tile, 4 super-blocks in 2 ranges
+    (257, 4096, 16),    # 16 super-blocks in 8 ranges, one full token tile
+    (1000, 14336, 33),  # down-projection width: 56 super-blocks, 3 token tiles
 ])
 def test_gemm_partials_bit_exact(gpu, port, n_out, n_in, m):
     s = _synth()
@@ -82,6 +87,7 @@ def test_gemm_partials_bit_exact(gpu, port, n_out, n_in, m):
         gpu.free_weight(h)
 
 
+@pytest.mark.parametrize("m", [64, 16])
 @pytest.mark.parametrize("sc,mn,q,lead", [
     (32, 63, 4, False),   # sc*q4 = 128: every low part is -128, q8 = -127 -> L = +128*127*256, the largest L
     (32, 63, 4, True),    # first element negated: q8 = +127 elsewhere -> L near -128*127*256
@@ -89,10 +95,11 @@ def test_gemm_partials_bit_exact(gpu, port, n_out, n_in, m):
     (17, 0, 15, True),    # sc*q4 = 255: high part 1, low part -1
     (63, 63, 0, False),   # zero nibbles: only the mins term
 ])
-def test_gemm_accumulator_extremes(gpu, port, sc, mn, q, lead):
+def test_gemm_accumulator_extremes(gpu, port, sc, mn, q, lead, m):
     """Q8_K maps the first largest |x| of a block to -127 (gguf_dot_q8.c:377-392): constant rows
-    give q8 = -127 everywhere, a negated first element gives q8 = +127 everywhere else."""
-    n_out, n_in, m = 128, 1024, 64
+    give q8 = -127 everywhere, a negated first element gives q8 = +127 everywhere else.  At m = 16 the
+    16-token tiles run with the K range split."""
+    n_out, n_in = 128, 1024
     w = uniform_q4k(n_out, n_in, [sc] * 8, [mn] * 8, q)
     x = np.full((m, n_in), 3.0, np.float32)
     if lead:
@@ -113,6 +120,10 @@ def test_gemm_accumulator_extremes(gpu, port, sc, mn, q, lead):
     (300, 1024, 100, True),
     (1000, 14336, 70, False),    # down-projection width
     (6144, 4096, 65, True),      # fused q|k|v width, one token past a tile
+    (4096, 4096, 16, False),     # config 2/4 batch 16: 16-token tile, K split in 8
+    (14336, 4096, 9, True),      # gate width at the smallest routed batch
+    (4096, 14336, 16, False),    # down projection at batch 16
+    (300, 1024, 40, True),       # 3 token tiles, ragged rows
 ])
 def test_gemm_linear_matches_oracle(gpu, port, n_out, n_in, m, with_bias):
     s = _synth()
