@@ -28,7 +28,12 @@
 // from shared memory: A (the expanded weight, L and H parts) and B (activations) are K-major
 // tiles with the 128-byte swizzle, one K-half (128 elements) per pipeline stage.
 //
-// Warp roles (22 warps):
+// Batches of 9..63 tokens use the same kernel with 16-token tiles (template parameter BN):
+// N = 16 MMAs, 64 tensor-memory columns, one epilogue warp per quadrant (10 warps), and the
+// super-blocks of each row tile split into K ranges over several CTAs, whose fp32 partial sums
+// tc_split_reduce_kernel adds in range order.
+//
+// Warp roles (22 warps with 128-token tiles):
 //   0      producer: 2-D TMA of the raw Q4_K super-block of 128 rows (tensor map, zero-filled
 //          past the last row), bulk copies of activation tiles and per-token scale data
 //   1      tensor-memory allocation and the single-thread MMA issuer
@@ -37,11 +42,12 @@
 //          of the next 8-token group in flight while the current one is computed), mins term,
 //          scale, accumulate in fp32 registers, store
 // The epilogue is the busiest role (about 12 operations per output and super-block), so it
-// gets most of the warps; 4 warps per quadrant and 8-token load groups measured fastest.
+// gets most of the warps; 4 warps per quadrant and 8-token load groups measured fastest with
+// 128-token tiles.
 // Every wait is bounded; a timeout sets a status bit, raises the CTA abort flag and all roles
 // fall through to teardown (copies drained, MMAs committed, tensor memory freed).  The kernel
-// needs a whole SM (about 196 KB of shared memory), so the 512-column tensor-memory allocation
-// is never contended by another CTA.
+// needs a whole SM (about 196 / 140 KB of shared memory), so its tensor-memory allocation is
+// never contended by another CTA.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
