@@ -36,6 +36,10 @@ Workloads (``--workload``):
   ``--batch`` tokens (default 2048), run by the tensor-core GEMM (tcgen05 kind::i8).  Metric:
   useful int8 TOPS (2 * M * N * K per projection); the tensor roofline is 2 x the measured bf16
   peak (B200's dense int8 rate is twice bf16).
+* ``gemv``: one product per step, ``--shape n_out,n_in`` at ``--batch`` rows of weight type
+  ``--wtype`` (configurations 0 and 2 name Q8_0 and Q4_K; Q4_0, Q5_0, Q5_K and Q6_K run on the
+  same shapes), each step over the next of several weight copies that together exceed L2.  The
+  line adds the kernel alone (activations pre-quantized) as the roofline.  No reference arm.
 
 Arms: ``--impl ours`` (default) times the CUDA path; ``--impl reference`` times the reference's
 own CPU implementation (oracle/_ref, compiled from the reference sources) on this host's cores.
@@ -62,7 +66,15 @@ REF_DRIVER = ROOT / "oracle" / "_ref" / "libedgexpu_ref_driver.so"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 TRAFFIC = ROOT / "profiles" / "traffic.json"
 
-TYPE_Q8_0, TYPE_Q4_K = 8, 12
+TYPE_Q4_0, TYPE_Q5_0, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q6_K = 2, 6, 8, 12, 13, 14
+# GGUF weight types of the gemv workload: type id, (block elements, block bytes), arithmetic
+WTYPES = {"q4_0": TYPE_Q4_0, "q5_0": TYPE_Q5_0, "q8_0": TYPE_Q8_0, "q4_k": TYPE_Q4_K, "q5_k": TYPE_Q5_K,
+          "q6_k": TYPE_Q6_K}
+BLOCKS = {TYPE_Q4_0: (32, 18), TYPE_Q5_0: (32, 22), TYPE_Q8_0: (32, 34), TYPE_Q4_K: (256, 144),
+          TYPE_Q5_K: (256, 176), TYPE_Q6_K: (256, 210)}
+DTYPES = {TYPE_Q4_0: "u4 x i8 -> i32 -> f32", TYPE_Q5_0: "u5 x i8 -> i32 -> f32", TYPE_Q8_0: "i8 x i8 -> i32 -> f32",
+          TYPE_Q4_K: "u4/i8 x i8 -> i32 -> f32", TYPE_Q5_K: "u5/i8 x i8 -> i32 -> f32",
+          TYPE_Q6_K: "u6/i8 x i8 -> i32 -> f32"}
 GROUP_WITH_PREV = {"attn_k", "attn_v", "ffn_up"}  # read the same activations as the projection before
 FALLBACK_HBM_GBS = 6650.0
 
@@ -96,11 +108,13 @@ def load_pkg():
 
 
 def row_bytes(t, n):
-    return n // 32 * 34 if t == TYPE_Q8_0 else n // 256 * 144
+    qk, bb = BLOCKS[t]
+    return n // qk * bb
 
 
 def act_bytes(t, n):
-    return n // 32 * 34 if t == TYPE_Q8_0 else n // 256 * 292
+    """Bytes of one quantized activation row: Q8_0 blocks for the 32-element types, Q8_K for the K-quants."""
+    return n // 32 * 34 if BLOCKS[t][0] == 32 else n // 256 * 292
 
 
 def linear_alg_bytes(t, n_out, n_in, m):
@@ -747,7 +761,7 @@ def run_gemv(args):
     pkg.init(local)
     set_float_order(cuda, args)
     dev = torch.device("cuda", local)
-    t = TYPE_Q4_K if args.wtype == "q4_k" else TYPE_Q8_0
+    t = WTYPES[args.wtype]
     n_out, n_in = (int(v) for v in args.shape.split(","))
     m = args.batch
     wb = n_out * row_bytes(t, n_in)
@@ -844,10 +858,10 @@ def run_gemv(args):
     if err:
         raise RuntimeError(err.decode())
     line = {
-        "metric": f"{'Q4_K' if t == TYPE_Q4_K else 'Q8_0'} GEMV HBM GB/s ({n_out}x{n_in}, batch {m})",
+        "metric": f"{args.wtype.upper()} GEMV HBM GB/s ({n_out}x{n_in}, batch {m})",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u4/i8 x i8 -> i32 -> f32" if t == TYPE_Q4_K else "i8 x i8 -> i32 -> f32",
+        "dtype": DTYPES[t],
         "data": "synthetic (seeded random-init GGUF blocks generated in HBM)",
         "config": {"workload": "gemv", "type": args.wtype, "n_out": n_out, "n_in": n_in, "batch": m,
                    "weight_copies": copies, "l2": f"rotating {copies} weight copies ({copies * wb} bytes) > L2",
@@ -1411,7 +1425,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["gemv", "llama3_8b_q4k_prefill", "native_greedy",
                                                               "device_decode"],
                     default="llama3_8b_q4k_decode")
-    ap.add_argument("--wtype", choices=["q4_k", "q8_0"], default="q4_k", help="gemv workload: weight type")
+    ap.add_argument("--wtype", choices=sorted(WTYPES), default="q4_k",
+                    help="gemv workload: weight type; prefill workload: q4_k or q8_0")
     ap.add_argument("--shape", default="14336,4096", help="gemv workload: n_out,n_in")
     ap.add_argument("--rotate-bytes", type=float, default=512e6, help="gemv workload: total bytes of weight copies")
     ap.add_argument("--batch", type=int, default=0, help="tokens per step (default 1 for decode, 2048 for prefill)")
@@ -1434,6 +1449,8 @@ def main():
     if args.batch <= 0:
         args.batch = 2048 if args.workload == "llama3_8b_q4k_prefill" else 1
     if args.workload == "llama3_8b_q4k_prefill":
+        if args.wtype not in ("q4_k", "q8_0"):
+            ap.error("the prefill workload runs the Q4_K and Q8_0 tensor-core GEMMs: --wtype q4_k or q8_0")
         (run_prefill_reference if args.impl == "reference" else run_prefill)(args)
         return
     if args.workload == "device_decode":

@@ -101,21 +101,28 @@ def torch_weight(wtype: int, n_out: int, n_in: int, generator, device, pad: int 
     """Same recipe generated on the device; returns a flat uint8 tensor with `pad` spare bytes."""
     import torch
 
-    if wtype == 8:
-        nb, bb, lo, hi = n_in // 32, Q8_0_BYTES, 1e-4, 2e-3
-    else:
-        nb, bb, lo, hi = n_in // 256, Q4_K_BYTES, 1e-4, 1e-3
-    nblk = n_out * nb
+    qk, bb = BLOCK[wtype]
+    nblk = n_out * (n_in // qk)
     flat = torch.empty(nblk * bb + pad, dtype=torch.uint8, device=device)
     flat[nblk * bb:] = 0
     blk = flat[: nblk * bb].view(nblk, bb)
-    if wtype == 8:
+    if wtype == TYPE_Q8_0:
         blk[:, 2:] = torch.randint(-127, 128, (nblk, 32), dtype=torch.int8, device=device,
                                    generator=generator).view(torch.uint8)
-        d = torch.empty(nblk, dtype=torch.float32, device=device).uniform_(lo, hi, generator=generator)
+        d = torch.empty(nblk, dtype=torch.float32, device=device).uniform_(1e-4, 2e-3, generator=generator)
         blk[:, 0:2] = d.to(torch.float16).view(torch.uint8).view(nblk, 2)
-    else:
+    elif wtype == TYPE_Q4_K:
         blk[:, 4:] = torch.randint(0, 256, (nblk, bb - 4), dtype=torch.uint8, device=device, generator=generator)
-        dd = torch.empty(nblk, 2, dtype=torch.float32, device=device).uniform_(lo, hi, generator=generator)
+        dd = torch.empty(nblk, 2, dtype=torch.float32, device=device).uniform_(1e-4, 1e-3, generator=generator)
         blk[:, 0:4] = dd.to(torch.float16).view(torch.uint8).view(nblk, 4)
+    else:  # uniform bytes, then the fp16 fields of the numpy recipe above
+        off, count, lo, hi = _FP16_FIELDS[wtype]
+        blk[:] = torch.randint(0, 256, (nblk, bb), dtype=torch.uint8, device=device, generator=generator)
+        dd = torch.empty(nblk, count, dtype=torch.float32, device=device).uniform_(lo, hi, generator=generator)
+        blk[:, off:off + 2 * count] = dd.to(torch.float16).view(torch.uint8).view(nblk, 2 * count)
     return flat
+
+
+# (byte offset, number of consecutive fp16 fields, uniform range) per block of the other types
+_FP16_FIELDS = {TYPE_Q4_0: (0, 1, 1e-4, 2e-3), TYPE_Q5_0: (0, 1, 1e-4, 2e-3), TYPE_Q5_K: (0, 2, 1e-4, 1e-3),
+                TYPE_Q6_K: (208, 1, 1e-4, 1e-3)}

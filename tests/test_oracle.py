@@ -491,3 +491,29 @@ def test_x86_order_linear_bit_exact(port, ref, wtype):
         got = port.linear(x, w, wtype, n_out, b, x86=True)
         want = ref.linear(x, w, wtype, n_out, b)
         np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("wtype", ALL)
+def test_device_recipe_matches_numpy_recipe(wtype):
+    """The benchmarks' weights (synth.torch_weight, generated where they are used) follow the
+    parity tests' numpy recipe: same block size, and fp16 scale fields finite and inside the
+    recipe's range, so a benchmark never streams NaN or infinite block scales."""
+    import torch
+
+    s = _synth()
+    n_out, n_in = 8, 1024
+    g = torch.Generator()
+    g.manual_seed(wtype)
+    flat = s.torch_weight(wtype, n_out, n_in, g, "cpu", pad=64).numpy()
+    qk, bb = BLOCK[wtype]
+    nblk = n_out * n_in // qk
+    assert flat.size == nblk * bb + 64 and not flat[nblk * bb:].any()
+    blk = flat[: nblk * bb].reshape(nblk, bb)
+    ref = s.weight(np.random.default_rng(wtype), wtype, n_out, n_in).reshape(nblk, bb)
+    off, count = {TYPE_Q6_K: (208, 1), TYPE_Q4_K: (0, 2), TYPE_Q5_K: (0, 2)}.get(wtype, (0, 1))
+    got = blk[:, off:off + 2 * count].copy().view(np.float16).astype(np.float32)
+    want = ref[:, off:off + 2 * count].copy().view(np.float16).astype(np.float32)
+    assert np.isfinite(got).all()
+    lo, hi = float(want.min()), float(want.max())
+    span = hi - lo
+    assert got.min() >= lo - 0.1 * span and got.max() <= hi + 0.1 * span
