@@ -123,6 +123,52 @@ def linear_alg_bytes(t, n_out, n_in, m):
     return n_out * row_bytes(t, n_in) + m * (4 * n_in + act_bytes(t, n_in) + 4 * n_out)
 
 
+# Library routing constants, for counting the kernels a call launches (the gpu_launches claim):
+# rowstream_kernel.cuh (activation tile budget, rows per launch, prologue quantization), launch.h
+# (tensor-core thresholds, tensor-parallel exchange slot), gemm_tc.cu (row tile, K split).
+PROLOGUE_QUANT_MAX_M, ROWSTREAM_MAX_M, ACT_BUDGET = 2, 16, 96 * 1024
+TC_MIN_M, TC_SMALL_MIN_M, TC_BM, TP_SLOT_BYTES = 64, 9, 128, 512 * 1024
+
+
+def rowstream_max_m(t, k):
+    """Activation rows one row-stream launch takes (rowstream_max_m)."""
+    if BLOCKS[t][0] == 32:  # Q8_0 activations: 32 int8 + an fp32 scale per block
+        per = 36 * (k // 32)
+    else:  # Q8_K activations per 128-element unit: bytes, int32 and int16 sums, half a scale
+        u = k // 128
+        per = ((144 * u + (u // 2) * 4 + 15) & ~15) + 16 * u
+    return min(ROWSTREAM_MAX_M, ACT_BUDGET // (per + 64))
+
+
+def tc_split_ranges(m, n_rows, k, sm_count):
+    """K ranges of a Q4_K tensor-core launch (tc_split): more than one adds the reduction kernel."""
+    nb = k // 256
+    bn = 16 if m < TC_MIN_M else 128
+    base = -(-n_rows // TC_BM) * -(-m // bn)
+    n_ks = 1
+    if bn == 16 and base < 2 * sm_count:
+        n_ks = max(1, min(-(-2 * sm_count // base), nb // 2))
+    sb_per = -(-nb // n_ks)
+    return -(-nb // sb_per)
+
+
+def linear_launches(t, m, k, n_outs, relaxed, sm_count, tp_col=False):
+    """Kernels of one linear call over the tensors `n_outs` sharing their activations, routed as the
+    library routes it (run_linear_dev, edgexpu_cuda_linear_quant_multi_dev, the tensor-parallel
+    linear): tensor-core GEMMs for relaxed-order Q4_K batches of 9+ and Q8_0 batches of 64+,
+    otherwise the row-stream GEMV in chunks of rows, behind one quantize launch unless the GEMV
+    quantizes in its own prologue."""
+    if not tp_col and relaxed and t == TYPE_Q4_K and m >= TC_SMALL_MIN_M:
+        return 1 + sum(1 + (tc_split_ranges(m, n, k, sm_count) > 1) for n in n_outs)
+    if not tp_col and relaxed and t == TYPE_Q8_0 and m >= TC_MIN_M:
+        return 2 * len(n_outs)
+    chunk = rowstream_max_m(t, k)
+    if tp_col:
+        chunk = min(chunk, TP_SLOT_BYTES // 8 // n_outs[0], m)
+        return -(-m // chunk) + (0 if chunk <= PROLOGUE_QUANT_MAX_M else 1)
+    return -(-m // chunk) + (0 if m <= PROLOGUE_QUANT_MAX_M else 1)
+
+
 def logits_alg_bytes(t, vocab, n_embd):
     extra = act_bytes(t, n_embd) if t == TYPE_Q8_0 else 0
     return vocab * row_bytes(t, n_embd) + 4 * n_embd + extra + 8
@@ -700,11 +746,13 @@ def run_ours(args, wl):
         except FileNotFoundError as e:
             cpu_baseline = {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
 
-    # one GEMV launch per group + the logits kernel; Q4_K batches of 9..63 in the relaxed order run the
-    # tensor-core GEMM instead: one activation packing per group, then a K-split GEMM and the reduction of
-    # its partial sums per tensor
-    tc_small = t == TYPE_Q4_K and args.float_order == "relaxed" and 9 <= m < 64
-    launches_per_step = wl["layers"] * sum((1 + 2 * len(grp)) if tc_small else 1 for grp in groups) + m
+    # the kernels of every group's call as the library routes it, plus one logits kernel per token
+    relaxed = args.float_order == "relaxed"
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    tc_small = t == TYPE_Q4_K and relaxed and 9 <= m < 64
+    launches_per_step = wl["layers"] * sum(
+        linear_launches(t, m, shapes[grp[0]][2], [shapes[i][1] for i in grp], relaxed, sms,
+                        tp_col=p2p and len(grp) == 1 and shapes[grp[0]][3] == "col") for grp in groups) + m
     line = {
         "metric": f"{'Q4_K' if t == TYPE_Q4_K else 'Q8_0'} GEMV HBM GB/s ({args.workload}, batch {m})",
         "value": round(value_gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -873,7 +921,8 @@ def run_gemv(args):
         "e2e": {"value": round(nbytes * args.steps / e2e_s / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": 4 * m * n_in, "d2h_bytes_per_step": 4 * m * n_out + 4,
                 "path": "edgexpu_cpu_linear_quant_batch (host buffers)"},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": args.steps * linear_launches(t, m, n_in, [n_out], args.float_order == "relaxed",
+                                                     torch.cuda.get_device_properties(dev).multi_processor_count),
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

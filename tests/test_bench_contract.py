@@ -91,3 +91,30 @@ def test_gemv_reference_arm_is_unavailable(wtype):
     assert r.returncode == 0
     line = json.loads(r.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and "unavailable" in line
+
+
+def test_launch_counts_follow_the_library_routing():
+    """linear_launches restates the library's routing (capi.cu run_linear_dev and the grouped call,
+    tp_p2p.cu's linear, gemm_tc.cu tc_split) on 148 SMs; the cases below were traced by hand."""
+    b = _bench()
+    Q4K, Q80, SM = b.TYPE_Q4_K, b.TYPE_Q8_0, 148
+    # batch 1: the GEMV quantizes in its prologue, one launch per call (the headline's 129 per token)
+    assert b.linear_launches(Q4K, 1, 4096, [4096, 1024, 1024], True, SM) == 1
+    assert b.linear_launches(Q4K, 1, 14336, [4096], True, SM, tp_col=True) == 1
+    wl = b.WORKLOADS["llama3_8b_q4k_decode"]
+    assert wl["layers"] * 4 + 1 == 129
+    # batch 16, relaxed: one packing, then per tensor a K-split GEMM and its reduction
+    assert b.linear_launches(Q4K, 16, 4096, [4096, 1024, 1024], True, SM) == 7
+    assert b.linear_launches(Q4K, 16, 4096, [14336, 14336], True, SM) == 5
+    assert b.linear_launches(Q4K, 16, 14336, [4096], True, SM) == 3
+    # prefill: 128-token tiles cover the SMs, no split
+    assert b.linear_launches(Q4K, 2048, 4096, [14336], True, SM) == 2
+    assert b.tc_split_ranges(2048, 14336, 4096, SM) == 1
+    # x86 order: quantize once, then GEMV chunks of rows (16 at K = 4096, 5 at K = 14336)
+    assert b.rowstream_max_m(Q4K, 4096) == 16 and b.rowstream_max_m(Q4K, 14336) == 5
+    assert b.linear_launches(Q4K, 16, 4096, [4096], False, SM) == 2
+    assert b.linear_launches(Q4K, 16, 14336, [4096], False, SM) == 5
+    # Q8_0: configuration 0's GEMV, and the tensor-core GEMM from 64 rows (packing + GEMM)
+    assert b.linear_launches(Q80, 1, 576, [1536], True, SM) == 1
+    assert b.linear_launches(Q80, 4, 576, [1536], True, SM) == 2
+    assert b.linear_launches(Q80, 64, 4096, [4096, 1024], True, SM) == 4
