@@ -1213,7 +1213,9 @@ def run_prefill(args):
         "cpu_baseline": cpu_baseline,
         "e2e": {"value": round(e2e_tops, 2), "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "edgexpu_cpu_linear_quant_batch (host buffers), one call per projection"},
-        "gpu_launches": L * (len(groups) + len(shapes)) * args.steps,
+        "gpu_launches": L * args.steps * sum(
+            linear_launches(WT, m, shapes[grp[0]][2], [shapes[i][1] for i in grp], True,
+                            torch.cuda.get_device_properties(dev).multi_processor_count) for grp in groups),
         "clocks": clocks,
     }
     if rank == 0:

@@ -118,3 +118,16 @@ def test_launch_counts_follow_the_library_routing():
     assert b.linear_launches(Q80, 1, 576, [1536], True, SM) == 1
     assert b.linear_launches(Q80, 4, 576, [1536], True, SM) == 2
     assert b.linear_launches(Q80, 64, 4096, [4096, 1024], True, SM) == 4
+
+
+def test_prefill_layer_launch_counts():
+    """One prefill layer: Q4_K packs once per group (4) and runs one GEMM per tensor (7); Q8_0 packs
+    per tensor (7 x 2)."""
+    b = _bench()
+    shapes, groups = b.PREFILL["proj"], [[0, 1, 2], [3], [4, 5], [6]]
+
+    def per_layer(wt, m):
+        return sum(b.linear_launches(wt, m, shapes[g[0]][2], [shapes[i][1] for i in g], True, 148) for g in groups)
+
+    assert per_layer(b.TYPE_Q4_K, 2048) == 11
+    assert per_layer(b.TYPE_Q8_0, 2048) == 14
